@@ -1,0 +1,124 @@
+/*
+ * lalb_oracle.h -- CPU restatement of LAL's quantized-matmul hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker: the pytest suite,
+ * the smoke check and the CPU-baseline leg of the benchmark call it to produce
+ * the expected answer or the CPU timing.  The product (liblalb.so, the sm_100a
+ * kernels) never links or calls it.
+ *
+ * What it restates (the reference's kernel headers runtime/lal_q4k_kernel.h and
+ * runtime/lal_q8_kernel.h are listed in the reference README.md:130-131 but are
+ * absent from the reference snapshot):
+ *   - the llama.cpp-compatible Q4_K super-block format (README.md:28, 284):
+ *     144 bytes per 256 weights = fp16 d | fp16 dmin | 12 bytes of packed 6-bit
+ *     scales/mins | 128 bytes of 4-bit quants, w = d*sc_j*q - dmin*m_j;
+ *   - unpack_scales_6bit (README.md:212): 12 packed bytes -> 8 scales + 8 mins;
+ *   - the "simple min-max" Q4_K weight quantizer (README.md:48, 154);
+ *   - the per-32-block fp32 -> int8 activation quantizer (fp32 scale);
+ *   - lal_matmul_q4_k (README.md:130, 210): Q4_K x Q8 dot, int32 per 32-wide
+ *     sub-block, fp32 combine;
+ *   - lal_lm_head_int8_range (README.md:131, 211, 285): int8 x int8 LM head
+ *     over a row range (the "sign trick" |w|*sign(w)x is an identity for
+ *     w != -128, which the quantizer never produces), plus first-max argmax
+ *     (models/ste_train.c:1503-1509, sample_argmax);
+ *   - the seed STE model's per-element CORE/BINARY/PRUNE int8 forward.
+ *
+ * Parity status: the Q4_K byte layout and dequantization are pinned against
+ * gguf 0.19.0 (llama.cpp's Python package, gguf/quants.py Q4_K); the int8
+ * activation quantizer is pinned against gguf's Q8_0 quantize_blocks.  The
+ * Q4_K min-max weight quantizer itself has no third-party twin (the
+ * reference's converter scripts/convert_qwen7b_q4k.py is absent).
+ *
+ * All arithmetic is IEEE single precision with no contraction
+ * (-ffp-contract=off); integer sums are exact.
+ */
+#ifndef LALB_ORACLE_H
+#define LALB_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LALB_O_QK 256          /* weights per Q4_K super-block */
+#define LALB_O_QB 32           /* weights per sub-block / activation block */
+#define LALB_O_Q4K_BYTES 144   /* bytes per Q4_K super-block */
+
+/* --- seeded synthetic data ------------------------------------------------ */
+/* Counter-based normal generator: element i of stream `seed` is
+ *   u = mix64(seed * 0xD1B54A32D192ED03 + i), u1 = ((u>>40)+1)/2^24,
+ *   u2 = ((u>>16)&0xFFFFFF)/2^24, z = sqrt(-2 ln u1) cos(2 pi u2)  (double),
+ * out[k] = (float)(sigma * z) for i = offset + k.  mix64 is the SplitMix64
+ * finalizer (Steele, Lea, Flood 2014). */
+uint64_t lalb_o_mix64(uint64_t z);
+void lalb_o_fill_normal(float *out, size_t n, uint64_t seed, uint64_t offset,
+                        float sigma);
+
+/* --- fp16 ---------------------------------------------------------------- */
+uint16_t lalb_o_f32_to_f16(float f);   /* round to nearest even */
+float    lalb_o_f16_to_f32(uint16_t h);
+
+/* --- Q4_K format --------------------------------------------------------- */
+void lalb_o_unpack_scales_6bit(const uint8_t scales12[12], uint8_t out16[16]);
+void lalb_o_q4k_quantize(const float *w, int rows, int K, uint8_t *blocks);
+void lalb_o_q4k_dequantize(const uint8_t *blocks, int rows, int K, float *w);
+
+/* --- activation quantizer: per 32-block amax/127, roundf, clamp +-127 ----- */
+void lalb_o_quantize_act(const float *x, int M, int K, int8_t *xq, float *sx,
+                         int32_t *sumq);
+
+/* --- Q4_K x Q8 matvec / matmul -------------------------------------------
+ * y[m*rows + r] = sum over sub-blocks s of
+ *     sx[m][s] * ( d*(float)(sc_s*isum_s) - dmin*(float)(m_s*sumq[m][s]) )
+ * summed in double and rounded once.  isum (nullable) receives the exact
+ * int32 sub-block dot products, laid out [m][r][K/32]. */
+void lalb_o_q4k_matmul(const uint8_t *W, int rows, int K, const int8_t *xq,
+                       const float *sx, const int32_t *sumq, int M, float *y,
+                       int32_t *isum);
+
+/* --- Q8 (int8 per-row-scaled) LM head ----------------------------------- */
+void lalb_o_q8_quantize_rows(const float *w, int rows, int K, int8_t *q,
+                             float *s);
+/* logits[r - r0] = sw[r] * (float)( sum_b sx[b]*(float)isum_b )  for r in
+ * [r0, r1); isum (nullable) gets [r1-r0][K/32] int32 block dots.  Returns the
+ * first index (absolute row number) of the maximum logit. */
+int lalb_o_q8_lmhead_range(const int8_t *W, const float *sw, int K, int r0,
+                           int r1, const int8_t *xq, const float *sx,
+                           float *logits, int32_t *isum);
+int lalb_o_argmax(const float *v, int n);
+
+/* --- decode chain used by the Qwen-shape matmul set ----------------------- */
+/* act[i] = (float)(g / (1 + exp(-g)) * up[i]) evaluated in double. */
+void lalb_o_swiglu(const float *gate, const float *up, int n, float *act);
+
+/* --- seed STE model, per-element CORE/BINARY/PRUNE int8 encoding --------- */
+/* state[i] (0 CORE, 1 BINARY, 2 PRUNE) and w[i] (fp32) per weight, W [rows][K].
+ * Per row j:  amax = max |w| over CORE entries, alpha = mean |w| over BINARY
+ * entries, s_j = max(amax, alpha) / 127 (0 if both are 0);
+ *   CORE   code = clamp(roundf(w / s_j), -127, 127)
+ *   BINARY code = (w > 0 ? 1 : -1) * clamp(roundf(alpha / s_j), 1, 127)
+ *   PRUNE  code = 0.
+ * Forward (fp32 X [M][K]):  Y[m][j] = s_j * (float)(sum_i code*X) + bias[j],
+ * the sum taken in double. */
+void lalb_o_logic_state(uint64_t seed, size_t n, float p_core, float p_binary,
+                        uint8_t *state);
+void lalb_o_logic_pack(const float *w, const uint8_t *state, int rows, int K,
+                       int8_t *codes, float *srow);
+void lalb_o_logic_forward(const int8_t *codes, const float *srow,
+                          const float *bias, int rows, int K, const float *X,
+                          int M, float *Y);
+
+/* --- AVX2 + OpenMP CPU baseline (same integer results as the scalar code) - */
+int  lalb_cpu_threads(void);
+void lalb_cpu_quantize_act(const float *x, int M, int K, int8_t *xq, float *sx,
+                           int32_t *sumq);
+void lalb_cpu_q4k_gemv(const uint8_t *W, int rows, int K, const int8_t *xq,
+                       const float *sx, const int32_t *sumq, float *y);
+int  lalb_cpu_q8_lmhead(const int8_t *W, const float *sw, int rows, int K,
+                        const int8_t *xq, const float *sx, float *logits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

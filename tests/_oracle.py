@@ -1,0 +1,170 @@
+"""numpy-facing wrapper of the CPU oracle (oracle/liblalb_oracle.so).
+
+Test infrastructure: the checker that the GPU results are compared with.
+Builds the oracle with `make -C oracle` when the library is missing.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ORACLE_DIR = os.path.join(ROOT, "oracle")
+SO = os.path.join(ORACLE_DIR, "liblalb_oracle.so")
+P = ctypes.c_void_p
+c_int, c_float, c_size_t, c_u64 = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_uint64
+
+_SIG = {
+    "lalb_o_mix64": (c_u64, [c_u64]),
+    "lalb_o_fill_normal": (None, [P, c_size_t, c_u64, c_u64, c_float]),
+    "lalb_o_f32_to_f16": (ctypes.c_uint16, [c_float]),
+    "lalb_o_f16_to_f32": (c_float, [ctypes.c_uint16]),
+    "lalb_o_unpack_scales_6bit": (None, [P, P]),
+    "lalb_o_q4k_quantize": (None, [P, c_int, c_int, P]),
+    "lalb_o_q4k_dequantize": (None, [P, c_int, c_int, P]),
+    "lalb_o_quantize_act": (None, [P, c_int, c_int, P, P, P]),
+    "lalb_o_q4k_matmul": (None, [P, c_int, c_int, P, P, P, c_int, P, P]),
+    "lalb_o_q8_quantize_rows": (None, [P, c_int, c_int, P, P]),
+    "lalb_o_q8_lmhead_range": (c_int, [P, P, c_int, c_int, c_int, P, P, P, P]),
+    "lalb_o_argmax": (c_int, [P, c_int]),
+    "lalb_o_swiglu": (None, [P, P, c_int, P]),
+    "lalb_o_logic_state": (None, [c_u64, c_size_t, c_float, c_float, P]),
+    "lalb_o_logic_pack": (None, [P, P, c_int, c_int, P, P]),
+    "lalb_o_logic_forward": (None, [P, P, P, c_int, c_int, P, c_int, P]),
+    "lalb_cpu_threads": (c_int, []),
+    "lalb_cpu_quantize_act": (None, [P, c_int, c_int, P, P, P]),
+    "lalb_cpu_q4k_gemv": (None, [P, c_int, c_int, P, P, P, P]),
+    "lalb_cpu_q8_lmhead": (c_int, [P, P, c_int, c_int, P, P, P]),
+}
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(SO):
+            subprocess.run(["make", "-C", ORACLE_DIR], check=True, capture_output=True)
+        L = ctypes.CDLL(SO)
+        for k, (r, a) in _SIG.items():
+            f = getattr(L, k)
+            f.restype, f.argtypes = r, a
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(P)
+
+
+def normal(n, seed, sigma=1.0, offset=0):
+    out = np.empty(n, np.float32)
+    lib().lalb_o_fill_normal(_p(out), n, seed, offset, sigma)
+    return out
+
+
+def q4k_quantize(w):
+    rows, K = w.shape
+    out = np.empty((rows, K // 256 * 144), np.uint8)
+    lib().lalb_o_q4k_quantize(_p(np.ascontiguousarray(w, np.float32)), rows, K, _p(out))
+    return out
+
+
+def q4k_dequantize(blocks, rows, K):
+    out = np.empty((rows, K), np.float32)
+    lib().lalb_o_q4k_dequantize(_p(np.ascontiguousarray(blocks)), rows, K, _p(out))
+    return out
+
+
+def unpack_scales(s12):
+    out = np.empty(16, np.uint8)
+    lib().lalb_o_unpack_scales_6bit(_p(np.ascontiguousarray(s12, np.uint8)), _p(out))
+    return out
+
+
+def quantize_act(x):
+    x = np.ascontiguousarray(x, np.float32)
+    M, K = (1, x.size) if x.ndim == 1 else x.shape
+    xq = np.empty((M, K), np.int8)
+    sx = np.empty((M, K // 32), np.float32)
+    sq = np.empty((M, K // 32), np.int32)
+    lib().lalb_o_quantize_act(_p(x), M, K, _p(xq), _p(sx), _p(sq))
+    return xq, sx, sq
+
+
+def q4k_matmul(W, rows, K, xq, sx, sq, want_isum=False):
+    M = xq.shape[0] if xq.ndim == 2 else 1
+    y = np.empty((M, rows), np.float32)
+    isum = np.empty((M, rows, K // 32), np.int32) if want_isum else None
+    lib().lalb_o_q4k_matmul(_p(np.ascontiguousarray(W)), rows, K, _p(np.ascontiguousarray(xq)),
+                            _p(np.ascontiguousarray(sx)), _p(np.ascontiguousarray(sq)), M,
+                            _p(y), _p(isum))
+    return y, isum
+
+
+def q8_quantize_rows(w):
+    rows, K = w.shape
+    q = np.empty((rows, K), np.int8)
+    s = np.empty(rows, np.float32)
+    lib().lalb_o_q8_quantize_rows(_p(np.ascontiguousarray(w, np.float32)), rows, K, _p(q), _p(s))
+    return q, s
+
+
+def q8_lmhead(Wq, sw, xq, sx, r0, r1, want_isum=False):
+    K = Wq.shape[1]
+    logits = np.empty(r1 - r0, np.float32)
+    isum = np.empty((r1 - r0, K // 32), np.int32) if want_isum else None
+    am = lib().lalb_o_q8_lmhead_range(_p(Wq), _p(sw), K, r0, r1,
+                                      _p(np.ascontiguousarray(xq).reshape(-1)),
+                                      _p(np.ascontiguousarray(sx).reshape(-1)), _p(logits),
+                                      _p(isum))
+    return logits, isum, am
+
+
+def swiglu(gate, up):
+    act = np.empty_like(gate, dtype=np.float32)
+    lib().lalb_o_swiglu(_p(np.ascontiguousarray(gate, np.float32)),
+                        _p(np.ascontiguousarray(up, np.float32)), gate.size, _p(act))
+    return act
+
+
+def rms_normalise(x):
+    """x * (float)(1/sqrt(mean(x^2) + 1e-6)), the scale computed in double."""
+    x = np.asarray(x, np.float32)
+    ss = np.sum(x.astype(np.float64) ** 2)
+    scale = np.float32(1.0 / np.sqrt(ss / x.size + 1e-6))
+    return (x * scale).astype(np.float32)
+
+
+def decode_chain(layers, lm_q, lm_s, h_in, cfg):
+    """The decoder's per-token math on the CPU (see include/lalb.h).
+
+    layers: list of dicts with Q4_K byte arrays wqkv, wo, wgu, wdown.
+    Returns (h_final, logits, argmax)."""
+    hid, q_rows, kv, ffn = cfg["hidden"], cfg["q_rows"], cfg["kv_rows"], cfg["ffn"]
+    h = np.array(h_in, np.float32)
+    for lw in layers:
+        xq, sx, sq = quantize_act(rms_normalise(h))
+        qkv, _ = q4k_matmul(lw["wqkv"], q_rows + 2 * kv, hid, xq, sx, sq)
+        q = qkv[0, :q_rows]
+        xq, sx, sq = quantize_act(q)
+        o, _ = q4k_matmul(lw["wo"], hid, q_rows, xq, sx, sq)
+        h = (h + o[0]).astype(np.float32)
+        xq, sx, sq = quantize_act(rms_normalise(h))
+        gu, _ = q4k_matmul(lw["wgu"], 2 * ffn, hid, xq, sx, sq)
+        gu = gu[0].reshape(-1, 2, 32)          # 32-row gate/up tiles
+        act = swiglu(gu[:, 0, :].reshape(-1), gu[:, 1, :].reshape(-1))
+        xq, sx, sq = quantize_act(act)
+        d, _ = q4k_matmul(lw["wdown"], hid, ffn, xq, sx, sq)
+        h = (h + d[0]).astype(np.float32)
+    xq, sx, _ = quantize_act(rms_normalise(h))
+    logits, _, am = q8_lmhead(lm_q, lm_s, xq, sx, 0, lm_q.shape[0])
+    return h, logits, am
+
+
+def normwise_rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = np.max(np.abs(b))
+    return float(np.max(np.abs(a - b)) / (den if den > 0 else 1.0))
