@@ -1,0 +1,434 @@
+#!/usr/bin/env python
+"""bench.py -- Qwen2.5-7B-shape Q4_K decode on B200 through liblalb.so.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl lalb|reference]
+
+A step is one decode token of the matmul set: 28 layers x (qkv 4608x3584,
+o 3584x3584, gate/up 37888x3584 with fused SwiGLU, down 3584x18944), all
+Q4_K, plus the 152064x3584 int8 LM head with argmax -- 4.22 GB of weights
+streamed from HBM per token (inputs larger than L2, so no flush is needed).
+Weights are seeded N(0, 0.02) drawn and quantized on the GPU by the library;
+the hidden state is seeded N(0, 1).  Attention is outside the measured path
+(the q projection stands in for the attention output).
+
+One JSON line on rank 0.  Under torchrun (N > 1) every rank runs an
+independent replica of the decode on its own GPU (weak scaling).
+`--impl reference` times the CPU kernels (AVX2 + OpenMP port of the
+reference's absent lal_q4k_kernel.h / lal_q8_kernel.h) on the host cores.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(n_layer=28, hidden=3584, q_rows=3584, kv_rows=512, ffn=18944, vocab=152064)
+METRIC = "Q4_K GEMV HBM GB/s (% of peak); 7B-shape decode tok/s at 1/2/4/8 B200"
+WORKLOAD = ("qwen2.5-7b-shape decode matmul set: 28 layers x (qkv 4608x3584, o 3584x3584, "
+            "gate/up 37888x3584 + fused SwiGLU, down 3584x18944) Q4_K + 152064x3584 int8 "
+            "LM head + argmax, batch 1")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def q4k_bytes(rows, K):
+    return rows * (K // 256) * 144
+
+
+def layer_mats(c):
+    """(rows, K) of the four Q4_K matrices of one layer."""
+    return [(c["q_rows"] + 2 * c["kv_rows"], c["hidden"]), (c["hidden"], c["q_rows"]),
+            (2 * c["ffn"], c["hidden"]), (c["hidden"], c["ffn"])]
+
+
+def algorithmic_bytes(c):
+    """Bytes that must cross HBM per token: weights + activations in/out."""
+    per_layer = [q4k_bytes(rows, K) + 4 * K + 4 * rows for rows, K in layer_mats(c)]
+    head = c["vocab"] * c["hidden"] + 4 * c["vocab"] + 4 * c["hidden"] + 4
+    return per_layer, head
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """dram bytes per launch of the Q4_K matvec from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "q4k_gemv_decode7b_ncu.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+# --------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus_id = bus_id.lower()
+        self.proc = None
+
+    def start(self):
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + self.QUERY, "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.tmp.seek(0)
+        rows = [r.split(", ") for r in self.tmp.read().strip().splitlines()]
+        os.unlink(self.tmp.name)
+        mine = [r for r in rows if len(r) >= 10 and r[1].lower().endswith(self.bus_id[-12:])]
+        if not mine:
+            return None
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        sm = [v for v in (num(r[2]) for r in mine) if v is not None]
+        power = [v for v in (num(r[4]) for r in mine) if v is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in mine for n, v in zip(names, r[6:10]) if v.strip() == "Active"})
+        busy = sorted(sm)[len(sm) // 4:] if sm else []
+        return {"sm_mhz": statistics.median(busy) if busy else None,
+                "sm_max_mhz": num(mine[0][3]), "power_w_max": max(power) if power else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# the GPU arm
+# --------------------------------------------------------------------------
+def build_decoder(ctx, lb, torch, c, seed):
+    """Seeded N(0,0.02) weights drawn and quantized on the GPU."""
+    big = max(max(r * k for r, k in layer_mats(c)), c["vocab"] * c["hidden"])
+    tmp = torch.empty(big, dtype=torch.float32, device="cuda")
+    layers = []
+    for l in range(c["n_layer"]):
+        mats = []
+        for j, (rows, K) in enumerate(layer_mats(c)):
+            w = tmp[: rows * K].view(rows, K)
+            ctx.fill_normal(w, seed=seed + 16 * l + j, sigma=0.02)
+            mats.append(ctx.q4k_quantize(w))
+        layers.append(mats)
+    w = tmp[: c["vocab"] * c["hidden"]].view(c["vocab"], c["hidden"])
+    ctx.fill_normal(w, seed=seed + 9999, sigma=0.02)
+    lm_q, lm_s = ctx.q8_quantize_rows(w)
+    torch.cuda.synchronize()
+    del tmp
+    dec = lb.Decoder(ctx, **c)
+    for l, m in enumerate(layers):
+        dec.set_layer(l, *m)
+    dec.set_lm_head(lm_q, lm_s)
+    return dec, layers, (lm_q, lm_s)
+
+
+def gemv_standalone(ctx, torch, stream, reps=200):
+    """The single 18944x3584 Q4_K GEMV with the fused quantizer; 8 weight
+    copies (305 MB, > 2x L2) rotated so every launch streams from HBM."""
+    rows, K = 18944, 3584
+    copies = []
+    w = torch.empty(rows * K, dtype=torch.float32, device="cuda")
+    for i in range(8):
+        ctx.fill_normal(w, seed=500 + i, sigma=0.02)
+        copies.append(ctx.q4k_quantize(w.view(rows, K)))
+    del w
+    x = torch.empty(K, dtype=torch.float32, device="cuda")
+    ctx.fill_normal(x, seed=600, sigma=1.0)
+    y = torch.empty(rows, dtype=torch.float32, device="cuda")
+    with torch.cuda.stream(stream):
+        for i in range(16):
+            ctx.matmul_q4_k(copies[i % 8], x, rows, K, out=y)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            ctx.matmul_q4_k(copies[i % 8], x, rows, K, out=y)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    nbytes = q4k_bytes(rows, K) + 4 * K + 4 * rows
+    return {"shape": [rows, K], "us_per_launch": round(us, 3), "bytes": nbytes,
+            "gbs": round(nbytes / us / 1e3, 1)}
+
+
+def run_gpu(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import lalmodel_b200 as lb
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=300))
+    c = CFG
+    ctx = lb.Context(local_rank)
+    dec, layers, lm = build_decoder(ctx, lb, torch, c, seed=1234)
+    h_in = torch.empty(c["hidden"], dtype=torch.float32, device="cuda")
+    ctx.fill_normal(h_in, seed=77 + rank, sigma=1.0)
+    am = torch.empty(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+    launches = dec.launches_per_step()
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            dec.step(h_in, None, None, am)
+    torch.cuda.synchronize()
+
+    props = torch.cuda.get_device_properties(local_rank)
+    bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+    sampler = ClockSampler(bus)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            dec.step(h_in, None, None, am)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # per-kernel durations of one token (events between kernels, no overlap)
+    per_layer_b, head_b = algorithmic_bytes(c)
+    with torch.cuda.stream(stream):
+        prof = np.median(np.array([dec.profile_step(h_in) for _ in range(5)]), axis=0)
+    q4k_launches = 4 * c["n_layer"]
+    q4k_us = float(sum(prof[:q4k_launches]))
+    q4k_bytes_tok = c["n_layer"] * sum(per_layer_b)
+    peak, peak_kind = measured_peak()
+    achieved = q4k_bytes_tok / (q4k_us * 1e-6) / 1e9
+    head_us = float(prof[-1])
+    kinds = ["qkv", "o", "gate_up", "down"]
+    per_kind = {k: round(float(np.mean(prof[i:q4k_launches:4])), 2) for i, k in enumerate(kinds)}
+    per_kind_gbs = {k: round(per_layer_b[i] / (per_kind[k] * 1e-6) / 1e9, 1)
+                    for i, k in enumerate(kinds)}
+
+    # end to end through the host-buffer entry point (H2D input, D2H argmax)
+    pinned = h_in.cpu().pin_memory()
+    n_e2e = max(20, min(args.steps, 400))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            dec.step_host(pinned)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(n_e2e):
+            dec.step_host(pinned)
+        f1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([f0.elapsed_time(f1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * n_e2e / (float(t.item()) / 1000.0)
+
+    gemv = gemv_standalone(ctx, torch, stream) if rank == 0 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_sample(layers, lm, c, budget_s=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (q4 x i8 dp4a -> int32 per 32-block, fp32 terms, f64 row sum)",
+            "data": "synthetic: seeded N(0,0.02) weights quantized on the GPU (Q4_K min-max, "
+                    "int8 per-row LM head); seeded N(0,1) hidden state",
+            "config": {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": world,
+                       "seq_len": 1,
+                       "parallelism": "replicas%d" % world if world > 1 else "single",
+                       "l2": "inputs larger than L2: %.2f GB of weights streamed per step"
+                             % ((q4k_bytes_tok + head_b) / 1e9),
+                       "bytes_per_step": q4k_bytes_tok + head_b},
+            "roofline": {"kernel": "q4k_gemv (the %d Q4_K matvec launches of a token)" % q4k_launches,
+                         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
+                         "bytes_per_launch_avg": q4k_bytes_tok / q4k_launches,
+                         "us_per_launch_avg": round(q4k_us / q4k_launches, 3),
+                         "us_by_kind": per_kind, "gbs_by_kind": per_kind_gbs,
+                         "lm_head_us": round(head_us, 2),
+                         "lm_head_gbs": round(head_b / (head_us * 1e-6) / 1e9, 1),
+                         "step_gbs": round((q4k_bytes_tok + head_b) / (ms_per_step * 1e-3) / 1e9, 1)},
+            "gemv": gemv and {**gemv, "frac": round(gemv["gbs"] / peak, 4)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * c["hidden"], "d2h_bytes_per_step": 4},
+            "gpu_launches": args.steps * launches,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------
+# CPU: the oracle's AVX2 + OpenMP kernels (port of the reference's absent
+# CPU kernels) timed on the host cores
+# --------------------------------------------------------------------------
+def _cpu_lib():
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import _oracle as O  # builds oracle/liblalb_oracle.so if needed
+
+    return O
+
+
+def cpu_layer_and_head(O, L, mats, lmq, lms, c, h):
+    """One decoder layer of the matmul chain + the LM head on the CPU.
+    Returns (seconds for the layer, seconds for the head)."""
+    p = O._p
+    hid, qr, kv, ffn = c["hidden"], c["q_rows"], c["kv_rows"], c["ffn"]
+    xq = np.empty(max(hid, ffn), np.int8)
+    sx = np.empty(max(hid, ffn) // 32, np.float32)
+    sq = np.empty(max(hid, ffn) // 32, np.int32)
+    t0 = time.perf_counter()
+    qkv = np.empty(qr + 2 * kv, np.float32)
+    L.lalb_cpu_quantize_act(p(O.rms_normalise(h)), 1, hid, p(xq), p(sx), p(sq))
+    L.lalb_cpu_q4k_gemv(p(mats[0]), qr + 2 * kv, hid, p(xq), p(sx), p(sq), p(qkv))
+    L.lalb_cpu_quantize_act(p(np.ascontiguousarray(qkv[:qr])), 1, qr, p(xq), p(sx), p(sq))
+    o = np.empty(hid, np.float32)
+    L.lalb_cpu_q4k_gemv(p(mats[1]), hid, qr, p(xq), p(sx), p(sq), p(o))
+    h = (h + o).astype(np.float32)
+    L.lalb_cpu_quantize_act(p(O.rms_normalise(h)), 1, hid, p(xq), p(sx), p(sq))
+    gu = np.empty(2 * ffn, np.float32)
+    L.lalb_cpu_q4k_gemv(p(mats[2]), 2 * ffn, hid, p(xq), p(sx), p(sq), p(gu))
+    gu = gu.reshape(-1, 2, 32)
+    act = O.swiglu(gu[:, 0].reshape(-1), gu[:, 1].reshape(-1))
+    L.lalb_cpu_quantize_act(p(act), 1, ffn, p(xq), p(sx), p(sq))
+    d = np.empty(hid, np.float32)
+    L.lalb_cpu_q4k_gemv(p(mats[3]), hid, ffn, p(xq), p(sx), p(sq), p(d))
+    h = (h + d).astype(np.float32)
+    t1 = time.perf_counter()
+    L.lalb_cpu_quantize_act(p(O.rms_normalise(h)), 1, hid, p(xq), p(sx), p(sq))
+    logits = np.empty(lmq.shape[0], np.float32)
+    L.lalb_cpu_q8_lmhead(p(lmq), p(lms), lmq.shape[0], hid, p(xq), p(sx), p(logits))
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1
+
+
+def cpu_timed(O, mats, lmq, lms, c, warmup, max_steps, budget_s):
+    L = O.lib()
+    h = O.normal(c["hidden"], seed=77)
+    for _ in range(max(1, warmup)):
+        cpu_layer_and_head(O, L, mats, lmq, lms, c, h)
+    tl, th = [], []
+    t_start = time.perf_counter()
+    while len(tl) < max_steps and (not tl or time.perf_counter() - t_start < budget_s):
+        a, b = cpu_layer_and_head(O, L, mats, lmq, lms, c, h)
+        tl.append(a)
+        th.append(b)
+    t_layer, t_head = statistics.median(tl), statistics.median(th)
+    tok_s = 1.0 / (c["n_layer"] * t_layer + t_head)
+    sample = ("%d x (1 decoder layer %.2f ms + LM head %.2f ms) on the same weights; "
+              "token time = %d layers + head" % (len(tl), 1e3 * t_layer, 1e3 * t_head, c["n_layer"]))
+    return tok_s, len(tl), L.lalb_cpu_threads(), sample
+
+
+def cpu_baseline_sample(layers, lm, c, budget_s):
+    """Layer 0's weights and the LM head copied from the GPU; the host cores
+    run one layer + the head repeatedly for ~budget_s seconds."""
+    O = _cpu_lib()
+    mats = [m.cpu().numpy().reshape(-1) for m in layers[0]]
+    lmq, lms = lm[0].cpu().numpy(), lm[1].cpu().numpy()
+    tok_s, n, cores, sample = cpu_timed(O, mats, lmq, lms, c, 2, 10 ** 6, budget_s)
+    return {"value": round(tok_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": sample}
+
+
+def run_reference(args, rank, world):
+    """The CPU arm: the same metric and workload on the host cores."""
+    if rank != 0:
+        return
+    O = _cpu_lib()
+    c = CFG
+    mats = []
+    for j, (rows, K) in enumerate(layer_mats(c)):
+        w = O.normal(rows * K, seed=1234 + j, sigma=0.02).reshape(rows, K)
+        mats.append(O.q4k_quantize(w).reshape(-1))
+        del w
+    w = O.normal(c["vocab"] * c["hidden"], seed=1234 + 9999, sigma=0.02).reshape(c["vocab"], c["hidden"])
+    lmq, lms = O.q8_quantize_rows(w)
+    del w
+    tok_s, n, cores, sample = cpu_timed(O, mats, lmq, lms, c, args.warmup, args.steps,
+                                        args.cpu_seconds * 4)
+    line = {"impl": "reference", "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s",
+            "n_gpus": world, "steps": n, "warmup": args.warmup,
+            "ms_per_step": round(1e3 / tok_s, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 (AVX2 maddubs -> int32, fp32 combine)",
+            "data": "synthetic: seeded N(0,0.02) weights quantized on the CPU, N(0,1) hidden state",
+            "config": {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": 1,
+                       "seq_len": 1, "parallelism": "host cores (OpenMP)"},
+            "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": cores,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="lalb", choices=["lalb", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--n-layer", type=int, default=CFG["n_layer"],
+                    help="fewer layers: only for profiling captures, not a bench line")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    CFG["n_layer"] = args.n_layer
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_gpu(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

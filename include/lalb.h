@@ -1,0 +1,206 @@
+/*
+ * lalb.h -- C ABI of the B200 (sm_100a) quantized-matmul hot path of LAL.
+ *
+ * Plain C99, includable from the reference engine's C sources.  Every entry
+ * point returns an int status (0 = LALB_OK, negative = lalb_status); none
+ * exits, prints or falls back to the CPU.  All tensor arguments are DEVICE
+ * pointers owned by the caller unless a name ends in _host; the library owns
+ * only the context (a status word, a small scratch area and, for decoders,
+ * activation buffers).  Work is enqueued on the caller's stream
+ * (lalb_stream = cudaStream_t; NULL = the legacy default stream).
+ *
+ * Formats
+ *   Q4_K  144-byte super-block per 256 weights, llama.cpp layout:
+ *         fp16 d | fp16 dmin | 12 bytes packed 6-bit scales/mins | 128 bytes
+ *         of 4-bit quants (32-byte group g holds sub-block 2g in the low
+ *         nibbles and 2g+1 in the high nibbles); w = d*sc_j*q - dmin*m_j.
+ *         A matrix is row-major: row r is K/256 consecutive blocks.
+ *   Q8 activations  per 32-block: int8 q = clamp(roundf(x/s), +-127) with
+ *         fp32 s = amax/127, plus sumq = sum of the 32 q (int32).
+ *   Q8 LM head  int8 [rows][K] with one fp32 scale per row.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   lal_matmul_q4_k         runtime/lal_q4k_kernel.h (README.md:130,210)
+ *   lal_lm_head_int8_range  runtime/lal_q8_kernel.h  (README.md:131,211)
+ *   unpack_scales_6bit      (README.md:212)
+ *   the lal_cuda.h pattern  runtime/lal_cuda.h:12-97 (extern "C", resident
+ *                           device weights, runtime/lal_cuda.h:56-68)
+ * The reference's kernel headers are absent from its snapshot; the
+ * signatures below keep their names and argument meaning (weights, row
+ * range, activation, output) with explicit sizes, a context and a stream.
+ */
+#ifndef LALB_H
+#define LALB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define LALB_API __attribute__((visibility("default")))
+#else
+#define LALB_API
+#endif
+
+#define LALB_ABI_VERSION 1
+#define LALB_QK_K 256
+#define LALB_QB 32
+#define LALB_Q4K_BLOCK_BYTES 144
+
+typedef enum {
+    LALB_OK = 0,
+    LALB_ERR_INVALID = -1,     /* bad pointer, size, alignment or state */
+    LALB_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+    LALB_ERR_NOMEM = -3,       /* device or host allocation failed */
+    LALB_ERR_UNSUPPORTED = -4, /* shape outside what the kernels handle */
+    LALB_ERR_TIMEOUT = -5,     /* a bounded device wait gave up */
+    LALB_ERR_COMM = -6,        /* multi-GPU communicator failure */
+    LALB_ERR_DEVICE = -7       /* not an sm_100 device */
+} lalb_status;
+
+typedef struct lalb_ctx lalb_ctx;
+typedef void *lalb_stream;
+
+/* ---- context --------------------------------------------------------- */
+LALB_API int         lalb_abi_version(void);
+LALB_API const char *lalb_status_string(int status);
+/* Binds the calling thread to `device` and allocates the context's status
+ * word and scratch (a few hundred bytes).  Fails with LALB_ERR_DEVICE on a
+ * device other than compute capability 10.0. */
+LALB_API int         lalb_init(int device, lalb_ctx **out);
+LALB_API int         lalb_destroy(lalb_ctx *ctx);
+/* Text of the last error recorded on this context ("" if none). */
+LALB_API const char *lalb_last_error(const lalb_ctx *ctx);
+/* Synchronises the device and returns the device-side status word
+ * (0 = no bounded wait has expired); reset != 0 clears it. */
+LALB_API int         lalb_device_status(lalb_ctx *ctx, int reset);
+
+/* ---- formats ---------------------------------------------------------- */
+/* Host helper (no GPU): 12 packed bytes -> out16[0..7] scales,
+ * out16[8..15] mins.  Replaces unpack_scales_6bit (README.md:212). */
+LALB_API int lalb_unpack_scales_6bit(const uint8_t *scales12, uint8_t *out16);
+
+/* Seeded N(0, sigma) fill of n floats (element i of stream `seed` is a
+ * function of seed and offset+i only). */
+LALB_API int lalb_fill_normal(lalb_ctx *ctx, float *out, size_t n, uint64_t seed,
+                              uint64_t offset, float sigma, lalb_stream stream);
+
+/* Min-max Q4_K quantization of w [rows][K] (K % 256 == 0) into
+ * blocks [rows][K/256][144] (the converter's quantizer; README.md:48,154). */
+LALB_API int lalb_q4k_quantize(lalb_ctx *ctx, const float *w, int rows, int K,
+                               void *blocks, lalb_stream stream);
+
+/* Per-row int8 quantization of an LM head w [rows][K]: s = amax/127,
+ * q = clamp(roundf(w/s), +-127). */
+LALB_API int lalb_q8_quantize_rows(lalb_ctx *ctx, const float *w, int rows, int K,
+                                   int8_t *q, float *s, lalb_stream stream);
+
+/* Per-32-block int8 activation quantizer for M vectors of K (K % 32 == 0):
+ * xq [M][K], sx [M][K/32], sumq [M][K/32] (sumq may be NULL). */
+LALB_API int lalb_quantize_act(lalb_ctx *ctx, const float *x, int M, int K,
+                               int8_t *xq, float *sx, int32_t *sumq,
+                               lalb_stream stream);
+
+/* ---- Q4_K x Q8 matvec (decode, batch 1) --------------------------------
+ * y[r] = sum_j sx_j * (d*sc_j*isum_j - dmin*m_j*sumq_j) over the 32-wide
+ * sub-blocks j of row r, isum_j = the exact int32 dot of the 32 4-bit quants
+ * with the 32 int8 activations.  The activation quantizer is fused: x is
+ * fp32 [K].  W must be 16-byte aligned; K % 256 == 0, K <= 65536.
+ * Replaces lal_matmul_q4_k (runtime/lal_q4k_kernel.h, README.md:130,210). */
+LALB_API int lalb_matmul_q4_k(lalb_ctx *ctx, const void *W, int rows, int K,
+                              const float *x, float *y, lalb_stream stream);
+
+/* Same product on an activation already quantized by lalb_quantize_act.
+ * isum (nullable) receives the int32 sub-block dots [rows][K/32]. */
+LALB_API int lalb_matmul_q4_k_q8(lalb_ctx *ctx, const void *W, int rows, int K,
+                                 const int8_t *xq, const float *sx,
+                                 const int32_t *sumq, float *y, int32_t *isum,
+                                 lalb_stream stream);
+
+/* ---- Q8 LM head --------------------------------------------------------
+ * For r in [row_begin, row_end): logits[r - row_begin] =
+ *   sw[r] * sum_b sx_b * isum_b(r)   (isum_b = int32 dot of 32-block b)
+ * with x (fp32 [K], K % 32 == 0, K <= 4096) quantized in the prologue.
+ * argmax (nullable, device int32) receives the absolute row index of the
+ * first maximum logit in the range.  W rows are K bytes; W + r*K must be
+ * 16-byte aligned.  Calls on one context must not overlap on the GPU (the
+ * argmax reduction uses the context's scratch).
+ * Replaces lal_lm_head_int8_range (runtime/lal_q8_kernel.h,
+ * README.md:131,211). */
+LALB_API int lalb_lm_head_int8_range(lalb_ctx *ctx, const int8_t *W, const float *sw,
+                                     int K, int row_begin, int row_end,
+                                     const float *x, float *logits, int32_t *argmax,
+                                     lalb_stream stream);
+
+/* Same on a pre-quantized activation; isum (nullable) gets
+ * [row_end-row_begin][K/32] int32 block dots. */
+LALB_API int lalb_lm_head_int8_q8(lalb_ctx *ctx, const int8_t *W, const float *sw,
+                                  int K, int row_begin, int row_end,
+                                  const int8_t *xq, const float *sx, float *logits,
+                                  int32_t *isum, int32_t *argmax, lalb_stream stream);
+
+/* ---- Qwen2.5-shape decode matmul set (one token) -----------------------
+ * Per layer, with h the fp32 residual stream [hidden]:
+ *   qkv  = Wqkv . Q8(rmsnorm(h))              rows q_rows + 2*kv_rows
+ *   h    = h + Wo . Q8(qkv[0:q_rows])          (the attention output is
+ *                                              out of scope; q stands in)
+ *   a    = silu(gate) * up, gate/up = Wgu . Q8(rmsnorm(h))
+ *   h    = h + Wdown . Q8(a)
+ * then logits = LMhead . Q8(rmsnorm(h)) and argmax.  rmsnorm uses unit
+ * weights, eps 1e-6, its scale computed in double; silu(g)*u is evaluated
+ * in double and rounded once.  Wgu interleaves gate and up in 32-row
+ * tiles: rows [64t, 64t+32) are gate rows [32t, 32t+32), rows
+ * [64t+32, 64t+64) the up rows of the same range.  Weights are
+ * caller-owned device buffers. */
+typedef struct {
+    int n_layer;
+    int hidden;     /* K of qkv / gate-up, rows of o / down */
+    int q_rows;     /* n_head * head_dim */
+    int kv_rows;    /* n_kv_head * head_dim */
+    int ffn;        /* intermediate size */
+    int vocab;      /* LM-head rows */
+} lalb_decoder_cfg;
+
+typedef struct {
+    const void *wqkv;   /* Q4_K [q_rows + 2*kv_rows][hidden] */
+    const void *wo;     /* Q4_K [hidden][q_rows] */
+    const void *wgu;    /* Q4_K [2*ffn][hidden], 32-row gate/up tiles */
+    const void *wdown;  /* Q4_K [hidden][ffn] */
+} lalb_layer_weights;
+
+typedef struct lalb_decoder lalb_decoder;
+
+LALB_API int lalb_decoder_create(lalb_ctx *ctx, const lalb_decoder_cfg *cfg,
+                                 lalb_decoder **out);
+LALB_API int lalb_decoder_set_layer(lalb_decoder *dec, int layer,
+                                    const lalb_layer_weights *w);
+LALB_API int lalb_decoder_set_lm_head(lalb_decoder *dec, const int8_t *w,
+                                      const float *sw);
+/* One token on device buffers: h_in [hidden] (read only), h_out [hidden]
+ * (nullable: final residual stream), logits [vocab] (nullable), argmax
+ * (device int32, nullable).  On a non-default stream the token is captured
+ * into a CUDA graph on first use of a pointer set and replayed after. */
+LALB_API int lalb_decoder_step(lalb_decoder *dec, const float *h_in, float *h_out,
+                               float *logits, int32_t *argmax, lalb_stream stream);
+/* One token from host memory: copies h_in_host (pinned recommended) to the
+ * device, runs the step, copies the argmax back to *argmax_host and waits
+ * for the stream. */
+LALB_API int lalb_decoder_step_host(lalb_decoder *dec, const float *h_in_host,
+                                    int32_t *argmax_host, lalb_stream stream);
+/* One token with a CUDA event between consecutive kernels (no graph, no
+ * programmatic overlap): kernel_us (host, lalb_decoder_launches_per_step
+ * floats) receives each kernel's duration in launch order -- per layer
+ * qkv, o, gate/up, down; then the LM head.  Synchronises the stream. */
+LALB_API int lalb_decoder_profile_step(lalb_decoder *dec, const float *h_in,
+                                       float *kernel_us, lalb_stream stream);
+/* Number of kernels one step launches. */
+LALB_API int lalb_decoder_launches_per_step(const lalb_decoder *dec);
+LALB_API int lalb_decoder_destroy(lalb_decoder *dec);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LALB_H */

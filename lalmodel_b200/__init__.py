@@ -1,0 +1,215 @@
+"""lalmodel_b200 -- LAL's quantized-matmul hot path, B200-native (sm_100a).
+
+Host-side mirror of the reference engine's kernel interface, over the C ABI
+declared in include/lalb.h and implemented by liblalb.so:
+
+  lal_matmul_q4_k          Q4_K x Q8 matvec   (runtime/lal_q4k_kernel.h,
+                                               README.md:130,210)
+  lal_lm_head_int8_range   int8 LM head + argmax over a row range
+                                              (runtime/lal_q8_kernel.h,
+                                               README.md:131,211)
+  unpack_scales_6bit       12 packed bytes -> 8 scales + 8 mins
+                                              (README.md:212)
+
+Device memory and streams come from PyTorch (plumbing only); every compute
+call goes through liblalb.so on the caller's current CUDA stream.  Nothing
+here computes on the CPU: a missing library or a non-sm_100 device raises.
+"""
+import ctypes
+
+import torch
+
+from . import _abi
+from ._abi import DecoderCfg, LalbError, LayerWeights
+
+QK_K = 256
+QB = 32
+Q4K_BLOCK_BYTES = 144
+
+__all__ = ["Context", "Decoder", "LalbError", "lal_matmul_q4_k", "lal_lm_head_int8_range",
+           "unpack_scales_6bit", "q4k_row_bytes", "QK_K", "QB", "Q4K_BLOCK_BYTES"]
+
+
+def q4k_row_bytes(K):
+    return (K // QK_K) * Q4K_BLOCK_BYTES
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def unpack_scales_6bit(scales12):
+    """12 packed bytes -> 16 bytes (8 scales, then 8 mins); host-only helper."""
+    src = (ctypes.c_uint8 * 12).from_buffer_copy(bytes(scales12))
+    dst = (ctypes.c_uint8 * 16)()
+    _abi.call(None, "lalb_unpack_scales_6bit", src, dst)
+    return bytes(dst)
+
+
+class Context:
+    """One lalb_ctx bound to one CUDA device."""
+
+    def __init__(self, device=0):
+        self.device = torch.device("cuda", device)
+        h = ctypes.c_void_p()
+        st = _abi.lib().lalb_init(device, ctypes.byref(h))
+        if st != 0:
+            raise LalbError("lalb_init", st, "device %d" % device)
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            _abi.lib().lalb_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _call(self, name, *args):
+        return _abi.call(self.h, name, *args)
+
+    def device_status(self, reset=False):
+        st = _abi.lib().lalb_device_status(self.h, 1 if reset else 0)
+        if st < 0:
+            raise LalbError("lalb_device_status", st, _abi.lib().lalb_last_error(self.h).decode())
+        return st
+
+    # ---- data and formats ------------------------------------------------
+    def fill_normal(self, out, seed, sigma, offset=0):
+        self._call("lalb_fill_normal", self.h, _p(out), out.numel(), seed, offset,
+                   ctypes.c_float(sigma), _stream())
+        return out
+
+    def q4k_quantize(self, w, out=None):
+        rows, K = w.shape
+        if out is None:
+            out = torch.empty((rows, q4k_row_bytes(K)), dtype=torch.uint8, device=w.device)
+        self._call("lalb_q4k_quantize", self.h, _p(w), rows, K, _p(out), _stream())
+        return out
+
+    def q8_quantize_rows(self, w):
+        rows, K = w.shape
+        q = torch.empty((rows, K), dtype=torch.int8, device=w.device)
+        s = torch.empty(rows, dtype=torch.float32, device=w.device)
+        self._call("lalb_q8_quantize_rows", self.h, _p(w), rows, K, _p(q), _p(s), _stream())
+        return q, s
+
+    def quantize_act(self, x):
+        M, K = x.shape if x.dim() == 2 else (1, x.shape[0])
+        xq = torch.empty((M, K), dtype=torch.int8, device=x.device)
+        sx = torch.empty((M, K // QB), dtype=torch.float32, device=x.device)
+        sq = torch.empty((M, K // QB), dtype=torch.int32, device=x.device)
+        self._call("lalb_quantize_act", self.h, _p(x), M, K, _p(xq), _p(sx), _p(sq), _stream())
+        return xq, sx, sq
+
+    # ---- hot path ----------------------------------------------------------
+    def matmul_q4_k(self, W, x, rows, K, out=None):
+        y = out if out is not None else torch.empty(rows, dtype=torch.float32, device=x.device)
+        self._call("lalb_matmul_q4_k", self.h, _p(W), rows, K, _p(x), _p(y), _stream())
+        return y
+
+    def matmul_q4_k_q8(self, W, xq, sx, sumq, rows, K, want_isum=False):
+        y = torch.empty(rows, dtype=torch.float32, device=xq.device)
+        isum = (torch.empty((rows, K // QB), dtype=torch.int32, device=xq.device)
+                if want_isum else None)
+        self._call("lalb_matmul_q4_k_q8", self.h, _p(W), rows, K, _p(xq), _p(sx), _p(sumq),
+                   _p(y), _p(isum), _stream())
+        return y, isum
+
+    def lm_head_int8_range(self, W, sw, x, row_begin, row_end, want_logits=True):
+        K = W.shape[1]
+        n = row_end - row_begin
+        logits = torch.empty(n, dtype=torch.float32, device=x.device) if want_logits else None
+        am = torch.empty(1, dtype=torch.int32, device=x.device)
+        self._call("lalb_lm_head_int8_range", self.h, _p(W), _p(sw), K, row_begin, row_end,
+                   _p(x), _p(logits), _p(am), _stream())
+        return logits, am
+
+    def lm_head_int8_q8(self, W, sw, xq, sx, row_begin, row_end, want_isum=False):
+        K = W.shape[1]
+        n = row_end - row_begin
+        logits = torch.empty(n, dtype=torch.float32, device=xq.device)
+        isum = torch.empty((n, K // QB), dtype=torch.int32, device=xq.device) if want_isum else None
+        am = torch.empty(1, dtype=torch.int32, device=xq.device)
+        self._call("lalb_lm_head_int8_q8", self.h, _p(W), _p(sw), K, row_begin, row_end, _p(xq),
+                   _p(sx), _p(logits), _p(isum), _p(am), _stream())
+        return logits, isum, am
+
+
+class Decoder:
+    """The Qwen2.5-shape decode matmul set (include/lalb.h, lalb_decoder_*)."""
+
+    def __init__(self, ctx, n_layer, hidden, q_rows, kv_rows, ffn, vocab):
+        self.ctx = ctx
+        self.cfg = DecoderCfg(n_layer, hidden, q_rows, kv_rows, ffn, vocab)
+        h = ctypes.c_void_p()
+        ctx._call("lalb_decoder_create", ctx.h, ctypes.byref(self.cfg), ctypes.byref(h))
+        self.h = h
+
+    def set_layer(self, layer, wqkv, wo, wgu, wdown):
+        lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())
+        self.ctx._call("lalb_decoder_set_layer", self.h, layer, ctypes.byref(lw))
+
+    def set_lm_head(self, w, sw):
+        self.ctx._call("lalb_decoder_set_lm_head", self.h, _p(w), _p(sw))
+
+    def step(self, h_in, h_out=None, logits=None, argmax=None):
+        self.ctx._call("lalb_decoder_step", self.h, _p(h_in), _p(h_out), _p(logits),
+                       _p(argmax), _stream())
+
+    def step_host(self, h_in_host):
+        """h_in_host: pinned CPU float32 tensor; returns the argmax (int)."""
+        out = ctypes.c_int32(0)
+        self.ctx._call("lalb_decoder_step_host", self.h, _p(h_in_host), ctypes.byref(out),
+                       _stream())
+        return out.value
+
+    def profile_step(self, h_in):
+        """Per-kernel durations (microseconds) of one token, in launch order."""
+        n = self.launches_per_step()
+        buf = (ctypes.c_float * n)()
+        self.ctx._call("lalb_decoder_profile_step", self.h, _p(h_in), buf, _stream())
+        return list(buf)
+
+    def launches_per_step(self):
+        return _abi.lib().lalb_decoder_launches_per_step(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            _abi.lib().lalb_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default_ctx = {}
+
+
+def _ctx_for(t):
+    dev = t.device.index if t.device.index is not None else torch.cuda.current_device()
+    if dev not in _default_ctx:
+        _default_ctx[dev] = Context(dev)
+    return _default_ctx[dev]
+
+
+def lal_matmul_q4_k(W, x, rows, K, ctx=None):
+    """y = W . x for a Q4_K matrix W [rows][K/256 blocks] and fp32 x [K]."""
+    ctx = ctx or _ctx_for(x)
+    return ctx.matmul_q4_k(W, x, rows, K)
+
+
+def lal_lm_head_int8_range(W, sw, x, row_begin, row_end, ctx=None):
+    """logits for rows [row_begin, row_end) of the int8 head, and the argmax row."""
+    ctx = ctx or _ctx_for(x)
+    return ctx.lm_head_int8_range(W, sw, x, row_begin, row_end)

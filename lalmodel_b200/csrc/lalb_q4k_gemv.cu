@@ -1,0 +1,445 @@
+// lalb_q4k_gemv.cu -- Q4_K x Q8 matvec for batch-1 decode on sm_100a.
+//
+// Memory-bound by design: the only bytes that must cross HBM are the Q4_K
+// super-blocks (4.5 bits per weight).  Structure of one CTA (256 threads):
+//
+//   * it owns a contiguous range of weight rows, i.e. one contiguous byte
+//     range of the row-major Q4_K matrix;
+//   * thread 0 streams that range into a ring of shared-memory stages with
+//     1-D bulk copies (cp.async.bulk, the TMA engine), completion tracked by
+//     one mbarrier per stage, L2 policy evict-first;
+//   * meanwhile all threads quantize the activation (fp32 -> int8 per
+//     32-block, optional RMS normalisation) into shared memory -- the
+//     quantizer is fused, no separate launch;
+//   * a "team" of WR warps owns one row of a stage; team lane t owns the
+//     64-weight groups c = t, t + 32*WR, ... (a group = one 32-byte run of
+//     quants = sub-blocks 2g and 2g+1 of a super-block).  The lane keeps the
+//     int8 activations of its groups in registers for the whole kernel, so
+//     shared memory traffic is the weights only;
+//   * per group: 3 x 16-byte shared loads (header, two quant halves), 16 dp4a
+//     producing the two exact int32 sub-block sums, and two fp32 sub-block
+//     terms sx*(d*(sc*isum) - dmin*(m*sumq)), each rounded op by op;
+//   * the terms are accumulated in double (warp shuffles, then across the
+//     team) and the row result is rounded to fp32 once, so the output does
+//     not depend on the thread mapping or summation order;
+//   * fused epilogues: store, residual add, SwiGLU + re-quantization of the
+//     product for the next matvec.
+//
+// References (paths inside the reference project): lal_matmul_q4_k
+// (runtime/lal_q4k_kernel.h, README.md:130,210), unpack_scales_6bit
+// (README.md:212), Q4_K layout (README.md:28,284).
+#include <algorithm>
+
+#include "lalb_internal.cuh"
+#include "lalb_kernels.cuh"
+
+using namespace lalb;
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+struct Layout {
+    uint32_t off_xq, off_sx, off_sq, off_red, off_tile, off_stage;
+    uint32_t stage_bytes, total;
+};
+
+__host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) {
+    return (v + a - 1) / a * a;
+}
+
+// Shared-memory layout shared by host (size) and device (pointers).
+__host__ __device__ inline Layout make_layout(int K, int wr, int nstages) {
+    Layout L;
+    const uint32_t ns = K / 32;
+    L.off_xq = 128;                                  // mbarriers live below
+    L.off_sx = align_up(L.off_xq + K, 16);
+    L.off_sq = L.off_sx + 4 * ns;
+    L.off_red = align_up(L.off_sq + 4 * ns, 16);
+    L.off_tile = L.off_red + 2 * kWarps * 8;         // double partials
+    L.off_stage = align_up(L.off_tile + 2 * 64 * 4, 128);
+    const uint32_t rps = kWarps / wr;
+    L.stage_bytes = rps * (uint32_t)(K / 256) * 144u;
+    L.total = L.off_stage + nstages * L.stage_bytes;
+    return L;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One 64-weight group (sub-blocks 2g, 2g+1 of super-block c/4): adds its two
+// fp32 sub-block terms to acc; writes the two exact int32 sub-block dot
+// products to isum2 when non-null.  sx = activation scale, sq = sumq (as an
+// exactly representable float).
+__device__ __forceinline__ void q4k_group(const uint8_t *__restrict__ rowp, int c,
+                                          const int (&xv)[16], float sx0, float sq0,
+                                          float sx1, float sq1, int32_t *isum2, double &acc) {
+    const int b = c >> 2, g = c & 3;
+    const uint8_t *bp = rowp + b * 144;
+    const uint4 h = *reinterpret_cast<const uint4 *>(bp);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(bp + 16 + 32 * g);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(bp + 32 + 32 * g);
+    const float d = f16_bits_to_f32(h.x & 0xFFFFu);
+    const float dmin = f16_bits_to_f32(h.x >> 16);
+    const ScaleWords sw = unpack_scale_words(h.y, h.z, h.w);
+    const uint32_t scw = g < 2 ? sw.sc_lo : sw.sc_hi;
+    const uint32_t mnw = g < 2 ? sw.mn_lo : sw.mn_hi;
+    const uint32_t sh = (g & 1) * 16;
+    const int sc0 = (scw >> sh) & 0xFF, sc1 = (scw >> (sh + 8)) & 0xFF;
+    const int m0 = (mnw >> sh) & 0xFF, m1 = (mnw >> (sh + 8)) & 0xFF;
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    int s0 = 0, s1 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        s0 = dp4a((int)(q[i] & 0x0F0F0F0Fu), xv[i], s0);
+        s1 = dp4a((int)((q[i] >> 4) & 0x0F0F0F0Fu), xv[8 + i], s1);
+    }
+    if (isum2) {
+        isum2[0] = s0;
+        isum2[1] = s1;
+    }
+    // t = sx * (d*(sc*isum) - dmin*(m*sumq)); sc*isum and m*sumq are exact
+    const float t0 = __fmul_rn(sx0, __fsub_rn(__fmul_rn(d, (float)(sc0 * s0)),
+                                              __fmul_rn(dmin, __fmul_rn((float)m0, sq0))));
+    const float t1 = __fmul_rn(sx1, __fsub_rn(__fmul_rn(d, (float)(sc1 * s1)),
+                                              __fmul_rn(dmin, __fmul_rn((float)m1, sq1))));
+    acc += (double)t0;
+    acc += (double)t1;
+}
+
+template <int WR, int GPL, int IN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    q4k_gemv_kernel(const Q4kGemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int RPS = kWarps / WR;  // rows per stage (one per team)
+    const int K = a.K;
+    const int G = K >> 6, NS = K >> 5;
+    const uint32_t row_bytes = (uint32_t)(K >> 8) * 144u;
+    const Layout L = make_layout(K, WR, a.nstages);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
+    int8_t *xq_s = reinterpret_cast<int8_t *>(smem + L.off_xq);
+    float *sx_s = reinterpret_cast<float *>(smem + L.off_sx);
+    float *sq_s = reinterpret_cast<float *>(smem + L.off_sq);  // sumq as float
+    double *red_s = reinterpret_cast<double *>(smem + L.off_red);
+    float *tile_s = reinterpret_cast<float *>(smem + L.off_tile);
+    uint8_t *stage_s = smem + L.off_stage;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int team = warp / WR, wit = warp % WR;
+    const int tl = wit * 32 + lane;
+
+    // contiguous row range of this CTA, in units of a.unit rows
+    const int nunits = a.rows / a.unit;
+    const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x);
+    const int u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
+    const int r0 = u0 * a.unit, r1 = u1 * a.unit;
+    const int nst = (r1 - r0 + RPS - 1) / RPS;
+    const int nstages = a.nstages;
+
+    uint64_t policy = 0;
+    auto issue = [&](int i) {
+        const int rs = r0 + i * RPS;
+        const int nr = min(RPS, r1 - rs);
+        const uint32_t bytes = (uint32_t)nr * row_bytes;
+        const int buf = i % nstages;
+        mbar_arrive_expect_tx(&bar[buf], bytes);
+        bulk_g2s(stage_s + (size_t)buf * L.stage_bytes, a.W + (size_t)rs * row_bytes, bytes,
+                 &bar[buf], policy);
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < nstages; ++s) mbar_init(&bar[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        policy = l2_evict_first_policy();
+        const int pre = min(nstages, nst);
+        for (int i = 0; i < pre; ++i) issue(i);
+    }
+
+    // The weights are never written by the preceding kernel, so their
+    // stream starts before the dependency wait; activations come after it.
+    pdl_wait();
+
+    // ---- activation prologue -------------------------------------------------
+    if (IN == kInQ8) {
+        const int4 *src = reinterpret_cast<const int4 *>(a.xq);
+        int4 *dst = reinterpret_cast<int4 *>(xq_s);
+        for (int i = tid; i < K / 16; i += kThreads) dst[i] = src[i];
+        for (int i = tid; i < NS; i += kThreads) {
+            sx_s[i] = a.sx[i];
+            sq_s[i] = (float)a.sumq[i];
+        }
+    } else {
+        float scale = 1.0f;
+        if (IN == kInF32Rms) scale = block_rms_scale(a.x, K);
+        for (int blk = warp; blk < NS; blk += kWarps) {
+            float v = a.x[blk * 32 + lane];
+            if (IN == kInF32Rms) {
+                v = __fmul_rn(v, scale);
+                if (a.gamma) v = __fmul_rn(v, a.gamma[blk * 32 + lane]);
+            }
+            const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
+            const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
+            const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
+            const float t = roundf(__fmul_rn(v, id));
+            const int q = t > 127.0f ? 127 : (t < -127.0f ? -127 : (int)t);
+            xq_s[blk * 32 + lane] = (int8_t)q;
+            const int s = __reduce_add_sync(0xffffffffu, q);
+            if (lane == 0) {
+                sx_s[blk] = dsc;
+                sq_s[blk] = (float)s;
+            }
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    // ---- per-lane activation registers ------------------------------------
+    int xv[GPL][16];
+    float sa0[GPL], sb0[GPL], sa1[GPL], sb1[GPL];
+#pragma unroll
+    for (int k = 0; k < GPL; ++k) {
+        const int c = tl + k * 32 * WR;
+        if (c < G) {
+            const int4 *p = reinterpret_cast<const int4 *>(xq_s + 64 * c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int4 v = p[j];
+                xv[k][4 * j + 0] = v.x;
+                xv[k][4 * j + 1] = v.y;
+                xv[k][4 * j + 2] = v.z;
+                xv[k][4 * j + 3] = v.w;
+            }
+            sa0[k] = sx_s[2 * c];
+            sb0[k] = sq_s[2 * c];
+            sa1[k] = sx_s[2 * c + 1];
+            sb1[k] = sq_s[2 * c + 1];
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xv[k][j] = 0;
+            sa0[k] = sb0[k] = sa1[k] = sb1[k] = 0.0f;
+        }
+    }
+
+    // ---- main loop over stages ---------------------------------------------
+    int issued = min(nstages, nst);
+    for (int i = 0; i < nst; ++i) {
+        const int buf = i % nstages;
+        const uint32_t parity = (uint32_t)(i / nstages) & 1u;
+        const bool ok = mbar_wait_bounded(&bar[buf], parity, a.status);
+        const int row = r0 + i * RPS + team;
+        double acc = 0.0;
+        if (ok && row < r1) {
+            const uint8_t *rowp = stage_s + (size_t)buf * L.stage_bytes + team * row_bytes;
+            int32_t *isum_row = a.isum ? a.isum + (size_t)row * NS : nullptr;
+#pragma unroll
+            for (int k = 0; k < GPL; ++k) {
+                const int c = tl + k * 32 * WR;
+                if (c < G)
+                    q4k_group(rowp, c, xv[k], sa0[k], sb0[k], sa1[k], sb1[k],
+                              isum_row ? isum_row + 2 * c : nullptr, acc);
+            }
+        }
+        acc = warp_sum_d(acc);
+        if (WR == 1) {
+            if (lane == 0 && row < r1) {
+                const float v = (float)acc;
+                if (EPI == kEpiSwiglu) {
+                    tile_s[(((row - r0) >> 6) & 1) * 64 + ((row - r0) & 63)] = v;
+                } else {
+                    a.y[row] = EPI == kEpiResid ? __fadd_rn(a.resid[row], v) : v;
+                }
+            }
+        } else if (lane == 0) {
+            red_s[(i & 1) * kWarps + team * WR + wit] = acc;
+        }
+        const bool stop = __syncthreads_or(!ok);
+        if (stop) break;
+        if (tid == 0 && issued < nst) {
+            issue(issued);
+            ++issued;
+        }
+        if (WR > 1 && tid < RPS) {
+            const int rw = r0 + i * RPS + tid;
+            if (rw < r1) {
+                double s = 0.0;
+#pragma unroll
+                for (int w = 0; w < WR; ++w) s += red_s[(i & 1) * kWarps + tid * WR + w];
+                const float v = (float)s;
+                if (EPI == kEpiSwiglu) {
+                    tile_s[(((rw - r0) >> 6) & 1) * 64 + ((rw - r0) & 63)] = v;
+                } else {
+                    a.y[rw] = EPI == kEpiResid ? __fadd_rn(a.resid[rw], v) : v;
+                }
+            }
+        }
+        if (EPI == kEpiSwiglu) {
+            // a 64-row tile (32 gate + 32 up rows) completes every 64/RPS stages
+            const int done_rows = (i + 1) * RPS;
+            if ((done_rows & 63) == 0) {
+                if (WR > 1) __syncthreads();   // the tile entries written above
+                const int tloc = (done_rows - 1) >> 6;
+                if (warp == kWarps - 1) {
+                    const float *tb = tile_s + (tloc & 1) * 64;
+                    const float av = silu_mul(tb[lane], tb[32 + lane]);
+                    const uint32_t amax =
+                        __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av)));
+                    const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
+                    const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
+                    const float t = roundf(__fmul_rn(av, id));
+                    const int q = t > 127.0f ? 127 : (t < -127.0f ? -127 : (int)t);
+                    const int gt = (r0 >> 6) + tloc;  // 32-element block of the product
+                    a.aq[gt * 32 + lane] = (int8_t)q;
+                    if (a.act_out) a.act_out[gt * 32 + lane] = av;
+                    const int s = __reduce_add_sync(0xffffffffu, q);
+                    if (lane == 0) {
+                        a.asx[gt] = dsc;
+                        a.asumq[gt] = s;
+                    }
+                }
+            }
+        }
+    }
+    // drain: every issued copy must land before the CTA's shared memory is
+    // released (returns at once after a normal run; bounded otherwise)
+    if (tid == 0) {
+        for (int i = max(0, issued - nstages); i < issued; ++i) {
+            const int buf = i % nstages;
+            mbar_wait_bounded(&bar[buf], (uint32_t)(i / nstages) & 1u, a.status);
+        }
+    }
+}
+
+struct Variant {
+    int wr, gpl;
+};
+
+Variant pick_variant(int G) {
+    if (G <= 64) return {1, 2};
+    if (G <= 384) return {4, 3};
+    if (G <= 1024) return {8, 4};
+    return {0, 0};
+}
+
+template <int IN, int EPI>
+void *kernel_ptr(int wr, int gpl) {
+    if (wr == 1 && gpl == 2) return (void *)q4k_gemv_kernel<1, 2, IN, EPI>;
+    if (wr == 4 && gpl == 3) return (void *)q4k_gemv_kernel<4, 3, IN, EPI>;
+    if (wr == 8 && gpl == 4) return (void *)q4k_gemv_kernel<8, 4, IN, EPI>;
+    return nullptr;
+}
+
+void *select_kernel(int in, int epi, int wr, int gpl) {
+#define LALB_SEL(I, E) \
+    if (in == I && epi == E) return kernel_ptr<I, E>(wr, gpl);
+    LALB_SEL(kInF32, kEpiStore)
+    LALB_SEL(kInF32Rms, kEpiStore)
+    LALB_SEL(kInQ8, kEpiStore)
+    LALB_SEL(kInF32, kEpiResid)
+    LALB_SEL(kInQ8, kEpiResid)
+    LALB_SEL(kInF32Rms, kEpiSwiglu)
+#undef LALB_SEL
+    return nullptr;
+}
+
+}  // namespace
+
+// Launches one Q4_K matvec.  `unit` = row granularity of the CTA split (64
+// for the SwiGLU epilogue).  ctas_per_sm: 1 or 2 (clamped to what fits).
+int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int epi,
+                         cudaStream_t stream, bool pdl, int ctas_per_sm) {
+    Q4kGemvArgs a = args_in;
+    if (!a.W || a.rows <= 0 || a.K <= 0 || a.K % 256)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: bad shape rows=%d K=%d", a.rows, a.K);
+    if (reinterpret_cast<uintptr_t>(a.W) & 15)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: W must be 16-byte aligned");
+    if (a.unit <= 0 || a.rows % a.unit)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: rows %% unit != 0");
+    const int G = a.K / 64;
+    const Variant v = pick_variant(G);
+    if (!v.wr) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d > 65536", a.K);
+    if (in == kInQ8 && (reinterpret_cast<uintptr_t>(a.xq) & 15))
+        return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: xq must be 16-byte aligned");
+    void *fn = select_kernel(in, epi, v.wr, v.gpl);
+    if (!fn) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: no variant in=%d epi=%d", in, epi);
+
+    // pipeline depth: fill the per-CTA shared-memory budget
+    const size_t budget = ctas_per_sm >= 2 ? 110 * 1024 : ctx->smem_optin - 1024;
+    const Layout base = make_layout(a.K, v.wr, 0);
+    int nst = (int)((budget - base.off_stage) / base.stage_bytes);
+    if (nst > 8) nst = 8;
+    if (nst < 2) {
+        nst = (int)((ctx->smem_optin - 1024 - base.off_stage) / base.stage_bytes);
+        ctas_per_sm = 1;
+        if (nst < 2) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d too large for smem", a.K);
+        if (nst > 8) nst = 8;
+    }
+    a.nstages = nst;
+    a.status = &ctx->scratch->status;
+    const Layout L = make_layout(a.K, v.wr, nst);
+    {
+        const int st = lalb_set_smem_attr(ctx, fn, (int)L.total);
+        if (st) return st;
+    }
+    int resident = 0;
+    LALB_CUDA_TRY(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, (const void *)fn,
+                                                                     kThreads, L.total));
+    if (resident < 1) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: CTA does not fit");
+    if (ctas_per_sm > resident) ctas_per_sm = resident;
+    const int nunits = a.rows / a.unit;
+    int grid = ctx->sm_count * ctas_per_sm;
+    if (grid > nunits) grid = nunits;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *params[] = {&a};
+    LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, fn, params));
+    return LALB_OK;
+}
+
+extern "C" int lalb_matmul_q4_k(lalb_ctx *ctx, const void *W, int rows, int K, const float *x,
+                                float *y, lalb_stream stream) {
+    if (!ctx) return LALB_ERR_INVALID;
+    if (!x || !y) return lalb_fail(ctx, LALB_ERR_INVALID, "matmul_q4_k: null x/y");
+    Q4kGemvArgs a = {};
+    a.W = static_cast<const uint8_t *>(W);
+    a.rows = rows;
+    a.K = K;
+    a.x = x;
+    a.y = y;
+    a.unit = 1;
+    return lalb_launch_q4k_gemv(ctx, a, kInF32, kEpiStore, (cudaStream_t)stream, false, 1);
+}
+
+extern "C" int lalb_matmul_q4_k_q8(lalb_ctx *ctx, const void *W, int rows, int K,
+                                   const int8_t *xq, const float *sx, const int32_t *sumq,
+                                   float *y, int32_t *isum, lalb_stream stream) {
+    if (!ctx) return LALB_ERR_INVALID;
+    if (!xq || !sx || !sumq || !y)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "matmul_q4_k_q8: null argument");
+    Q4kGemvArgs a = {};
+    a.W = static_cast<const uint8_t *>(W);
+    a.rows = rows;
+    a.K = K;
+    a.xq = xq;
+    a.sx = sx;
+    a.sumq = sumq;
+    a.y = y;
+    a.isum = isum;
+    a.unit = 1;
+    return lalb_launch_q4k_gemv(ctx, a, kInQ8, kEpiStore, (cudaStream_t)stream, false, 1);
+}

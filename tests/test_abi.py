@@ -1,0 +1,67 @@
+"""CPU tests of the C ABI: the library loads, exports every declared entry
+point, and its host-only / argument-checking paths behave (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+import _oracle as O
+import lalmodel_b200 as lb
+from lalmodel_b200 import _abi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    text = open(os.path.join(ROOT, "include", "lalb.h")).read()
+    return sorted(set(re.findall(r"LALB_API[^;(]*?\b(lalb_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert len(names) >= 20
+    for must in ["lalb_matmul_q4_k", "lalb_lm_head_int8_range", "lalb_unpack_scales_6bit",
+                 "lalb_decoder_step"]:
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(_abi.LIB_PATH)
+    missing = [n for n in declared_symbols() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_binding_table_matches_header():
+    assert sorted(_abi.SIGNATURES) == declared_symbols()
+
+
+def test_abi_version_and_status_strings():
+    L = _abi.lib()
+    assert L.lalb_abi_version() == 1
+    for st in range(0, -8, -1):
+        assert L.lalb_status_string(st)
+
+
+def test_unpack_scales_host_helper_matches_oracle():
+    rng = np.random.default_rng(0)
+    for _ in range(200):
+        s = rng.integers(0, 256, 12, dtype=np.uint8)
+        assert lb.unpack_scales_6bit(s.tobytes()) == O.unpack_scales(s).tobytes()
+
+
+def test_init_without_sm100_device_fails_cleanly():
+    import torch
+
+    if torch.cuda.is_available():
+        return  # covered by the GPU tests
+    h = ctypes.c_void_p()
+    assert _abi.lib().lalb_init(0, ctypes.byref(h)) == -7  # LALB_ERR_DEVICE
+    assert not h.value
+
+
+def test_null_arguments_rejected_without_device():
+    L = _abi.lib()
+    assert L.lalb_unpack_scales_6bit(None, None) == -1
+    assert L.lalb_matmul_q4_k(None, None, 1, 256, None, None, None) == -1
+    assert L.lalb_decoder_step(None, None, None, None, None, None) == -1
