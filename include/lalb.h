@@ -142,6 +142,30 @@ LALB_API int lalb_lm_head_int8_q8(lalb_ctx *ctx, const int8_t *W, const float *s
                                   const int8_t *xq, const float *sx, float *logits,
                                   int32_t *isum, int32_t *argmax, lalb_stream stream);
 
+/* Allocation-free LM head.  This entry point has no counterpart in the
+ * reference.  It is for callers that cannot call cudaMalloc: an engine whose
+ * own memory pool owns the device and forbids libraries from allocating (a
+ * cudaMalloc would also stall every stream on the device), or code that
+ * cannot create a lalb_ctx because creating one allocates.  It computes
+ * exactly what lalb_lm_head_int8_range computes, on the current device, with
+ * no context and no allocation: its argmax reduction state (16 bytes) lives
+ * in a 256-byte static device array that every GPU loading the library holds
+ * until the process exits.  That need does not grow with the row count or K,
+ * so the sizes it rejects are the kernel's own: K > 4096 returns
+ * LALB_ERR_UNSUPPORTED; K not a multiple of 32, an inverted range, a null or
+ * misaligned pointer return LALB_ERR_INVALID.  Errors are reported only
+ * through the returned status (there is no context to hold a message).
+ * The first call on a device sets it up (looks up the array's device
+ * address, reads the SM count, raises the kernel's shared-memory limit);
+ * make that first call before any stream capture.  Every call shares the
+ * array and clears the 16 bytes it uses on the caller's stream before the
+ * kernel runs; calls that overlap on the GPU (another stream, another host
+ * thread on the same device) race on it. */
+LALB_API int lalb_lm_head_int8_range_noalloc(const int8_t *W, const float *sw, int K,
+                                             int row_begin, int row_end, const float *x,
+                                             float *logits, int32_t *argmax,
+                                             lalb_stream stream);
+
 /* ---- Qwen2.5-shape decode matmul set (one token) -----------------------
  * Per layer, with h the fp32 residual stream [hidden]:
  *   qkv  = Wqkv . Q8(rmsnorm(h))              rows q_rows + 2*kv_rows

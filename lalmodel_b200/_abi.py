@@ -44,6 +44,7 @@ SIGNATURES = {
     "lalb_matmul_q4_k_q8": (c_int, [P, P, c_int, c_int, P, P, P, P, P, P]),
     "lalb_lm_head_int8_range": (c_int, [P, P, P, c_int, c_int, c_int, P, P, P, P]),
     "lalb_lm_head_int8_q8": (c_int, [P, P, P, c_int, c_int, c_int, P, P, P, P, P, P]),
+    "lalb_lm_head_int8_range_noalloc": (c_int, [P, P, c_int, c_int, c_int, P, P, P, P]),
     "lalb_decoder_create": (c_int, [P, ctypes.POINTER(DecoderCfg), ctypes.POINTER(P)]),
     "lalb_decoder_set_layer": (c_int, [P, c_int, ctypes.POINTER(LayerWeights)]),
     "lalb_decoder_set_lm_head": (c_int, [P, P, P]),

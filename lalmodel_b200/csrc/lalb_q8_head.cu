@@ -20,6 +20,7 @@
 // arrive (ticket counter) publishes the row index and resets the scratch
 // for the next call.
 #include <algorithm>
+#include <mutex>
 
 #include "lalb_internal.cuh"
 #include "lalb_kernels.cuh"
@@ -327,4 +328,124 @@ extern "C" int lalb_lm_head_int8_q8(lalb_ctx *ctx, const int8_t *W, const float 
     a.isum = isum;
     a.argmax = argmax;
     return lalb_launch_q8_head(ctx, a, kInQ8, (cudaStream_t)stream, false, 1);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free LM head.
+//
+// Some callers cannot call cudaMalloc: an engine whose own caching pool owns
+// every byte of device memory and forbids libraries from allocating behind
+// its back (cudaMalloc also stalls the whole device while it runs), or code
+// that must not create a lalb_ctx because creating one allocates.  For them
+// the argmax reduction state lives in the file-scope array below instead of
+// a context's scratch.  It needs no context: device properties come from
+// cudaDeviceGetAttribute, and errors are reported only through the status.
+// ---------------------------------------------------------------------------
+namespace {
+
+// 256 bytes, held by every GPU that loads the library until the process
+// exits.  A call uses the first 16: the packed best key (8 bytes), the CTA
+// ticket (4) and the bounded-wait status word (4).  That need does not grow
+// with the row count or K.
+constexpr int kNoAllocScratchBytes = 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocDevice {
+    unsigned char *scratch;   // device address of g_noalloc_scratch on this device
+    int sm_count;
+    int smem_budget;          // dynamic shared memory one CTA may use
+    bool ready;
+};
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: the array's device address (the
+// host-side name g_noalloc_scratch is only a stand-in and must never reach a
+// kernel), the SM count, and the kernel's shared-memory limit.
+int noalloc_setup(int dev, NoAllocDevice **out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice &d = g_noalloc_dev[dev];
+    if (!d.ready) {
+        void *ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) {
+            cudaGetLastError();
+            return LALB_ERR_CUDA;
+        }
+        int sm = 0, optin = 0;
+        if (cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+                cudaSuccess) {
+            cudaGetLastError();
+            return LALB_ERR_CUDA;
+        }
+        const int budget = optin - 1024;
+        if (cudaFuncSetAttribute((const void *)q8_head_kernel<kInF32>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, budget) != cudaSuccess) {
+            cudaGetLastError();
+            return LALB_ERR_CUDA;
+        }
+        d.scratch = static_cast<unsigned char *>(ptr);
+        d.sm_count = sm;
+        d.smem_budget = budget;
+        d.ready = true;
+    }
+    *out = &d;
+    return LALB_OK;
+}
+
+}  // namespace
+
+extern "C" int lalb_lm_head_int8_range_noalloc(const int8_t *W, const float *sw, int K,
+                                               int row_begin, int row_end, const float *x,
+                                               float *logits, int32_t *argmax,
+                                               lalb_stream stream) {
+    if (!W || !sw || !x || K <= 0 || K % 32 || row_begin < 0 || row_end < row_begin)
+        return LALB_ERR_INVALID;
+    if (K > 32 * 32 * kMaxGpl) return LALB_ERR_UNSUPPORTED;  // the kernel's K limit (4096)
+    if (reinterpret_cast<uintptr_t>(W) & 15) return LALB_ERR_INVALID;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return LALB_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return LALB_ERR_UNSUPPORTED;
+    NoAllocDevice *nd = nullptr;
+    if (int st = noalloc_setup(dev, &nd)) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int nrows = row_end - row_begin;
+    if (nrows == 0) {
+        if (argmax && cudaMemsetAsync(argmax, 0xFF, sizeof(int32_t), s) != cudaSuccess)
+            return LALB_ERR_CUDA;
+        return LALB_OK;
+    }
+    const Layout base = make_layout(K, 0);
+    int nst = (int)((nd->smem_budget - (int)base.off_stage) / (int)base.stage_bytes);
+    if (nst > 8) nst = 8;
+    if (nst < 2) return LALB_ERR_UNSUPPORTED;
+    const Layout L = make_layout(K, nst);
+
+    // the array keeps the previous call's contents: clear the key, ticket and
+    // status word that this call's reduction starts from
+    if (cudaMemsetAsync(nd->scratch, 0, 16, s) != cudaSuccess) return LALB_ERR_CUDA;
+
+    Q8HeadArgs a = {};
+    a.W = W;
+    a.sw = sw;
+    a.K = K;
+    a.row_begin = row_begin;
+    a.row_end = row_end;
+    a.x = x;
+    a.logits = logits;
+    a.argmax = argmax;
+    a.nstages = nst;
+    a.best = reinterpret_cast<unsigned long long *>(nd->scratch);
+    a.ticket = reinterpret_cast<unsigned int *>(nd->scratch + 8);
+    a.status = reinterpret_cast<unsigned int *>(nd->scratch + 12);
+    int grid = nd->sm_count;
+    const int units = (nrows + kRps - 1) / kRps;
+    if (grid > units) grid = units;
+    q8_head_kernel<kInF32><<<grid, kThreads, L.total, s>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return LALB_ERR_CUDA;
+    return LALB_OK;
 }
