@@ -153,13 +153,14 @@ def build_decoder(ctx, lb, torch, c, seed):
     return dec, layers, (lm_q, lm_s)
 
 
-def gemv_standalone(ctx, torch, stream, reps=200):
-    """The single 18944x3584 Q4_K GEMV with the fused quantizer; 8 weight
-    copies (305 MB, > 2x L2) rotated so every launch streams from HBM."""
+def gemv_standalone(ctx, torch, stream, reps=200, ncopies=8):
+    """The single 18944x3584 Q4_K GEMV with the fused quantizer; weight
+    copies (8 x 38 MB = 305 MB, > 2x L2) rotated so every launch streams
+    from HBM."""
     rows, K = 18944, 3584
     copies = []
     w = torch.empty(rows * K, dtype=torch.float32, device="cuda")
-    for i in range(8):
+    for i in range(ncopies):
         ctx.fill_normal(w, seed=500 + i, sigma=0.02)
         copies.append(ctx.q4k_quantize(w.view(rows, K)))
     del w
@@ -168,17 +169,37 @@ def gemv_standalone(ctx, torch, stream, reps=200):
     y = torch.empty(rows, dtype=torch.float32, device="cuda")
     with torch.cuda.stream(stream):
         for i in range(16):
-            ctx.matmul_q4_k(copies[i % 8], x, rows, K, out=y)
+            ctx.matmul_q4_k(copies[i % ncopies], x, rows, K, out=y)
+    torch.cuda.synchronize()
+    # the timed launches are replayed from a CUDA graph: no host overhead
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(reps):
+            ctx.matmul_q4_k(copies[i % ncopies], x, rows, K, out=y)
+    with torch.cuda.stream(stream):
+        g.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(reps):
-            ctx.matmul_q4_k(copies[i % 8], x, rows, K, out=y)
+        g.replay()
         e1.record(stream)
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / reps
     nbytes = q4k_bytes(rows, K) + 4 * K + 4 * rows
     return {"shape": [rows, K], "us_per_launch": round(us, 3), "bytes": nbytes,
             "gbs": round(nbytes / us / 1e3, 1)}
+
+
+def run_gemv_case(args):
+    """Only the single-GEMV workload (4 rotating copies, 153 MB > L2): a small
+    case for profiler captures, not a bench line."""
+    import torch
+
+    import lalmodel_b200 as lb
+
+    ctx = lb.Context(0)
+    r = gemv_standalone(ctx, torch, torch.cuda.Stream(), reps=args.steps, ncopies=4)
+    print(json.dumps({"case": "gemv", **r}), flush=True)
+    ctx.close()
 
 
 def run_gpu(args, rank, world, local_rank):
@@ -417,6 +438,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--n-layer", type=int, default=CFG["n_layer"],
                     help="fewer layers: only for profiling captures, not a bench line")
+    ap.add_argument("--case", default="decode", choices=["decode", "gemv"],
+                    help="gemv: only the single 18944x3584 GEMV, for profiler captures")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -426,6 +449,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.case == "gemv":
+        run_gemv_case(args)
     else:
         run_gpu(args, rank, world, local_rank)
 

@@ -269,14 +269,37 @@ extern "C" int lalb_decoder_profile_step(lalb_decoder *d, const float *h_in, flo
     if (!h_in || !kernel_us)
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_profile_step: null argument");
     if (int st = check_ready(d)) return st;
-    cudaStream_t s = (cudaStream_t)stream;
+    // The instrumented token is captured into a graph and replayed, so the
+    // intervals hold device time only (no host launch latency between them).
+    cudaStream_t s = nullptr;
+    LALB_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    cudaEvent_t dep = nullptr;
     const int n = 4 * d->cfg.n_layer + 1;
     std::vector<cudaEvent_t> ev(n + 1, nullptr);
     int st = LALB_OK;
     for (auto &e : ev)
         if (cudaEventCreate(&e) != cudaSuccess) st = LALB_ERR_CUDA;
-    if (!st) st = launch_token(d, h_in, nullptr, nullptr, d->argmax_dev, s, &ev);
+    // order the private stream after the caller's work
+    if (!st && (cudaEventCreateWithFlags(&dep, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventRecord(dep, (cudaStream_t)stream) != cudaSuccess ||
+                cudaStreamWaitEvent(s, dep, 0) != cudaSuccess))
+        st = LALB_ERR_CUDA;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    if (!st && cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        st = LALB_ERR_CUDA;
+    if (!st) {
+        st = launch_token(d, h_in, nullptr, nullptr, d->argmax_dev, s, &ev);
+        if (cudaStreamEndCapture(s, &g) != cudaSuccess && !st) st = LALB_ERR_CUDA;
+    }
+    if (!st && cudaGraphInstantiate(&ge, g, 0) != cudaSuccess) st = LALB_ERR_CUDA;
+    if (!st && cudaGraphLaunch(ge, s) != cudaSuccess) st = LALB_ERR_CUDA;
     if (!st && cudaEventSynchronize(ev[n]) != cudaSuccess) st = LALB_ERR_CUDA;
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    if (dep) cudaEventDestroy(dep);
+    cudaStreamSynchronize(s);
+    cudaStreamDestroy(s);
     for (int i = 0; !st && i < n; ++i) {
         float ms = 0.0f;
         if (cudaEventElapsedTime(&ms, ev[i], ev[i + 1]) != cudaSuccess) st = LALB_ERR_CUDA;

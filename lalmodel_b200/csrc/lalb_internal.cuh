@@ -130,6 +130,16 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc,
         : "memory");
 }
 
+// Same copy without an L2 policy (activations, which should stay cached).
+__device__ __forceinline__ void bulk_g2s_plain(void *smem_dst, const void *gsrc,
+                                               uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ---- programmatic dependent launch -----------------------------------------
 // wait: block until the preceding kernel in the stream has completed and its
 // writes are visible (no-op when the launch had no programmatic dependency).

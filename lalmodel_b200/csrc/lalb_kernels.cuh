@@ -37,6 +37,7 @@ struct Q4kGemvArgs {
     int32_t *asumq;        //   its per-32 sums [rows/64]
     float *act_out;        //   nullable: the fp32 product [rows/2]
     int unit;              // CTA row split granularity (64 for kEpiSwiglu)
+    int act_bulk;          // set by the launcher: activations arrive by bulk copy
     int nstages;           // set by the launcher
     unsigned int *status;  // set by the launcher
 };

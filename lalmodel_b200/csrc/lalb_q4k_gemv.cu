@@ -39,9 +39,10 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kMaxStagedK = 4096;   // fp32 activations up to this K are bulk-copied to smem
 
 struct Layout {
-    uint32_t off_xq, off_sx, off_sq, off_red, off_tile, off_stage;
+    uint32_t off_xq, off_sx, off_sq, off_xf, off_red, off_tile, off_stage;
     uint32_t stage_bytes, total;
 };
 
@@ -49,14 +50,17 @@ __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) {
     return (v + a - 1) / a * a;
 }
 
-// Shared-memory layout shared by host (size) and device (pointers).
-__host__ __device__ inline Layout make_layout(int K, int wr, int nstages) {
+// Shared-memory layout shared by host (size) and device (pointers).  The
+// first 128 bytes hold the mbarriers: one per weight stage + one for the
+// activation copy.  xf_floats = K when the fp32 activation is staged.
+__host__ __device__ inline Layout make_layout(int K, int wr, int nstages, int xf_floats) {
     Layout L;
     const uint32_t ns = K / 32;
-    L.off_xq = 128;                                  // mbarriers live below
+    L.off_xq = 128;
     L.off_sx = align_up(L.off_xq + K, 16);
     L.off_sq = L.off_sx + 4 * ns;
-    L.off_red = align_up(L.off_sq + 4 * ns, 16);
+    L.off_xf = align_up(L.off_sq + 4 * ns, 16);
+    L.off_red = align_up(L.off_xf + 4 * xf_floats, 16);
     L.off_tile = L.off_red + 2 * kWarps * 8;         // double partials
     L.off_stage = align_up(L.off_tile + 2 * 64 * 4, 128);
     const uint32_t rps = kWarps / wr;
@@ -69,6 +73,31 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+
+// unsigned bytes of a times signed bytes of b, accumulated into c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Quantizes one 32-element block held one element per lane: writes the int8
+// codes and returns (through the pointers, lane 0 only) the fp32 scale and
+// the int32 sum.  Same operations as the CPU restatement.
+__device__ __forceinline__ void quantize_block32(float v, int lane, int8_t *xq32, float *sx,
+                                                 int *sumq) {
+    const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
+    const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
+    const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
+    const float t = roundf(__fmul_rn(v, id));
+    const int q = t > 127.0f ? 127 : (t < -127.0f ? -127 : (int)t);
+    xq32[lane] = (int8_t)q;
+    const int s = __reduce_add_sync(0xffffffffu, q);
+    if (lane == 0) {
+        *sx = dsc;
+        *sumq = s;
+    }
 }
 
 // One 64-weight group (sub-blocks 2g, 2g+1 of super-block c/4): adds its two
@@ -92,12 +121,18 @@ __device__ __forceinline__ void q4k_group(const uint8_t *__restrict__ rowp, int 
     const int sc0 = (scw >> sh) & 0xFF, sc1 = (scw >> (sh + 8)) & 0xFF;
     const int m0 = (mnw >> sh) & 0xFF, m1 = (mnw >> (sh + 8)) & 0xFF;
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    int s0 = 0, s1 = 0;
+    // low nibbles: plain dot; high nibbles masked in place (16*h as unsigned
+    // bytes), which yields exactly 16 * the dot product
+    int s0a = 0, s0b = 0, s1a = 0, s1b = 0;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        s0 = dp4a((int)(q[i] & 0x0F0F0F0Fu), xv[i], s0);
-        s1 = dp4a((int)((q[i] >> 4) & 0x0F0F0F0Fu), xv[8 + i], s1);
+    for (int i = 0; i < 8; i += 2) {
+        s0a = dp4a_us(q[i] & 0x0F0F0F0Fu, xv[i], s0a);
+        s1a = dp4a_us(q[i] & 0xF0F0F0F0u, xv[8 + i], s1a);
+        s0b = dp4a_us(q[i + 1] & 0x0F0F0F0Fu, xv[i + 1], s0b);
+        s1b = dp4a_us(q[i + 1] & 0xF0F0F0F0u, xv[9 + i], s1b);
     }
+    const int s0 = s0a + s0b;
+    const int s1 = (s1a + s1b) >> 4;
     if (isum2) {
         isum2[0] = s0;
         isum2[1] = s1;
@@ -119,11 +154,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int K = a.K;
     const int G = K >> 6, NS = K >> 5;
     const uint32_t row_bytes = (uint32_t)(K >> 8) * 144u;
-    const Layout L = make_layout(K, WR, a.nstages);
+    const bool staged = IN != kInQ8 && a.act_bulk;
+    const Layout L = make_layout(K, WR, a.nstages, staged ? K : 0);
+    const int nstages = a.nstages;
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *act_bar = bar + nstages;
     int8_t *xq_s = reinterpret_cast<int8_t *>(smem + L.off_xq);
     float *sx_s = reinterpret_cast<float *>(smem + L.off_sx);
-    float *sq_s = reinterpret_cast<float *>(smem + L.off_sq);  // sumq as float
+    int *sq_s = reinterpret_cast<int *>(smem + L.off_sq);
+    float *xf_s = reinterpret_cast<float *>(smem + L.off_xf);
     double *red_s = reinterpret_cast<double *>(smem + L.off_red);
     float *tile_s = reinterpret_cast<float *>(smem + L.off_tile);
     uint8_t *stage_s = smem + L.off_stage;
@@ -138,7 +177,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
     const int r0 = u0 * a.unit, r1 = u1 * a.unit;
     const int nst = (r1 - r0 + RPS - 1) / RPS;
-    const int nstages = a.nstages;
 
     uint64_t policy = 0;
     auto issue = [&](int i) {
@@ -152,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     if (tid == 0) {
-        for (int s = 0; s < nstages; ++s) mbar_init(&bar[s], 1);
+        for (int s = 0; s <= nstages; ++s) mbar_init(&bar[s], 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -167,34 +205,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
 
     // ---- activation prologue -------------------------------------------------
-    if (IN == kInQ8) {
+    if (a.act_bulk) {
+        // one bulk copy per array into shared memory, then everyone waits
+        if (tid == 0) {
+            if (IN == kInQ8) {
+                mbar_arrive_expect_tx(act_bar, (uint32_t)K + 8u * NS);
+                bulk_g2s_plain(xq_s, a.xq, (uint32_t)K, act_bar);
+                bulk_g2s_plain(sx_s, a.sx, 4u * NS, act_bar);
+                bulk_g2s_plain(sq_s, a.sumq, 4u * NS, act_bar);
+            } else {
+                mbar_arrive_expect_tx(act_bar, 4u * K);
+                bulk_g2s_plain(xf_s, a.x, 4u * K, act_bar);
+            }
+        }
+        mbar_wait_bounded(act_bar, 0, a.status);
+    } else if (IN == kInQ8) {
         const int4 *src = reinterpret_cast<const int4 *>(a.xq);
         int4 *dst = reinterpret_cast<int4 *>(xq_s);
         for (int i = tid; i < K / 16; i += kThreads) dst[i] = src[i];
         for (int i = tid; i < NS; i += kThreads) {
             sx_s[i] = a.sx[i];
-            sq_s[i] = (float)a.sumq[i];
+            sq_s[i] = a.sumq[i];
         }
-    } else {
+    }
+    if (IN != kInQ8) {
+        const float *xsrc = staged ? xf_s : a.x;
         float scale = 1.0f;
-        if (IN == kInF32Rms) scale = block_rms_scale(a.x, K);
-        for (int blk = warp; blk < NS; blk += kWarps) {
-            float v = a.x[blk * 32 + lane];
+        if (IN == kInF32Rms) scale = block_rms_scale(xsrc, K);
+        // two blocks per warp per step, both loads issued before either is used
+        for (int blk = warp; blk < NS; blk += 2 * kWarps) {
+            const int blk2 = blk + kWarps;
+            float v = xsrc[blk * 32 + lane];
+            float v2 = blk2 < NS ? xsrc[blk2 * 32 + lane] : 0.0f;
             if (IN == kInF32Rms) {
                 v = __fmul_rn(v, scale);
-                if (a.gamma) v = __fmul_rn(v, a.gamma[blk * 32 + lane]);
+                v2 = __fmul_rn(v2, scale);
+                if (a.gamma) {
+                    v = __fmul_rn(v, a.gamma[blk * 32 + lane]);
+                    if (blk2 < NS) v2 = __fmul_rn(v2, a.gamma[blk2 * 32 + lane]);
+                }
             }
-            const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
-            const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
-            const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
-            const float t = roundf(__fmul_rn(v, id));
-            const int q = t > 127.0f ? 127 : (t < -127.0f ? -127 : (int)t);
-            xq_s[blk * 32 + lane] = (int8_t)q;
-            const int s = __reduce_add_sync(0xffffffffu, q);
-            if (lane == 0) {
-                sx_s[blk] = dsc;
-                sq_s[blk] = (float)s;
-            }
+            quantize_block32(v, lane, xq_s + blk * 32, sx_s + blk, sq_s + blk);
+            if (blk2 < NS) quantize_block32(v2, lane, xq_s + blk2 * 32, sx_s + blk2, sq_s + blk2);
         }
     }
     __syncthreads();
@@ -217,9 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 xv[k][4 * j + 3] = v.w;
             }
             sa0[k] = sx_s[2 * c];
-            sb0[k] = sq_s[2 * c];
+            sb0[k] = (float)sq_s[2 * c];
             sa1[k] = sx_s[2 * c + 1];
-            sb1[k] = sq_s[2 * c + 1];
+            sb1[k] = (float)sq_s[2 * c + 1];
         } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) xv[k][j] = 0;
@@ -288,20 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (warp == kWarps - 1) {
                     const float *tb = tile_s + (tloc & 1) * 64;
                     const float av = silu_mul(tb[lane], tb[32 + lane]);
-                    const uint32_t amax =
-                        __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av)));
-                    const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
-                    const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
-                    const float t = roundf(__fmul_rn(av, id));
-                    const int q = t > 127.0f ? 127 : (t < -127.0f ? -127 : (int)t);
                     const int gt = (r0 >> 6) + tloc;  // 32-element block of the product
-                    a.aq[gt * 32 + lane] = (int8_t)q;
                     if (a.act_out) a.act_out[gt * 32 + lane] = av;
-                    const int s = __reduce_add_sync(0xffffffffu, q);
-                    if (lane == 0) {
-                        a.asx[gt] = dsc;
-                        a.asumq[gt] = s;
-                    }
+                    quantize_block32(av, lane, a.aq + gt * 32, a.asx + gt, a.asumq + gt);
                 }
             }
         }
@@ -313,6 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int buf = i % nstages;
             mbar_wait_bounded(&bar[buf], (uint32_t)(i / nstages) & 1u, a.status);
         }
+        if (a.act_bulk) mbar_wait_bounded(act_bar, 0, a.status);
     }
 }
 
@@ -369,20 +411,29 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int 
     void *fn = select_kernel(in, epi, v.wr, v.gpl);
     if (!fn) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: no variant in=%d epi=%d", in, epi);
 
+    // activations arrive by bulk copy when aligned (and, for fp32, small
+    // enough to stage in shared memory)
+    const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (in == kInQ8)
+        a.act_bulk = al16(a.xq) && al16(a.sx) && al16(a.sumq);
+    else
+        a.act_bulk = a.K <= kMaxStagedK && al16(a.x);
+    const int xf = (in != kInQ8 && a.act_bulk) ? a.K : 0;
+
     // pipeline depth: fill the per-CTA shared-memory budget
     const size_t budget = ctas_per_sm >= 2 ? 110 * 1024 : ctx->smem_optin - 1024;
-    const Layout base = make_layout(a.K, v.wr, 0);
+    const Layout base = make_layout(a.K, v.wr, 0, xf);
     int nst = (int)((budget - base.off_stage) / base.stage_bytes);
-    if (nst > 8) nst = 8;
+    if (nst > 12) nst = 12;
     if (nst < 2) {
         nst = (int)((ctx->smem_optin - 1024 - base.off_stage) / base.stage_bytes);
         ctas_per_sm = 1;
         if (nst < 2) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d too large for smem", a.K);
-        if (nst > 8) nst = 8;
+        if (nst > 12) nst = 12;
     }
     a.nstages = nst;
     a.status = &ctx->scratch->status;
-    const Layout L = make_layout(a.K, v.wr, nst);
+    const Layout L = make_layout(a.K, v.wr, nst, xf);
     {
         const int st = lalb_set_smem_attr(ctx, fn, (int)L.total);
         if (st) return st;
