@@ -48,7 +48,8 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
     auto mark = [&]() -> cudaError_t {
         if (!ev) return cudaSuccess;
         pdl = false;
-        return cudaEventRecord((*ev)[mark_i++], s);
+        // external: inside stream capture this becomes a timestamp node
+        return cudaEventRecordWithFlags((*ev)[mark_i++], s, cudaEventRecordExternal);
     };
     for (int l = 0; l < c.n_layer; ++l) {
         const lalb_layer_weights &w = d->layers[l];
@@ -307,7 +308,9 @@ extern "C" int lalb_decoder_profile_step(lalb_decoder *d, const float *h_in, flo
     }
     for (auto &e : ev)
         if (e) cudaEventDestroy(e);
-    if (st == LALB_ERR_CUDA) return lalb_fail(ctx, st, "decoder_profile_step: event timing failed");
+    if (st == LALB_ERR_CUDA)
+        return lalb_fail(ctx, st, "decoder_profile_step: event timing failed (%s)",
+                         cudaGetErrorString(cudaGetLastError()));
     return st;
 }
 
