@@ -8,20 +8,21 @@
 //   * thread 0 streams that range into a ring of shared-memory stages with
 //     1-D bulk copies (cp.async.bulk, the TMA engine), completion tracked by
 //     one mbarrier per stage, L2 policy evict-first;
-//   * meanwhile all threads quantize the activation (fp32 -> int8 per
-//     32-block, optional RMS normalisation) into shared memory -- the
-//     quantizer is fused, no separate launch;
+//   * the activation arrives by one more bulk copy after the dependency wait
+//     and is quantized (fp32 -> int8 per 32-block, optional RMS
+//     normalisation) in shared memory by the whole CTA -- the quantizer is
+//     fused, no separate launch;
 //   * a "team" of WR warps owns one row of a stage; team lane t owns the
-//     64-weight groups c = t, t + 32*WR, ... (a group = one 32-byte run of
-//     quants = sub-blocks 2g and 2g+1 of a super-block).  The lane keeps the
-//     int8 activations of its groups in registers for the whole kernel, so
-//     shared memory traffic is the weights only;
-//   * per group: 3 x 16-byte shared loads (header, two quant halves), 16 dp4a
-//     producing the two exact int32 sub-block sums, and two fp32 sub-block
-//     terms sx*(d*(sc*isum) - dmin*(m*sumq)), each rounded op by op;
-//   * the terms are accumulated in double (warp shuffles, then across the
-//     team) and the row result is rounded to fp32 once, so the output does
-//     not depend on the thread mapping or summation order;
+//     128-weight half-block c = t (sub-blocks 4(c&1)..4(c&1)+3 of super-block
+//     c/2).  The lane keeps that half-block's int8 activations, scales and
+//     scale*sum terms in registers for the whole kernel, so shared-memory
+//     traffic is the weights only;
+//   * per half-block: 5 x 16-byte shared loads (header, 64 bytes of quants),
+//     32 dp4a giving the four exact int32 sub-block sums, and the exact fp64
+//     products sx*sc*isum and sx*sumq*m, combined with d and dmin;
+//   * the row is reduced in double (warp shuffles, then across the team) and
+//     rounded to fp32 once, so the output is the fp32 rounding of the exact
+//     dot product whatever the thread mapping;
 //   * fused epilogues: store, residual add, SwiGLU + re-quantization of the
 //     product for the next matvec.
 //
@@ -83,8 +84,8 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 }
 
 // Quantizes one 32-element block held one element per lane: writes the int8
-// codes and returns (through the pointers, lane 0 only) the fp32 scale and
-// the int32 sum.  Same operations as the CPU restatement.
+// codes, and (lane 0) the fp32 scale and the int32 sum.  Same operations as
+// the CPU restatement.
 __device__ __forceinline__ void quantize_block32(float v, int lane, int8_t *xq32, float *sx,
                                                  int *sumq) {
     const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
@@ -100,50 +101,68 @@ __device__ __forceinline__ void quantize_block32(float v, int lane, int8_t *xq32
     }
 }
 
-// One 64-weight group (sub-blocks 2g, 2g+1 of super-block c/4): adds its two
-// fp32 sub-block terms to acc; writes the two exact int32 sub-block dot
-// products to isum2 when non-null.  sx = activation scale, sq = sumq (as an
-// exactly representable float).
-__device__ __forceinline__ void q4k_group(const uint8_t *__restrict__ rowp, int c,
-                                          const int (&xv)[16], float sx0, float sq0,
-                                          float sx1, float sq1, int32_t *isum2, double &acc) {
-    const int b = c >> 2, g = c & 3;
+// Activation state of GPL half-blocks of 128 weights, held in registers.
+template <int GPL>
+struct HalfBlockAct {
+    int xv[GPL][32];       // 128 int8 codes each
+    double sxd[GPL][4];    // per sub-block scale (exact as double)
+    double ad[GPL][4];     // scale * sumq (exact as double)
+};
+
+// One half-block of one row: returns d*sum_j sx_j*sc_j*isum_j -
+// dmin*sum_j sx_j*sumq_j*m_j in double; writes the four exact int32
+// sub-block dot products to isum4 when non-null.
+__device__ __forceinline__ double q4k_half(const uint8_t *__restrict__ rowp, int c,
+                                           const int (&xv)[32], const double (&sxd)[4],
+                                           const double (&ad)[4], int32_t *isum4) {
+    const int b = c >> 1, hsel = c & 1;
     const uint8_t *bp = rowp + b * 144;
     const uint4 h = *reinterpret_cast<const uint4 *>(bp);
-    const uint4 qa = *reinterpret_cast<const uint4 *>(bp + 16 + 32 * g);
-    const uint4 qb = *reinterpret_cast<const uint4 *>(bp + 32 + 32 * g);
-    const float d = f16_bits_to_f32(h.x & 0xFFFFu);
-    const float dmin = f16_bits_to_f32(h.x >> 16);
-    const ScaleWords sw = unpack_scale_words(h.y, h.z, h.w);
-    const uint32_t scw = g < 2 ? sw.sc_lo : sw.sc_hi;
-    const uint32_t mnw = g < 2 ? sw.mn_lo : sw.mn_hi;
-    const uint32_t sh = (g & 1) * 16;
-    const int sc0 = (scw >> sh) & 0xFF, sc1 = (scw >> (sh + 8)) & 0xFF;
-    const int m0 = (mnw >> sh) & 0xFF, m1 = (mnw >> (sh + 8)) & 0xFF;
-    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    // low nibbles: plain dot; high nibbles masked in place (16*h as unsigned
-    // bytes), which yields exactly 16 * the dot product
-    int s0a = 0, s0b = 0, s1a = 0, s1b = 0;
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(bp + 16 + 64 * hsel);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(bp + 32 + 64 * hsel);
+    const uint4 q2 = *reinterpret_cast<const uint4 *>(bp + 48 + 64 * hsel);
+    const uint4 q3 = *reinterpret_cast<const uint4 *>(bp + 64 + 64 * hsel);
+    // scales / mins of sub-blocks 4hsel..4hsel+3, byte j = sub-block 4hsel+j
+    const uint32_t scw = hsel ? ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u))
+                              : (h.y & 0x3F3F3F3Fu);
+    const uint32_t mnw = hsel ? (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u))
+                              : (h.z & 0x3F3F3F3Fu);
+    const uint32_t w[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                            q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+    // sub-block 0: low nibbles of words 0-7; 1: high nibbles of words 0-7;
+    // 2: low nibbles of words 8-15; 3: high nibbles of words 8-15.  A high
+    // nibble masked in place is 16*q as an unsigned byte: the dot is 16x.
+    int a0 = 0, b0 = 0, a1 = 0, b1 = 0, a2 = 0, b2 = 0, a3 = 0, b3 = 0;
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
-        s0a = dp4a_us(q[i] & 0x0F0F0F0Fu, xv[i], s0a);
-        s1a = dp4a_us(q[i] & 0xF0F0F0F0u, xv[8 + i], s1a);
-        s0b = dp4a_us(q[i + 1] & 0x0F0F0F0Fu, xv[i + 1], s0b);
-        s1b = dp4a_us(q[i + 1] & 0xF0F0F0F0u, xv[9 + i], s1b);
+        a0 = dp4a_us(w[i] & 0x0F0F0F0Fu, xv[i], a0);
+        b0 = dp4a_us(w[i + 1] & 0x0F0F0F0Fu, xv[i + 1], b0);
+        a1 = dp4a_us(w[i] & 0xF0F0F0F0u, xv[8 + i], a1);
+        b1 = dp4a_us(w[i + 1] & 0xF0F0F0F0u, xv[9 + i], b1);
+        a2 = dp4a_us(w[8 + i] & 0x0F0F0F0Fu, xv[16 + i], a2);
+        b2 = dp4a_us(w[9 + i] & 0x0F0F0F0Fu, xv[17 + i], b2);
+        a3 = dp4a_us(w[8 + i] & 0xF0F0F0F0u, xv[24 + i], a3);
+        b3 = dp4a_us(w[9 + i] & 0xF0F0F0F0u, xv[25 + i], b3);
     }
-    const int s0 = s0a + s0b;
-    const int s1 = (s1a + s1b) >> 4;
-    if (isum2) {
-        isum2[0] = s0;
-        isum2[1] = s1;
+    const int s0 = a0 + b0, s1 = (a1 + b1) >> 4, s2 = a2 + b2, s3 = (a3 + b3) >> 4;
+    if (isum4) {
+        isum4[0] = s0;
+        isum4[1] = s1;
+        isum4[2] = s2;
+        isum4[3] = s3;
     }
-    // t = sx * (d*(sc*isum) - dmin*(m*sumq)); sc*isum and m*sumq are exact
-    const float t0 = __fmul_rn(sx0, __fsub_rn(__fmul_rn(d, (float)(sc0 * s0)),
-                                              __fmul_rn(dmin, __fmul_rn((float)m0, sq0))));
-    const float t1 = __fmul_rn(sx1, __fsub_rn(__fmul_rn(d, (float)(sc1 * s1)),
-                                              __fmul_rn(dmin, __fmul_rn((float)m1, sq1))));
-    acc += (double)t0;
-    acc += (double)t1;
+    // sc*isum fits 22 bits, so sx*(sc*isum) and sx*sumq*m are exact in fp64
+    double s1acc = sxd[0] * (double)((int)(scw & 0xFF) * s0);
+    s1acc = fma(sxd[1], (double)((int)((scw >> 8) & 0xFF) * s1), s1acc);
+    s1acc = fma(sxd[2], (double)((int)((scw >> 16) & 0xFF) * s2), s1acc);
+    s1acc = fma(sxd[3], (double)((int)(scw >> 24) * s3), s1acc);
+    double s2acc = ad[0] * (double)(mnw & 0xFF);
+    s2acc = fma(ad[1], (double)((mnw >> 8) & 0xFF), s2acc);
+    s2acc = fma(ad[2], (double)((mnw >> 16) & 0xFF), s2acc);
+    s2acc = fma(ad[3], (double)(mnw >> 24), s2acc);
+    const double d = (double)f16_bits_to_f32(h.x & 0xFFFFu);
+    const double dmin = (double)f16_bits_to_f32(h.x >> 16);
+    return fma(d, s1acc, -dmin * s2acc);
 }
 
 template <int WR, int GPL, int IN, int EPI>
@@ -152,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int RPS = kWarps / WR;  // rows per stage (one per team)
     const int K = a.K;
-    const int G = K >> 6, NS = K >> 5;
+    const int NH = K >> 7, NS = K >> 5;
     const uint32_t row_bytes = (uint32_t)(K >> 8) * 144u;
     const bool staged = IN != kInQ8 && a.act_bulk;
     const Layout L = make_layout(K, WR, a.nstages, staged ? K : 0);
@@ -253,29 +272,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_launch_dependents();
 
     // ---- per-lane activation registers ------------------------------------
-    int xv[GPL][16];
-    float sa0[GPL], sb0[GPL], sa1[GPL], sb1[GPL];
+    HalfBlockAct<GPL> act;
 #pragma unroll
     for (int k = 0; k < GPL; ++k) {
         const int c = tl + k * 32 * WR;
-        if (c < G) {
-            const int4 *p = reinterpret_cast<const int4 *>(xq_s + 64 * c);
+        if (c < NH) {
+            const int4 *p = reinterpret_cast<const int4 *>(xq_s + 128 * c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int4 v = p[j];
+                act.xv[k][4 * j + 0] = v.x;
+                act.xv[k][4 * j + 1] = v.y;
+                act.xv[k][4 * j + 2] = v.z;
+                act.xv[k][4 * j + 3] = v.w;
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const int4 v = p[j];
-                xv[k][4 * j + 0] = v.x;
-                xv[k][4 * j + 1] = v.y;
-                xv[k][4 * j + 2] = v.z;
-                xv[k][4 * j + 3] = v.w;
+                const double sxv = (double)sx_s[4 * c + j];
+                act.sxd[k][j] = sxv;
+                act.ad[k][j] = sxv * (double)sq_s[4 * c + j];
             }
-            sa0[k] = sx_s[2 * c];
-            sb0[k] = (float)sq_s[2 * c];
-            sa1[k] = sx_s[2 * c + 1];
-            sb1[k] = (float)sq_s[2 * c + 1];
         } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) xv[k][j] = 0;
-            sa0[k] = sb0[k] = sa1[k] = sb1[k] = 0.0f;
+            for (int j = 0; j < 32; ++j) act.xv[k][j] = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) act.sxd[k][j] = act.ad[k][j] = 0.0;
         }
     }
 
@@ -293,9 +314,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int k = 0; k < GPL; ++k) {
                 const int c = tl + k * 32 * WR;
-                if (c < G)
-                    q4k_group(rowp, c, xv[k], sa0[k], sb0[k], sa1[k], sb1[k],
-                              isum_row ? isum_row + 2 * c : nullptr, acc);
+                if (c < NH)
+                    acc += q4k_half(rowp, c, act.xv[k], act.sxd[k], act.ad[k],
+                                    isum_row ? isum_row + 4 * c : nullptr);
             }
         }
         acc = warp_sum_d(acc);
@@ -362,18 +383,23 @@ struct Variant {
     int wr, gpl;
 };
 
-Variant pick_variant(int G) {
-    if (G <= 64) return {1, 2};
-    if (G <= 384) return {4, 3};
-    if (G <= 1024) return {8, 4};
+// Lanes per row = 32*WR, each owning GPL half-blocks of 128 weights.
+Variant pick_variant(int NH) {
+    if (NH <= 32) return {1, 1};
+    if (NH <= 64) return {2, 1};
+    if (NH <= 128) return {4, 1};
+    if (NH <= 256) return {8, 1};
+    if (NH <= 512) return {8, 2};
     return {0, 0};
 }
 
 template <int IN, int EPI>
 void *kernel_ptr(int wr, int gpl) {
-    if (wr == 1 && gpl == 2) return (void *)q4k_gemv_kernel<1, 2, IN, EPI>;
-    if (wr == 4 && gpl == 3) return (void *)q4k_gemv_kernel<4, 3, IN, EPI>;
-    if (wr == 8 && gpl == 4) return (void *)q4k_gemv_kernel<8, 4, IN, EPI>;
+    if (wr == 1) return (void *)q4k_gemv_kernel<1, 1, IN, EPI>;
+    if (wr == 2) return (void *)q4k_gemv_kernel<2, 1, IN, EPI>;
+    if (wr == 4) return (void *)q4k_gemv_kernel<4, 1, IN, EPI>;
+    if (wr == 8 && gpl == 1) return (void *)q4k_gemv_kernel<8, 1, IN, EPI>;
+    if (wr == 8 && gpl == 2) return (void *)q4k_gemv_kernel<8, 2, IN, EPI>;
     return nullptr;
 }
 
@@ -403,8 +429,7 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int 
         return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: W must be 16-byte aligned");
     if (a.unit <= 0 || a.rows % a.unit)
         return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: rows %% unit != 0");
-    const int G = a.K / 64;
-    const Variant v = pick_variant(G);
+    const Variant v = pick_variant(a.K / 128);
     if (!v.wr) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d > 65536", a.K);
     if (in == kInQ8 && (reinterpret_cast<uintptr_t>(a.xq) & 15))
         return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: xq must be 16-byte aligned");

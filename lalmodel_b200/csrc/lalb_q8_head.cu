@@ -13,9 +13,10 @@
 // row).  Lane l owns 32-byte blocks c = l, l+32, l+64, l+96 and keeps their
 // activations in registers; it reads the two 16-byte halves of each block
 // in an order that alternates every 4 lanes, so a warp's shared loads hit
-// all 32 banks once per 128 bytes.  The fp32 block terms sx*isum are summed
-// in double and rounded once.  Argmax: per-warp running best (first maximum
-// wins because each warp walks rows in increasing order), a CTA reduction,
+// all 32 banks once per 128 bytes.  The exact block products sx*isum are
+// summed in double, scaled by the row scale and rounded to fp32 once.
+// Argmax: per-warp running best (first maximum wins because each warp walks
+// rows in increasing order), a CTA reduction,
 // one 64-bit atomicMax of (ordered logit, ~row) per CTA, and the last CTA to
 // arrive (ticket counter) publishes the row index and resets the scratch
 // for the next call.
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_head_kernel(const Q8HeadArgs a
     // ---- per-lane activation registers ---------------------------------------
     const int h0 = (lane >> 2) & 1;  // which 16-byte half this lane reads first
     int xv[kMaxGpl][8];
-    float sxv[kMaxGpl];
+    double sxv[kMaxGpl];
 #pragma unroll
     for (int k = 0; k < kMaxGpl; ++k) {
         const int c = lane + 32 * k;
@@ -140,11 +141,11 @@ __global__ void __launch_bounds__(kThreads, 1) q8_head_kernel(const Q8HeadArgs a
             const int4 hi = *reinterpret_cast<const int4 *>(xq_s + 32 * c + 16);
             xv[k][0] = lo.x; xv[k][1] = lo.y; xv[k][2] = lo.z; xv[k][3] = lo.w;
             xv[k][4] = hi.x; xv[k][5] = hi.y; xv[k][6] = hi.z; xv[k][7] = hi.w;
-            sxv[k] = sx_s[c];
+            sxv[k] = (double)sx_s[c];
         } else {
 #pragma unroll
             for (int j = 0; j < 8; ++j) xv[k][j] = 0;
-            sxv[k] = 0.0f;
+            sxv[k] = 0.0;
         }
     }
 
@@ -176,13 +177,13 @@ __global__ void __launch_bounds__(kThreads, 1) q8_head_kernel(const Q8HeadArgs a
                     s = dp4a((int)hi.z, xv[k][6], s);
                     s = dp4a((int)hi.w, xv[k][7], s);
                     if (isum_row) isum_row[c] = s;
-                    acc += (double)__fmul_rn(sxv[k], (float)s);
+                    acc = fma(sxv[k], (double)s, acc);   // sx*isum is exact in fp64
                 }
             }
         }
         acc = warp_sum_d(acc);
         if (row < r1 && ok) {
-            const float v = __fmul_rn(a.sw[row], (float)acc);
+            const float v = (float)((double)a.sw[row] * acc);
             if (lane == 0 && a.logits) a.logits[row - a.row_begin] = v;
             if (best_r < 0 || v > best_v) {
                 best_v = v;

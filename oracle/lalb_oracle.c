@@ -257,7 +257,9 @@ void lalb_o_q4k_matmul(const uint8_t *W, int rows, int K, const int8_t *xq,
             const int8_t *xm = xq + (size_t)m * K;
             const float *sxm = sx + (size_t)m * ns;
             const int32_t *sqm = sumq + (size_t)m * ns;
-            double acc = 0.0;
+            /* every product below is exact in binary128 (at most 24 + 11 + 22
+             * significant bits); the sum is rounded once, to fp32, at the end */
+            __float128 acc = 0;
             for (int b = 0; b < nb; b++) {
                 const uint8_t *blk = W + ((size_t)r * nb + b) * LALB_O_Q4K_BYTES;
                 float d = lalb_o_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
@@ -275,10 +277,9 @@ void lalb_o_q4k_matmul(const uint8_t *W, int rows, int K, const int8_t *xq,
                     }
                     int sidx = 8 * b + j;
                     if (isum) isum[((size_t)m * rows + r) * ns + sidx] = s;
-                    float a = d * (float)(sm[j] * s);
-                    float c = dmin * (float)(sm[8 + j] * sqm[sidx]);
-                    float t = sxm[sidx] * (a - c);
-                    acc += (double)t;
+                    __float128 a = (__float128)d * (__float128)(sm[j] * s);
+                    __float128 c = (__float128)dmin * (__float128)(sm[8 + j] * sqm[sidx]);
+                    acc += (__float128)sxm[sidx] * (a - c);
                 }
             }
             y[(size_t)m * rows + r] = (float)acc;
@@ -324,15 +325,15 @@ int lalb_o_q8_lmhead_range(const int8_t *W, const float *sw, int K, int r0,
 #pragma omp parallel for schedule(static)
     for (int r = r0; r < r1; r++) {
         const int8_t *wr = W + (size_t)r * K;
-        double acc = 0.0;
+        __float128 acc = 0;   /* exact: sx * isum has at most 24 + 20 bits */
         for (int b = 0; b < nblk; b++) {
             int32_t s = 0;
             for (int i = 0; i < 32; i++)
                 s += (int32_t)wr[32 * b + i] * (int32_t)xq[32 * b + i];
             if (isum) isum[(size_t)(r - r0) * nblk + b] = s;
-            acc += (double)(sx[b] * (float)s);
+            acc += (__float128)sx[b] * (__float128)s;
         }
-        logits[r - r0] = sw[r] * (float)acc;
+        logits[r - r0] = (float)((__float128)sw[r] * acc);
     }
     return r1 > r0 ? r0 + lalb_o_argmax(logits, r1 - r0) : -1;
 }

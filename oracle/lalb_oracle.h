@@ -29,8 +29,9 @@
  * Q4_K min-max weight quantizer itself has no third-party twin (the
  * reference's converter scripts/convert_qwen7b_q4k.py is absent).
  *
- * All arithmetic is IEEE single precision with no contraction
- * (-ffp-contract=off); integer sums are exact.
+ * Quantizers use IEEE single precision with no contraction (-ffp-contract=
+ * off); the matvec and LM-head outputs are the fp32 roundings of their exact
+ * real values (integer sums exact, products and sums in binary128).
  */
 #ifndef LALB_ORACLE_H
 #define LALB_ORACLE_H
@@ -69,10 +70,10 @@ void lalb_o_quantize_act(const float *x, int M, int K, int8_t *xq, float *sx,
                          int32_t *sumq);
 
 /* --- Q4_K x Q8 matvec / matmul -------------------------------------------
- * y[m*rows + r] = sum over sub-blocks s of
- *     sx[m][s] * ( d*(float)(sc_s*isum_s) - dmin*(float)(m_s*sumq[m][s]) )
- * summed in double and rounded once.  isum (nullable) receives the exact
- * int32 sub-block dot products, laid out [m][r][K/32]. */
+ * y[m*rows + r] = the fp32 rounding of the exact real value
+ *     sum over sub-blocks s of  sx[m][s] * (d*sc_s*isum_s - dmin*m_s*sumq[m][s])
+ * (computed exactly in binary128, rounded once).  isum (nullable) receives
+ * the exact int32 sub-block dot products, laid out [m][r][K/32]. */
 void lalb_o_q4k_matmul(const uint8_t *W, int rows, int K, const int8_t *xq,
                        const float *sx, const int32_t *sumq, int M, float *y,
                        int32_t *isum);
@@ -80,9 +81,9 @@ void lalb_o_q4k_matmul(const uint8_t *W, int rows, int K, const int8_t *xq,
 /* --- Q8 (int8 per-row-scaled) LM head ----------------------------------- */
 void lalb_o_q8_quantize_rows(const float *w, int rows, int K, int8_t *q,
                              float *s);
-/* logits[r - r0] = sw[r] * (float)( sum_b sx[b]*(float)isum_b )  for r in
- * [r0, r1); isum (nullable) gets [r1-r0][K/32] int32 block dots.  Returns the
- * first index (absolute row number) of the maximum logit. */
+/* logits[r - r0] = fp32 rounding of the exact sw[r] * sum_b sx[b]*isum_b for r
+ * in [r0, r1); isum (nullable) gets [r1-r0][K/32] int32 block dots.  Returns
+ * the first index (absolute row number) of the maximum logit. */
 int lalb_o_q8_lmhead_range(const int8_t *W, const float *sw, int K, int r0,
                            int r1, const int8_t *xq, const float *sx,
                            float *logits, int32_t *isum);
