@@ -38,6 +38,7 @@ struct Q4kGemvArgs {
     float *act_out;        //   nullable: the fp32 product [rows/2]
     int unit;              // CTA row split granularity (64 for kEpiSwiglu)
     int act_bulk;          // set by the launcher: activations arrive by bulk copy
+    int wr, teams;         // set by the launcher: warps per row, teams per CTA
     int nstages;           // set by the launcher
     unsigned int *status;  // set by the launcher
 };

@@ -1,30 +1,35 @@
 // lalb_q4k_gemv.cu -- Q4_K x Q8 matvec for batch-1 decode on sm_100a.
 //
 // Memory-bound by design: the only bytes that must cross HBM are the Q4_K
-// super-blocks (4.5 bits per weight).  Structure of one CTA (256 threads):
+// super-blocks (4.5 bits per weight).  One CTA owns a contiguous range of
+// weight rows (one contiguous byte range of the row-major matrix) and is
+// split into T independent teams of WR warps:
 //
-//   * it owns a contiguous range of weight rows, i.e. one contiguous byte
-//     range of the row-major Q4_K matrix;
-//   * thread 0 streams that range into a ring of shared-memory stages with
-//     1-D bulk copies (cp.async.bulk, the TMA engine), completion tracked by
-//     one mbarrier per stage, L2 policy evict-first;
-//   * the activation arrives by one more bulk copy after the dependency wait
-//     and is quantized (fp32 -> int8 per 32-block, optional RMS
-//     normalisation) in shared memory by the whole CTA -- the quantizer is
-//     fused, no separate launch;
-//   * a "team" of WR warps owns one row of a stage; team lane t owns the
-//     128-weight half-block c = t (sub-blocks 4(c&1)..4(c&1)+3 of super-block
-//     c/2).  The lane keeps that half-block's int8 activations, scales and
-//     scale*sum terms in registers for the whole kernel, so shared-memory
-//     traffic is the weights only;
-//   * per half-block: 5 x 16-byte shared loads (header, 64 bytes of quants),
-//     32 dp4a giving the four exact int32 sub-block sums, and the exact fp64
-//     products sx*sc*isum and sx*sumq*m, combined with d and dmin;
-//   * the row is reduced in double (warp shuffles, then across the team) and
-//     rounded to fp32 once, so the output is the fp32 rounding of the exact
-//     dot product whatever the thread mapping;
+//   * a stage is kR = 4 consecutive rows.  Team t takes stages t, t+T, ...;
+//     it owns kBufPerTeam shared-memory buffers and keeps them full itself:
+//     after the team has read a buffer, one of its lanes refills it with a
+//     1-D bulk copy (cp.async.bulk, the TMA engine) of the team's next stage,
+//     completion tracked by one mbarrier per buffer.  No CTA-wide barrier in
+//     the main loop; the weights stream with an L2 evict-first policy;
+//   * the activation arrives after the dependency wait (bulk copy when it is
+//     already quantized) and is quantized in the prologue one 32-block per
+//     thread (fp32 -> int8 with an fp32 scale, optional RMS normalisation);
+//   * warp k of a team owns the 128-weight half-blocks c = 32k + lane; the
+//     lane keeps that half-block's int8 activations, scales and scale*sum
+//     terms in registers for the whole kernel, so shared-memory traffic is
+//     the weights only;
+//   * per half-block and row: 5 x 16-byte shared loads (header, 64 bytes of
+//     quants), 32 dp4a giving the four exact int32 sub-block sums, and the
+//     exact fp64 products sx*sc*isum and sx*sumq*m, combined with d and dmin.
+//     The 4 rows of a stage are 4 independent chains;
+//   * a transposed shuffle reduction sums the 4 rows across the warp at once;
+//     teams of several warps combine their partials through shared memory
+//     (the last warp to arrive finishes the rows and refills the buffer);
+//   * rows are summed in double and rounded to fp32 once, so the output is the
+//     fp32 rounding of the exact dot product whatever the thread mapping;
 //   * fused epilogues: store, residual add, SwiGLU + re-quantization of the
-//     product for the next matvec.
+//     product for the next matvec (64-row tiles completed through a small
+//     ring of shared-memory tiles with arrival counters).
 //
 // References (paths inside the reference project): lal_matmul_q4_k
 // (runtime/lal_q4k_kernel.h, README.md:130,210), unpack_scales_6bit
@@ -38,13 +43,15 @@ using namespace lalb;
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kMaxStagedK = 4096;   // fp32 activations up to this K are bulk-copied to smem
+constexpr int kR = 4;            // rows per stage
+constexpr int kBufPerTeam = 2;   // stage buffers owned by each team
+constexpr int kTiles = 4;        // SwiGLU tile ring
+constexpr int kMaxThreads = 512;
 
 struct Layout {
-    uint32_t off_xq, off_sx, off_sq, off_xf, off_red, off_tile, off_stage;
-    uint32_t stage_bytes, total;
+    uint32_t off_xq, off_sx, off_sq, off_red, off_rcnt, off_issued, off_tile, off_tcnt, off_ttag;
+    uint32_t off_stage, stage_bytes, total;
+    int nstages;
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) {
@@ -52,28 +59,27 @@ __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) {
 }
 
 // Shared-memory layout shared by host (size) and device (pointers).  The
-// first 128 bytes hold the mbarriers: one per weight stage + one for the
-// activation copy.  xf_floats = K when the fp32 activation is staged.
-__host__ __device__ inline Layout make_layout(int K, int wr, int nstages, int xf_floats) {
+// first bytes hold the mbarriers: one per stage buffer + one for the
+// activation copy.
+__host__ __device__ inline Layout make_layout(int K, int wr, int teams) {
     Layout L;
     const uint32_t ns = K / 32;
-    L.off_xq = 128;
+    L.nstages = teams * kBufPerTeam;
+    L.off_xq = align_up(8u * (L.nstages + 1), 128);
     L.off_sx = align_up(L.off_xq + K, 16);
     L.off_sq = L.off_sx + 4 * ns;
-    L.off_xf = align_up(L.off_sq + 4 * ns, 16);
-    L.off_red = align_up(L.off_xf + 4 * xf_floats, 16);
-    L.off_tile = L.off_red + 2 * kWarps * 8;         // double partials
-    L.off_stage = align_up(L.off_tile + 2 * 64 * 4, 128);
-    const uint32_t rps = kWarps / wr;
-    L.stage_bytes = rps * (uint32_t)(K / 256) * 144u;
-    L.total = L.off_stage + nstages * L.stage_bytes;
+    L.off_red = align_up(L.off_sq + 4 * ns, 16);
+    uint32_t nred = (uint32_t)L.nstages * wr * kR;
+    if (nred < 40) nred = 40;                        // also the prologue's block reduction
+    L.off_rcnt = L.off_red + 8 * nred;
+    L.off_issued = L.off_rcnt + 4 * L.nstages;
+    L.off_tile = align_up(L.off_issued + 4 * teams, 16);
+    L.off_tcnt = L.off_tile + kTiles * 64 * 4;
+    L.off_ttag = L.off_tcnt + 4 * kTiles;
+    L.off_stage = align_up(L.off_ttag + 4 * kTiles, 128);
+    L.stage_bytes = kR * (uint32_t)(K / 256) * 144u;
+    L.total = L.off_stage + L.nstages * L.stage_bytes;
     return L;
-}
-
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
 }
 
 // unsigned bytes of a times signed bytes of b, accumulated into c
@@ -101,13 +107,51 @@ __device__ __forceinline__ void quantize_block32(float v, int lane, int8_t *xq32
     }
 }
 
-// Activation state of GPL half-blocks of 128 weights, held in registers.
-template <int GPL>
-struct HalfBlockAct {
-    int xv[GPL][32];       // 128 int8 codes each
-    double sxd[GPL][4];    // per sub-block scale (exact as double)
-    double ad[GPL][4];     // scale * sumq (exact as double)
-};
+// Quantizes one 32-block held entirely by one thread (same operations).
+__device__ __forceinline__ void quantize_block_thread(const float (&v)[32], int8_t *xq32,
+                                                      float *sx, int *sumq) {
+    uint32_t amax = 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = max(amax, __float_as_uint(fabsf(v[i])));
+    const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
+    const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
+    int s = 0;
+    uint32_t packed[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float t = roundf(__fmul_rn(v[4 * w + i], id));
+            const int q = t > 127.0f ? 127 : (t < -127.0f ? -127 : (int)t);
+            s += q;
+            word |= ((uint32_t)q & 0xFFu) << (8 * i);
+        }
+        packed[w] = word;
+    }
+    int4 *dst = reinterpret_cast<int4 *>(xq32);
+    dst[0] = make_int4((int)packed[0], (int)packed[1], (int)packed[2], (int)packed[3]);
+    dst[1] = make_int4((int)packed[4], (int)packed[5], (int)packed[6], (int)packed[7]);
+    *sx = dsc;
+    *sumq = s;
+}
+
+__device__ __forceinline__ void load_block32(const float *x, bool vec, float (&v)[32]) {
+    if (vec) {
+        const float4 *p = reinterpret_cast<const float4 *>(x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 f = p[i];
+            v[4 * i] = f.x;
+            v[4 * i + 1] = f.y;
+            v[4 * i + 2] = f.z;
+            v[4 * i + 3] = f.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = x[i];
+    }
+}
 
 // One half-block of one row: returns d*sum_j sx_j*sc_j*isum_j -
 // dmin*sum_j sx_j*sumq_j*m_j in double; writes the four exact int32
@@ -165,247 +209,276 @@ __device__ __forceinline__ double q4k_half(const uint8_t *__restrict__ rowp, int
     return fma(d, s1acc, -dmin * s2acc);
 }
 
-template <int WR, int GPL, int IN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-    q4k_gemv_kernel(const Q4kGemvArgs a) {
+// Sums v[0..3] (one value per row) over the 32 lanes.  On return lane L holds
+// the total of row ((L >> 4) & 1) * 2 + ((L >> 3) & 1).
+__device__ __forceinline__ double warp_sum_rows4(const double (&v)[4], int lane) {
+    const bool hi16 = lane & 16;
+    const double send0 = hi16 ? v[0] : v[2], send1 = hi16 ? v[1] : v[3];
+    const double keep0 = hi16 ? v[2] : v[0], keep1 = hi16 ? v[3] : v[1];
+    const double w0 = keep0 + __shfl_xor_sync(0xffffffffu, send0, 16);
+    const double w1 = keep1 + __shfl_xor_sync(0xffffffffu, send1, 16);
+    const bool hi8 = lane & 8;
+    double u = (hi8 ? w1 : w0) + __shfl_xor_sync(0xffffffffu, hi8 ? w0 : w1, 8);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+    return u;
+}
+
+template <int IN, int EPI>
+__global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int RPS = kWarps / WR;  // rows per stage (one per team)
+    const int WR = a.wr, T = a.teams;
     const int K = a.K;
     const int NH = K >> 7, NS = K >> 5;
     const uint32_t row_bytes = (uint32_t)(K >> 8) * 144u;
-    const bool staged = IN != kInQ8 && a.act_bulk;
-    const Layout L = make_layout(K, WR, a.nstages, staged ? K : 0);
-    const int nstages = a.nstages;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *act_bar = bar + nstages;
+    const Layout L = make_layout(K, WR, T);
+    const int nstages = L.nstages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *act_bar = full + nstages;
     int8_t *xq_s = reinterpret_cast<int8_t *>(smem + L.off_xq);
     float *sx_s = reinterpret_cast<float *>(smem + L.off_sx);
     int *sq_s = reinterpret_cast<int *>(smem + L.off_sq);
-    float *xf_s = reinterpret_cast<float *>(smem + L.off_xf);
     double *red_s = reinterpret_cast<double *>(smem + L.off_red);
+    int *rcnt_s = reinterpret_cast<int *>(smem + L.off_rcnt);
+    int *issued_s = reinterpret_cast<int *>(smem + L.off_issued);  // stages issued per team
     float *tile_s = reinterpret_cast<float *>(smem + L.off_tile);
+    int *tcnt_s = reinterpret_cast<int *>(smem + L.off_tcnt);
+    volatile int *ttag_s = reinterpret_cast<volatile int *>(smem + L.off_ttag);
     uint8_t *stage_s = smem + L.off_stage;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int team = warp / WR, wit = warp % WR;
-    const int tl = wit * 32 + lane;
+    const int nthreads = blockDim.x;
+    const int team = warp / WR, kw = warp % WR;
+    const int c = kw * 32 + lane;  // this lane's half-block
 
     // contiguous row range of this CTA, in units of a.unit rows
     const int nunits = a.rows / a.unit;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x);
     const int u1 = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x);
     const int r0 = u0 * a.unit, r1 = u1 * a.unit;
-    const int nst = (r1 - r0 + RPS - 1) / RPS;
+    const int nst = (r1 - r0 + kR - 1) / kR;
+    const int my_stages = team < nst ? (nst - team + T - 1) / T : 0;
 
-    uint64_t policy = 0;
-    auto issue = [&](int i) {
-        const int rs = r0 + i * RPS;
-        const int nr = min(RPS, r1 - rs);
+    // stage s of this team: buffer team*kBufPerTeam + (it % kBufPerTeam),
+    // that buffer's (it / kBufPerTeam)-th use, it = s / T
+    auto issue = [&](int it, uint64_t pol) {
+        const int s = team + it * T;
+        const int rs = r0 + s * kR;
+        const int nr = min(kR, r1 - rs);
         const uint32_t bytes = (uint32_t)nr * row_bytes;
-        const int buf = i % nstages;
-        mbar_arrive_expect_tx(&bar[buf], bytes);
+        const int buf = team * kBufPerTeam + it % kBufPerTeam;
+        issued_s[team] = it + 1;
+        mbar_arrive_expect_tx(&full[buf], bytes);
         bulk_g2s(stage_s + (size_t)buf * L.stage_bytes, a.W + (size_t)rs * row_bytes, bytes,
-                 &bar[buf], policy);
+                 &full[buf], pol);
     };
 
     if (tid == 0) {
-        for (int s = 0; s <= nstages; ++s) mbar_init(&bar[s], 1);
+        for (int s = 0; s <= nstages; ++s) mbar_init(&full[s], 1);
         fence_barrier_init();
     }
-    __syncthreads();
-    if (tid == 0) {
-        policy = l2_evict_first_policy();
-        const int pre = min(nstages, nst);
-        for (int i = 0; i < pre; ++i) issue(i);
+    for (int i = tid; i < nstages; i += nthreads) rcnt_s[i] = 0;
+    for (int i = tid; i < T; i += nthreads) issued_s[i] = 0;
+    if (tid < kTiles) {
+        tcnt_s[tid] = 0;
+        ttag_s[tid] = tid;
     }
+    __syncthreads();
+    const uint64_t policy = l2_evict_first_policy();
+    if (kw == 0 && lane == 0)
+        for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
 
     // The weights are never written by the preceding kernel, so their
     // stream starts before the dependency wait; activations come after it.
     pdl_wait();
 
     // ---- activation prologue -------------------------------------------------
-    if (a.act_bulk) {
-        // one bulk copy per array into shared memory, then everyone waits
-        if (tid == 0) {
-            if (IN == kInQ8) {
+    if (IN == kInQ8) {
+        if (a.act_bulk) {
+            if (tid == 0) {
                 mbar_arrive_expect_tx(act_bar, (uint32_t)K + 8u * NS);
                 bulk_g2s_plain(xq_s, a.xq, (uint32_t)K, act_bar);
                 bulk_g2s_plain(sx_s, a.sx, 4u * NS, act_bar);
                 bulk_g2s_plain(sq_s, a.sumq, 4u * NS, act_bar);
-            } else {
-                mbar_arrive_expect_tx(act_bar, 4u * K);
-                bulk_g2s_plain(xf_s, a.x, 4u * K, act_bar);
+            }
+            mbar_wait_bounded(act_bar, 0, a.status);
+        } else {
+            const int4 *src = reinterpret_cast<const int4 *>(a.xq);
+            int4 *dst = reinterpret_cast<int4 *>(xq_s);
+            for (int i = tid; i < K / 16; i += nthreads) dst[i] = src[i];
+            for (int i = tid; i < NS; i += nthreads) {
+                sx_s[i] = a.sx[i];
+                sq_s[i] = a.sumq[i];
             }
         }
-        mbar_wait_bounded(act_bar, 0, a.status);
-    } else if (IN == kInQ8) {
-        const int4 *src = reinterpret_cast<const int4 *>(a.xq);
-        int4 *dst = reinterpret_cast<int4 *>(xq_s);
-        for (int i = tid; i < K / 16; i += kThreads) dst[i] = src[i];
-        for (int i = tid; i < NS; i += kThreads) {
-            sx_s[i] = a.sx[i];
-            sq_s[i] = a.sumq[i];
-        }
-    }
-    if (IN != kInQ8) {
-        const float *xsrc = staged ? xf_s : a.x;
+    } else {
+        const bool vec = a.act_bulk;  // x is 16-byte aligned
         float scale = 1.0f;
-        if (IN == kInF32Rms) scale = block_rms_scale(xsrc, K);
-        // two blocks per warp per step, both loads issued before either is used
-        for (int blk = warp; blk < NS; blk += 2 * kWarps) {
-            const int blk2 = blk + kWarps;
-            float v = xsrc[blk * 32 + lane];
-            float v2 = blk2 < NS ? xsrc[blk2 * 32 + lane] : 0.0f;
+        if (IN == kInF32Rms) {
+            // sum of squares in double (each square is exact), then 1/rms
+            double ss = 0.0;
+            for (int blk = tid; blk < NS; blk += nthreads) {
+                float v[32];
+                load_block32(a.x + blk * 32, vec, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) ss += (double)v[i] * (double)v[i];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) red_s[warp] = ss;
+            __syncthreads();
+            if (tid == 0) {
+                double t = 0.0;
+                for (int w2 = 0; w2 < nthreads / 32; ++w2) t += red_s[w2];
+                red_s[32] = (double)(float)(1.0 / sqrt(t / (double)K + 1e-6));
+            }
+            __syncthreads();
+            scale = (float)red_s[32];
+        }
+        for (int blk = tid; blk < NS; blk += nthreads) {
+            float v[32];
+            load_block32(a.x + blk * 32, vec, v);
             if (IN == kInF32Rms) {
-                v = __fmul_rn(v, scale);
-                v2 = __fmul_rn(v2, scale);
-                if (a.gamma) {
-                    v = __fmul_rn(v, a.gamma[blk * 32 + lane]);
-                    if (blk2 < NS) v2 = __fmul_rn(v2, a.gamma[blk2 * 32 + lane]);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    v[i] = __fmul_rn(v[i], scale);
+                    if (a.gamma) v[i] = __fmul_rn(v[i], a.gamma[blk * 32 + i]);
                 }
             }
-            quantize_block32(v, lane, xq_s + blk * 32, sx_s + blk, sq_s + blk);
-            if (blk2 < NS) quantize_block32(v2, lane, xq_s + blk2 * 32, sx_s + blk2, sq_s + blk2);
+            quantize_block_thread(v, xq_s + blk * 32, sx_s + blk, sq_s + blk);
         }
     }
     __syncthreads();
     pdl_launch_dependents();
 
     // ---- per-lane activation registers ------------------------------------
-    HalfBlockAct<GPL> act;
+    int xv[32];
+    double sxd[4], ad[4];
+    if (c < NH) {
+        const int4 *p = reinterpret_cast<const int4 *>(xq_s + 128 * c);
 #pragma unroll
-    for (int k = 0; k < GPL; ++k) {
-        const int c = tl + k * 32 * WR;
-        if (c < NH) {
-            const int4 *p = reinterpret_cast<const int4 *>(xq_s + 128 * c);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int4 v = p[j];
-                act.xv[k][4 * j + 0] = v.x;
-                act.xv[k][4 * j + 1] = v.y;
-                act.xv[k][4 * j + 2] = v.z;
-                act.xv[k][4 * j + 3] = v.w;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const double sxv = (double)sx_s[4 * c + j];
-                act.sxd[k][j] = sxv;
-                act.ad[k][j] = sxv * (double)sq_s[4 * c + j];
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) act.xv[k][j] = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) act.sxd[k][j] = act.ad[k][j] = 0.0;
+        for (int j = 0; j < 8; ++j) {
+            const int4 v = p[j];
+            xv[4 * j + 0] = v.x;
+            xv[4 * j + 1] = v.y;
+            xv[4 * j + 2] = v.z;
+            xv[4 * j + 3] = v.w;
         }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            sxd[j] = (double)sx_s[4 * c + j];
+            ad[j] = sxd[j] * (double)sq_s[4 * c + j];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) xv[j] = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sxd[j] = ad[j] = 0.0;
     }
 
-    // ---- main loop over stages ---------------------------------------------
-    int issued = min(nstages, nst);
-    for (int i = 0; i < nst; ++i) {
-        const int buf = i % nstages;
-        const uint32_t parity = (uint32_t)(i / nstages) & 1u;
-        const bool ok = mbar_wait_bounded(&bar[buf], parity, a.status);
-        const int row = r0 + i * RPS + team;
-        double acc = 0.0;
-        if (ok && row < r1) {
-            const uint8_t *rowp = stage_s + (size_t)buf * L.stage_bytes + team * row_bytes;
-            int32_t *isum_row = a.isum ? a.isum + (size_t)row * NS : nullptr;
+    // ---- main loop: this team's stages --------------------------------------
+    const int myrow = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);  // row held after the reduction
+    for (int it = 0; it < my_stages; ++it) {
+        const int s = team + it * T;
+        const int buf = team * kBufPerTeam + it % kBufPerTeam;
+        const bool ok = mbar_wait_bounded(&full[buf], (uint32_t)(it / kBufPerTeam) & 1u, a.status);
+        if (!ok) break;
+        const int rs = r0 + s * kR;
+        const uint8_t *sb = stage_s + (size_t)buf * L.stage_bytes;
+        double acc[kR];
 #pragma unroll
-            for (int k = 0; k < GPL; ++k) {
-                const int c = tl + k * 32 * WR;
-                if (c < NH)
-                    acc += q4k_half(rowp, c, act.xv[k], act.sxd[k], act.ad[k],
-                                    isum_row ? isum_row + 4 * c : nullptr);
+        for (int r = 0; r < kR; ++r) {
+            acc[r] = 0.0;
+            if (c < NH && rs + r < r1)
+                acc[r] = q4k_half(sb + r * row_bytes, c, xv, sxd, ad,
+                                  a.isum ? a.isum + (size_t)(rs + r) * NS + 4 * c : nullptr);
+        }
+        double v = warp_sum_rows4(acc, lane);
+        bool finisher = true;   // this warp completes the stage's rows
+        if (WR > 1) {
+            if ((lane & 7) == 0) red_s[(buf * WR + kw) * kR + myrow] = v;
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                last = atomicAdd(&rcnt_s[buf], 1) == WR - 1;
+            }
+            finisher = __shfl_sync(0xffffffffu, last, 0);
+            if (finisher) {
+                __threadfence_block();
+                double sum = 0.0;
+                for (int w2 = 0; w2 < WR; ++w2) sum += red_s[(buf * WR + w2) * kR + myrow];
+                v = sum;
+                if (lane == 0) rcnt_s[buf] = 0;
             }
         }
-        acc = warp_sum_d(acc);
-        if (WR == 1) {
-            if (lane == 0 && row < r1) {
-                const float v = (float)acc;
-                if (EPI == kEpiSwiglu) {
-                    tile_s[(((row - r0) >> 6) & 1) * 64 + ((row - r0) & 63)] = v;
-                } else {
-                    a.y[row] = EPI == kEpiResid ? __fadd_rn(a.resid[row], v) : v;
+        if (finisher) {
+            const int row = rs + myrow;
+            if (EPI == kEpiSwiglu) {
+                // 64-row tile t (32 gate + 32 up rows) of this CTA's range
+                const int lrow = s * kR;
+                const int t = lrow >> 6, jb = t % kTiles;
+                if (lane == 0) {
+                    for (uint32_t k = 0; ttag_s[jb] != t; ++k) {
+                        if (k > LALB_SPIN_LIMIT) {
+                            atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
+                            break;
+                        }
+                        __nanosleep(32);
+                    }
                 }
-            }
-        } else if (lane == 0) {
-            red_s[(i & 1) * kWarps + team * WR + wit] = acc;
-        }
-        const bool stop = __syncthreads_or(!ok);
-        if (stop) break;
-        if (tid == 0 && issued < nst) {
-            issue(issued);
-            ++issued;
-        }
-        if (WR > 1 && tid < RPS) {
-            const int rw = r0 + i * RPS + tid;
-            if (rw < r1) {
-                double s = 0.0;
-#pragma unroll
-                for (int w = 0; w < WR; ++w) s += red_s[(i & 1) * kWarps + tid * WR + w];
-                const float v = (float)s;
-                if (EPI == kEpiSwiglu) {
-                    tile_s[(((rw - r0) >> 6) & 1) * 64 + ((rw - r0) & 63)] = v;
-                } else {
-                    a.y[rw] = EPI == kEpiResid ? __fadd_rn(a.resid[rw], v) : v;
+                __syncwarp();
+                if ((lane & 7) == 0) tile_s[jb * 64 + (lrow & 63) + myrow] = (float)v;
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    last = atomicAdd(&tcnt_s[jb], kR) == 64 - kR;
                 }
-            }
-        }
-        if (EPI == kEpiSwiglu) {
-            // a 64-row tile (32 gate + 32 up rows) completes every 64/RPS stages
-            const int done_rows = (i + 1) * RPS;
-            if ((done_rows & 63) == 0) {
-                if (WR > 1) __syncthreads();   // the tile entries written above
-                const int tloc = (done_rows - 1) >> 6;
-                if (warp == kWarps - 1) {
-                    const float *tb = tile_s + (tloc & 1) * 64;
-                    const float av = silu_mul(tb[lane], tb[32 + lane]);
-                    const int gt = (r0 >> 6) + tloc;  // 32-element block of the product
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    __threadfence_block();
+                    const float av = silu_mul(tile_s[jb * 64 + lane], tile_s[jb * 64 + 32 + lane]);
+                    const int gt = (r0 >> 6) + t;  // 32-element block of the product
                     if (a.act_out) a.act_out[gt * 32 + lane] = av;
                     quantize_block32(av, lane, a.aq + gt * 32, a.asx + gt, a.asumq + gt);
+                    __syncwarp();
+                    if (lane == 0) {
+                        tcnt_s[jb] = 0;
+                        __threadfence_block();
+                        ttag_s[jb] = t + kTiles;
+                    }
                 }
+            } else if ((lane & 7) == 0 && row < r1) {
+                const float f = (float)v;
+                a.y[row] = EPI == kEpiResid ? __fadd_rn(a.resid[row], f) : f;
             }
+            // every warp of the team is done with this buffer: refill it
+            __syncwarp();
+            if (lane == 0 && it + kBufPerTeam < my_stages) issue(it + kBufPerTeam, policy);
         }
     }
-    // drain: every issued copy must land before the CTA's shared memory is
-    // released (returns at once after a normal run; bounded otherwise)
-    if (tid == 0) {
-        for (int i = max(0, issued - nstages); i < issued; ++i) {
-            const int buf = i % nstages;
-            mbar_wait_bounded(&bar[buf], (uint32_t)(i / nstages) & 1u, a.status);
+    // drain: a copy still in flight (only after an expired wait) must land
+    // before the CTA's shared memory is released
+    __syncthreads();
+    if (kw == 0 && lane == 0) {
+        const int n = issued_s[team];
+        for (int j = 0; j < kBufPerTeam && j < n; ++j) {
+            const int last_it = ((n - 1 - j) / kBufPerTeam) * kBufPerTeam + j;
+            mbar_wait_bounded(&full[team * kBufPerTeam + j], (uint32_t)(last_it / kBufPerTeam) & 1u,
+                              a.status);
         }
-        if (a.act_bulk) mbar_wait_bounded(act_bar, 0, a.status);
     }
-}
-
-struct Variant {
-    int wr, gpl;
-};
-
-// Lanes per row = 32*WR, each owning GPL half-blocks of 128 weights.
-Variant pick_variant(int NH) {
-    if (NH <= 32) return {1, 1};
-    if (NH <= 64) return {2, 1};
-    if (NH <= 128) return {4, 1};
-    if (NH <= 256) return {8, 1};
-    if (NH <= 512) return {8, 2};
-    return {0, 0};
+    if (tid == 0 && IN == kInQ8 && a.act_bulk) mbar_wait_bounded(act_bar, 0, a.status);
 }
 
 template <int IN, int EPI>
-void *kernel_ptr(int wr, int gpl) {
-    if (wr == 1) return (void *)q4k_gemv_kernel<1, 1, IN, EPI>;
-    if (wr == 2) return (void *)q4k_gemv_kernel<2, 1, IN, EPI>;
-    if (wr == 4) return (void *)q4k_gemv_kernel<4, 1, IN, EPI>;
-    if (wr == 8 && gpl == 1) return (void *)q4k_gemv_kernel<8, 1, IN, EPI>;
-    if (wr == 8 && gpl == 2) return (void *)q4k_gemv_kernel<8, 2, IN, EPI>;
-    return nullptr;
+void *kernel_ptr() {
+    return (void *)q4k_gemv_kernel<IN, EPI>;
 }
 
-void *select_kernel(int in, int epi, int wr, int gpl) {
+void *select_kernel(int in, int epi) {
 #define LALB_SEL(I, E) \
-    if (in == I && epi == E) return kernel_ptr<I, E>(wr, gpl);
+    if (in == I && epi == E) return kernel_ptr<I, E>();
     LALB_SEL(kInF32, kEpiStore)
     LALB_SEL(kInF32Rms, kEpiStore)
     LALB_SEL(kInQ8, kEpiStore)
@@ -429,43 +502,38 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int 
         return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: W must be 16-byte aligned");
     if (a.unit <= 0 || a.rows % a.unit)
         return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: rows %% unit != 0");
-    const Variant v = pick_variant(a.K / 128);
-    if (!v.wr) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d > 65536", a.K);
+    const int NH = a.K / 128;
+    const int wr = (NH + 31) / 32;
+    if (wr > kMaxThreads / 32)
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d > 65536", a.K);
+    if (epi == kEpiSwiglu && (wr != 1 || a.unit % 64))
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: SwiGLU epilogue needs K <= 4096");
     if (in == kInQ8 && (reinterpret_cast<uintptr_t>(a.xq) & 15))
         return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: xq must be 16-byte aligned");
-    void *fn = select_kernel(in, epi, v.wr, v.gpl);
+    void *fn = select_kernel(in, epi);
     if (!fn) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: no variant in=%d epi=%d", in, epi);
-
-    // activations arrive by bulk copy when aligned (and, for fp32, small
-    // enough to stage in shared memory)
     const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    if (in == kInQ8)
-        a.act_bulk = al16(a.xq) && al16(a.sx) && al16(a.sumq);
-    else
-        a.act_bulk = a.K <= kMaxStagedK && al16(a.x);
-    const int xf = (in != kInQ8 && a.act_bulk) ? a.K : 0;
+    a.act_bulk = in == kInQ8 ? (al16(a.xq) && al16(a.sx) && al16(a.sumq)) : al16(a.x);
 
-    // pipeline depth: fill the per-CTA shared-memory budget
+    // teams: as many as fit the thread, register and shared-memory budget
     const size_t budget = ctas_per_sm >= 2 ? 110 * 1024 : ctx->smem_optin - 1024;
-    const Layout base = make_layout(a.K, v.wr, 0, xf);
-    int nst = (int)((budget - base.off_stage) / base.stage_bytes);
-    if (nst > 12) nst = 12;
-    if (nst < 2) {
-        nst = (int)((ctx->smem_optin - 1024 - base.off_stage) / base.stage_bytes);
-        ctas_per_sm = 1;
-        if (nst < 2) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d too large for smem", a.K);
-        if (nst > 12) nst = 12;
-    }
-    a.nstages = nst;
+    int teams = std::max(1, std::min(12 / wr, kMaxThreads / (32 * wr)));
+    while (teams > 1 && make_layout(a.K, wr, teams).total > budget) --teams;
+    Layout L = make_layout(a.K, wr, teams);
+    if (L.total > ctx->smem_optin - 1024)
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d too large for smem", a.K);
+    a.wr = wr;
+    a.teams = teams;
+    a.nstages = L.nstages;
     a.status = &ctx->scratch->status;
-    const Layout L = make_layout(a.K, v.wr, nst, xf);
     {
         const int st = lalb_set_smem_attr(ctx, fn, (int)L.total);
         if (st) return st;
     }
+    const int threads = 32 * wr * teams;
     int resident = 0;
     LALB_CUDA_TRY(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, (const void *)fn,
-                                                                     kThreads, L.total));
+                                                                     threads, L.total));
     if (resident < 1) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: CTA does not fit");
     if (ctas_per_sm > resident) ctas_per_sm = resident;
     const int nunits = a.rows / a.unit;
@@ -474,7 +542,7 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int 
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
