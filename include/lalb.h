@@ -108,7 +108,7 @@ LALB_API int lalb_quantize_act(lalb_ctx *ctx, const float *x, int M, int K,
  * y[r] = sum_j sx_j * (d*sc_j*isum_j - dmin*m_j*sumq_j) over the 32-wide
  * sub-blocks j of row r, isum_j = the exact int32 dot of the 32 4-bit quants
  * with the 32 int8 activations.  The activation quantizer is fused: x is
- * fp32 [K].  W must be 16-byte aligned; K % 256 == 0, K <= 65536.
+ * fp32 [K].  W must be 16-byte aligned; K % 256 == 0, K <= 32768.
  * Replaces lal_matmul_q4_k (runtime/lal_q4k_kernel.h, README.md:130,210). */
 LALB_API int lalb_matmul_q4_k(lalb_ctx *ctx, const void *W, int rows, int K,
                               const float *x, float *y, lalb_stream stream);

@@ -47,6 +47,7 @@ constexpr int kR = 4;            // rows per stage
 constexpr int kBufPerTeam = 2;   // stage buffers owned by each team
 constexpr int kTiles = 4;        // SwiGLU tile ring
 constexpr int kMaxThreads = 512;
+constexpr int kMaxK = 32768;     // two 4-row stages of this K fill one SM's shared memory
 
 struct Layout {
     uint32_t off_xq, off_sx, off_sq, off_red, off_rcnt, off_issued, off_tile, off_tcnt, off_ttag;
@@ -504,8 +505,8 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int 
         return lalb_fail(ctx, LALB_ERR_INVALID, "q4k gemv: rows %% unit != 0");
     const int NH = a.K / 128;
     const int wr = (NH + 31) / 32;
-    if (wr > kMaxThreads / 32)
-        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d > 65536", a.K);
+    if (a.K > kMaxK)
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: K=%d > %d", a.K, kMaxK);
     if (epi == kEpiSwiglu && (wr != 1 || a.unit % 64))
         return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: SwiGLU epilogue needs K <= 4096");
     if (in == kInQ8 && (reinterpret_cast<uintptr_t>(a.xq) & 15))

@@ -81,7 +81,7 @@ def q4k_case(rows, K, seed):
     (18944, 3584),   # single GEMV of the q4k unit-test shape (gate/up rows)
     (3584, 18944),   # down projection shape (K split over 4 warps per row)
     (512, 3584),     # k / v projection
-    (1, 256), (7, 512), (13, 768), (100, 8192), (5, 65536),
+    (1, 256), (7, 512), (13, 768), (100, 8192), (3, 4352), (5, 32768),
 ])
 def test_q4k_gemv_parity(ctx, rows, K):
     W, x = q4k_case(rows, K, seed=rows * 7 + K)
@@ -110,7 +110,7 @@ def test_q4k_gemv_rejects_bad_arguments(ctx):
         ctx.matmul_q4_k(W, x, 4, 500)              # K not a multiple of 256
     assert e.value.status == -1
     with pytest.raises(lb.LalbError) as e:
-        ctx.matmul_q4_k(W, x, 1, 65536 + 256)      # beyond the register plan
+        ctx.matmul_q4_k(W, x, 1, 32768 + 256)      # beyond the shared-memory plan
     assert e.value.status == -4
 
 
