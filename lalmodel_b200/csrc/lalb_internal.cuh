@@ -53,11 +53,12 @@ int lalb_cuda_fail(lalb_ctx *ctx, cudaError_t e, const char *what);
 // status word bits
 #define LALB_STATUS_WAIT_TIMEOUT 1u
 
-// Spin limit for every mbarrier wait: far above any legitimate wait (a
-// 64 KiB bulk copy lands in microseconds), small enough that a wait which
-// can never complete gives up within about a second (each try_wait may
-// suspend the thread for a short, hardware-defined interval).
-#define LALB_SPIN_LIMIT (1u << 20)
+// Bound on every wait: LALB_SPIN_LIMIT tries.  An mbarrier try_wait sleeps
+// until the phase completes or LALB_WAIT_HINT_NS passes, so a wait that can
+// never complete gives up after at most ~0.4 s, and a waiting warp does not
+// spin on the issue slots that the working warps need.
+#define LALB_SPIN_LIMIT (1u << 14)
+#define LALB_WAIT_HINT_NS 25000u
 
 namespace lalb {
 
@@ -90,10 +91,10 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t *bar,
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(LALB_WAIT_HINT_NS)
         : "memory");
     return ok;
 }

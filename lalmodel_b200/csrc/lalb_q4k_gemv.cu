@@ -108,18 +108,21 @@ __device__ __forceinline__ void quantize_block32(float v, int lane, int8_t *xq32
     }
 }
 
-// Quantizes one 32-block held entirely by one thread (same operations).
-__device__ __forceinline__ void quantize_block_thread(const float (&v)[32], int8_t *xq32,
-                                                      float *sx, int *sumq) {
+// Quantizes one 32-block held by a quad of lanes (8 elements each, quad
+// lane qi owns elements 8qi..8qi+7).  Same operations as the restatement.
+__device__ __forceinline__ void quantize_block_quad(const float (&v)[8], int qi, bool store,
+                                                    int8_t *xq32, float *sx, int *sumq) {
     uint32_t amax = 0;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) amax = max(amax, __float_as_uint(fabsf(v[i])));
+    for (int i = 0; i < 8; ++i) amax = max(amax, __float_as_uint(fabsf(v[i])));
+    amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
     const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
     int s = 0;
-    uint32_t packed[8];
+    uint32_t packed[2];
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
+    for (int w = 0; w < 2; ++w) {
         uint32_t word = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -130,27 +133,25 @@ __device__ __forceinline__ void quantize_block_thread(const float (&v)[32], int8
         }
         packed[w] = word;
     }
-    int4 *dst = reinterpret_cast<int4 *>(xq32);
-    dst[0] = make_int4((int)packed[0], (int)packed[1], (int)packed[2], (int)packed[3]);
-    dst[1] = make_int4((int)packed[4], (int)packed[5], (int)packed[6], (int)packed[7]);
-    *sx = dsc;
-    *sumq = s;
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (!store) return;
+    *reinterpret_cast<uint2 *>(xq32 + 8 * qi) = make_uint2(packed[0], packed[1]);
+    if (qi == 0) {
+        *sx = dsc;
+        *sumq = s;
+    }
 }
 
-__device__ __forceinline__ void load_block32(const float *x, bool vec, float (&v)[32]) {
+__device__ __forceinline__ void load8(const float *x, bool vec, float (&v)[8]) {
     if (vec) {
-        const float4 *p = reinterpret_cast<const float4 *>(x);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 f = p[i];
-            v[4 * i] = f.x;
-            v[4 * i + 1] = f.y;
-            v[4 * i + 2] = f.z;
-            v[4 * i + 3] = f.w;
-        }
+        const float4 a = reinterpret_cast<const float4 *>(x)[0];
+        const float4 b = reinterpret_cast<const float4 *>(x)[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = x[i];
+        for (int i = 0; i < 8; ++i) v[i] = x[i];
     }
 }
 
@@ -314,39 +315,53 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
         }
     } else {
         const bool vec = a.act_bulk;  // x is 16-byte aligned
+        // a quad of lanes per 32-block; whole warps per pass so the quad
+        // shuffles always have all lanes present
+        const int nquads = ((nthreads >> 5) << 5) >> 2;
         float scale = 1.0f;
         if (IN == kInF32Rms) {
             // sum of squares in double (each square is exact), then 1/rms
             double ss = 0.0;
-            for (int blk = tid; blk < NS; blk += nthreads) {
-                float v[32];
-                load_block32(a.x + blk * 32, vec, v);
+            for (int e = tid * 8; e < K; e += nthreads * 8) {
+                float v[8];
+                load8(a.x + e, vec, v);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) ss += (double)v[i] * (double)v[i];
+                for (int i = 0; i < 8; ++i) ss += (double)v[i] * (double)v[i];
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             if (lane == 0) red_s[warp] = ss;
             __syncthreads();
-            if (tid == 0) {
-                double t = 0.0;
-                for (int w2 = 0; w2 < nthreads / 32; ++w2) t += red_s[w2];
-                red_s[32] = (double)(float)(1.0 / sqrt(t / (double)K + 1e-6));
+            if (warp == 0) {
+                double t = lane < (nthreads >> 5) ? red_s[lane] : 0.0;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+                if (lane == 0) red_s[32] = (double)(float)(1.0 / sqrt(t / (double)K + 1e-6));
             }
             __syncthreads();
             scale = (float)red_s[32];
         }
-        for (int blk = tid; blk < NS; blk += nthreads) {
-            float v[32];
-            load_block32(a.x + blk * 32, vec, v);
-            if (IN == kInF32Rms) {
+        const int quad = tid >> 2, qi = tid & 3;
+        for (int blk0 = 0; blk0 < NS; blk0 += nquads) {
+            const int blk = blk0 + quad;
+            const bool have = blk < NS;
+            float v[8];
+            if (have) {
+                load8(a.x + blk * 32 + 8 * qi, vec, v);
+                if (IN == kInF32Rms) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    v[i] = __fmul_rn(v[i], scale);
-                    if (a.gamma) v[i] = __fmul_rn(v[i], a.gamma[blk * 32 + i]);
+                    for (int i = 0; i < 8; ++i) {
+                        v[i] = __fmul_rn(v[i], scale);
+                        if (a.gamma) v[i] = __fmul_rn(v[i], a.gamma[blk * 32 + 8 * qi + i]);
+                    }
                 }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = 0.0f;
             }
-            quantize_block_thread(v, xq_s + blk * 32, sx_s + blk, sq_s + blk);
+            // whole warps take part (the quad shuffles need every lane)
+            if (blk0 + (tid & ~31) / 4 < NS)
+                quantize_block_quad(v, qi, have, xq_s + blk * 32, sx_s + blk, sq_s + blk);
         }
     }
     __syncthreads();
