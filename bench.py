@@ -145,7 +145,8 @@ def build_decoder(ctx, lb, torch, c, seed):
     ctx.fill_normal(w, seed=seed + 9999, sigma=0.02)
     lm_q, lm_s = ctx.q8_quantize_rows(w)
     torch.cuda.synchronize()
-    del tmp
+    del tmp, w
+    torch.cuda.empty_cache()   # the fp32 staging buffer is not needed any more
     dec = lb.Decoder(ctx, **c)
     for l, m in enumerate(layers):
         dec.set_layer(l, *m)
@@ -438,12 +439,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--n-layer", type=int, default=CFG["n_layer"],
                     help="fewer layers: only for profiling captures, not a bench line")
+    ap.add_argument("--vocab", type=int, default=CFG["vocab"],
+                    help="smaller LM head: only for profiling captures, not a bench line")
     ap.add_argument("--case", default="decode", choices=["decode", "gemv"],
                     help="gemv: only the single 18944x3584 GEMV, for profiler captures")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     CFG["n_layer"] = args.n_layer
+    CFG["vocab"] = args.vocab
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
