@@ -64,14 +64,14 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic():
-    """dram bytes per launch of the Q4_K matvec from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "q4k_gemv_decode7b_ncu.md")
+def profile_traffic(name, key):
+    """A dram-bytes figure (`key: value` line) from a committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith(key + ":"):
                 return float(line.split(":")[1])
-    except OSError:
+    except (OSError, ValueError):
         pass
     return None
 
@@ -220,6 +220,9 @@ def run_gpu(args, rank, world, local_rank):
     ctx.fill_normal(h_in, seed=77 + rank, sigma=1.0)
     am = torch.empty(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.Stream()
+    dec.set_path({"auto": lb.Decoder.AUTO, "kernels": lb.Decoder.KERNELS,
+                  "persistent": lb.Decoder.PERSISTENT}[args.path])
+    persistent = dec.path() == lb.Decoder.PERSISTENT
     launches = dec.launches_per_step()
 
     with torch.cuda.stream(stream):
@@ -251,20 +254,60 @@ def run_gpu(args, rank, world, local_rank):
     ms_per_step = ms_max / args.steps
     value = world * args.steps / (ms_max / 1000.0)
 
-    # per-kernel durations of one token (events between kernels, no overlap)
     per_layer_b, head_b = algorithmic_bytes(c)
-    with torch.cuda.stream(stream):
-        prof = np.median(np.array([dec.profile_step(h_in) for _ in range(5)]), axis=0)
     q4k_launches = 4 * c["n_layer"]
-    q4k_us = float(sum(prof[:q4k_launches]))
     q4k_bytes_tok = c["n_layer"] * sum(per_layer_b)
+    tok_bytes = q4k_bytes_tok + head_b
     peak, peak_kind = measured_peak()
-    achieved = q4k_bytes_tok / (q4k_us * 1e-6) / 1e9
+
+    # The per-phase kernel chain (one launch per matvec) on the same weights:
+    # its step rate, and each kernel's duration from events between kernels.
+    dec.set_path(lb.Decoder.KERNELS)
+    n_chain = max(20, min(args.steps, 300))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            dec.step(h_in, None, None, am)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(n_chain):
+            dec.step(h_in, None, None, am)
+        g1.record(stream)
+        prof = np.median(np.array([dec.profile_step(h_in) for _ in range(5)]), axis=0)
+    torch.cuda.synchronize()
+    chain_ms = g0.elapsed_time(g1) / n_chain
+    dec.set_path({"auto": lb.Decoder.AUTO, "kernels": lb.Decoder.KERNELS,
+                  "persistent": lb.Decoder.PERSISTENT}[args.path])
+    q4k_us = float(sum(prof[:q4k_launches]))
     head_us = float(prof[-1])
     kinds = ["qkv", "o", "gate_up", "down"]
     per_kind = {k: round(float(np.mean(prof[i:q4k_launches:4])), 2) for i, k in enumerate(kinds)}
     per_kind_gbs = {k: round(per_layer_b[i] / (per_kind[k] * 1e-6) / 1e9, 1)
                     for i, k in enumerate(kinds)}
+    chain = {"tok_s": round(1000.0 / chain_ms, 2), "ms_per_step": round(chain_ms, 5),
+             "launches_per_step": q4k_launches + 1,
+             "q4k_gbs": round(q4k_bytes_tok / (q4k_us * 1e-6) / 1e9, 1),
+             "us_by_kind": per_kind, "gbs_by_kind": per_kind_gbs,
+             "lm_head_us": round(head_us, 2),
+             "lm_head_gbs": round(head_b / (head_us * 1e-6) / 1e9, 1)}
+    if persistent:
+        # one launch per token: its duration is the step time measured above
+        achieved = tok_bytes / (ms_per_step * 1e-3) / 1e9
+        roofline = {"kernel": "decode_persistent_kernel (the whole token, one launch)",
+                    "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                    "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "traffic": profile_traffic("decode_persistent_qwen7b_ncu.md",
+                                               "traffic_bytes_per_launch"),
+                    "bytes_per_launch": tok_bytes, "us_per_launch": round(ms_per_step * 1e3, 2)}
+    else:
+        achieved = q4k_bytes_tok / (q4k_us * 1e-6) / 1e9
+        roofline = {"kernel": "q4k_gemv (the %d Q4_K matvec launches of a token)" % q4k_launches,
+                    "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                    "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "traffic": profile_traffic("q4k_gemv_decode7b_ncu.md",
+                                               "traffic_bytes_per_launch"),
+                    "bytes_per_launch_avg": q4k_bytes_tok / q4k_launches,
+                    "us_per_launch_avg": round(q4k_us / q4k_launches, 3)}
+    roofline["step_gbs"] = round(tok_bytes / (ms_per_step * 1e-3) / 1e9, 1)
 
     # end to end through the host-buffer entry point (H2D input, D2H argmax)
     pinned = h_in.cpu().pin_memory()
@@ -299,19 +342,12 @@ def run_gpu(args, rank, world, local_rank):
             "config": {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": world,
                        "seq_len": 1,
                        "parallelism": "replicas%d" % world if world > 1 else "single",
+                       "path": "persistent" if persistent else "kernels",
                        "l2": "inputs larger than L2: %.2f GB of weights streamed per step"
-                             % ((q4k_bytes_tok + head_b) / 1e9),
-                       "bytes_per_step": q4k_bytes_tok + head_b},
-            "roofline": {"kernel": "q4k_gemv (the %d Q4_K matvec launches of a token)" % q4k_launches,
-                         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
-                         "bytes_per_launch_avg": q4k_bytes_tok / q4k_launches,
-                         "us_per_launch_avg": round(q4k_us / q4k_launches, 3),
-                         "us_by_kind": per_kind, "gbs_by_kind": per_kind_gbs,
-                         "lm_head_us": round(head_us, 2),
-                         "lm_head_gbs": round(head_b / (head_us * 1e-6) / 1e9, 1),
-                         "step_gbs": round((q4k_bytes_tok + head_b) / (ms_per_step * 1e-3) / 1e9, 1)},
+                             % (tok_bytes / 1e9),
+                       "bytes_per_step": tok_bytes},
+            "roofline": roofline,
+            "phase_chain": chain,
             "gemv": gemv and {**gemv, "frac": round(gemv["gbs"] / peak, 4)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
@@ -441,6 +477,8 @@ def main():
                     help="fewer layers: only for profiling captures, not a bench line")
     ap.add_argument("--vocab", type=int, default=CFG["vocab"],
                     help="smaller LM head: only for profiling captures, not a bench line")
+    ap.add_argument("--path", default="auto", choices=["auto", "kernels", "persistent"],
+                    help="decoder path: one persistent kernel per token, or one kernel per matvec")
     ap.add_argument("--case", default="decode", choices=["decode", "gemv"],
                     help="gemv: only the single 18944x3584 GEMV, for profiler captures")
     args = ap.parse_args()

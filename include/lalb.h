@@ -214,12 +214,40 @@ LALB_API int lalb_decoder_step(lalb_decoder *dec, const float *h_in, float *h_ou
  * for the stream. */
 LALB_API int lalb_decoder_step_host(lalb_decoder *dec, const float *h_in_host,
                                     int32_t *argmax_host, lalb_stream stream);
-/* One token with a CUDA event between consecutive kernels (no graph, no
- * programmatic overlap): kernel_us (host, lalb_decoder_launches_per_step
- * floats) receives each kernel's duration in launch order -- per layer
- * qkv, o, gate/up, down; then the LM head.  Synchronises the stream. */
+/* One token on the per-phase kernel chain with a CUDA event between
+ * consecutive kernels (no programmatic overlap): kernel_us (host,
+ * 4*n_layer + 1 floats) receives each kernel's duration in launch order --
+ * per layer qkv, o, gate/up, down; then the LM head.  Synchronises the
+ * stream. */
 LALB_API int lalb_decoder_profile_step(lalb_decoder *dec, const float *h_in,
                                        float *kernel_us, lalb_stream stream);
+/* One token on the persistent path with a phase timeline: trace_host
+ * (host, trace_len >= n_cta * (4*n_layer + 1) * 8 values) receives, for
+ * each CTA and phase, six GPU global-timer figures (ns): [0] the CTA
+ * finished the phase's work, [1] it left the grid barrier that ends the
+ * phase, [2] its activation prologue was done, [3] the time its first
+ * consumer warp waited for weights in the phase and [4] the time it spent
+ * computing, [5] its producer had issued the phase's last copy; then two
+ * counts: [6] the producer's and [7] the first consumer's mbarrier polls.
+ * *n_cta is the number of CTAs (one per SM).  Synchronises the stream. */
+LALB_API int lalb_decoder_trace_step(lalb_decoder *dec, const float *h_in,
+                                     unsigned long long *trace_host, int trace_len,
+                                     int *n_cta, lalb_stream stream);
+/* Execution path of lalb_decoder_step.  AUTO takes the persistent path
+ * (the whole token in one cooperative kernel, one CTA per SM) when the
+ * shapes fit it -- hidden <= 4096, q_rows <= 4096, ffn <= 20480, at most
+ * 8 gate/up tiles of 64 rows per SM -- and the per-phase kernel chain
+ * otherwise.  PERSISTENT fails with LALB_ERR_UNSUPPORTED when the shapes
+ * do not fit. */
+enum {
+    LALB_DECODE_AUTO = 0,
+    LALB_DECODE_KERNELS = 1,
+    LALB_DECODE_PERSISTENT = 2
+};
+LALB_API int lalb_decoder_set_path(lalb_decoder *dec, int path);
+/* The path lalb_decoder_step takes: LALB_DECODE_KERNELS or
+ * LALB_DECODE_PERSISTENT. */
+LALB_API int lalb_decoder_path(const lalb_decoder *dec);
 /* Number of kernels one step launches. */
 LALB_API int lalb_decoder_launches_per_step(const lalb_decoder *dec);
 LALB_API int lalb_decoder_destroy(lalb_decoder *dec);

@@ -172,11 +172,38 @@ class Decoder:
         return out.value
 
     def profile_step(self, h_in):
-        """Per-kernel durations (microseconds) of one token, in launch order."""
-        n = self.launches_per_step()
+        """Per-kernel durations (microseconds) of one token on the per-phase
+        kernel chain, in launch order (4*n_layer + 1 values)."""
+        n = 4 * self.cfg.n_layer + 1
         buf = (ctypes.c_float * n)()
         self.ctx._call("lalb_decoder_profile_step", self.h, _p(h_in), buf, _stream())
         return list(buf)
+
+    def trace_step(self, h_in, max_cta=1024):
+        """Phase timeline of one persistent-path token: an int64 array
+        [n_cta, 4*n_layer + 1, 8] per CTA and phase: GPU global-timer ns
+        (work done, barrier left, prologue done, consumer-0 wait, consumer-0
+        compute, producer done issuing), then the producer's and consumer 0's
+        mbarrier polls."""
+        import numpy as np
+        n_phase = 4 * self.cfg.n_layer + 1
+        n = max_cta * n_phase * 8
+        buf = (ctypes.c_ulonglong * n)()
+        n_cta = ctypes.c_int(0)
+        self.ctx._call("lalb_decoder_trace_step", self.h, _p(h_in), buf, n, ctypes.byref(n_cta),
+                       _stream())
+        arr = np.frombuffer(buf, dtype=np.uint64, count=n_cta.value * n_phase * 8)
+        return arr.reshape(n_cta.value, n_phase, 8).astype(np.int64)
+
+    AUTO, KERNELS, PERSISTENT = 0, 1, 2
+
+    def set_path(self, path):
+        """AUTO (persistent kernel when the shapes fit), KERNELS or PERSISTENT."""
+        self.ctx._call("lalb_decoder_set_path", self.h, path)
+
+    def path(self):
+        """The path step() takes: Decoder.KERNELS or Decoder.PERSISTENT."""
+        return _abi.lib().lalb_decoder_path(self.h)
 
     def launches_per_step(self):
         return _abi.lib().lalb_decoder_launches_per_step(self.h)

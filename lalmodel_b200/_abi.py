@@ -51,6 +51,9 @@ SIGNATURES = {
     "lalb_decoder_step": (c_int, [P, P, P, P, P, P]),
     "lalb_decoder_step_host": (c_int, [P, P, P, P]),
     "lalb_decoder_profile_step": (c_int, [P, P, P, P]),
+    "lalb_decoder_trace_step": (c_int, [P, P, P, c_int, P, P]),
+    "lalb_decoder_set_path": (c_int, [P, c_int]),
+    "lalb_decoder_path": (c_int, [P]),
     "lalb_decoder_launches_per_step": (c_int, [P]),
     "lalb_decoder_destroy": (c_int, [P]),
 }

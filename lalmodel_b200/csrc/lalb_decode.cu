@@ -29,6 +29,13 @@ struct lalb_decoder {
     float *h_in_dev = nullptr;
     int32_t *argmax_dev = nullptr;
     int32_t *argmax_host = nullptr;  // pinned
+    // persistent path
+    lalb_layer_weights *layers_dev = nullptr;  // [n_layer]
+    unsigned int *pctr = nullptr;              // grid-barrier counters [4*n_layer], ticket
+    unsigned long long *pbest = nullptr;       // argmax key
+    bool layers_dirty = true;
+    bool persist_fits = false;
+    int path = LALB_DECODE_AUTO;
     bool use_graph = true;
     std::map<std::tuple<const void *, void *, void *, void *, void *>, cudaGraphExec_t> graphs;
 };
@@ -126,6 +133,60 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
     return LALB_OK;
 }
 
+bool use_persistent(const lalb_decoder *d) {
+    return d->persist_fits && d->path != LALB_DECODE_KERNELS;
+}
+
+// The same token as launch_token, as one cooperative kernel.
+int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, float *logits,
+                            int32_t *argmax, cudaStream_t s,
+                            unsigned long long *trace = nullptr) {
+    lalb_ctx *ctx = d->ctx;
+    const lalb_decoder_cfg &c = d->cfg;
+    if (d->layers_dirty) {
+        if (c.n_layer > 0)
+            LALB_CUDA_TRY(ctx, cudaMemcpyAsync(d->layers_dev, d->layers.data(),
+                                               sizeof(lalb_layer_weights) * c.n_layer,
+                                               cudaMemcpyHostToDevice, s));
+        LALB_CUDA_TRY(ctx, cudaStreamSynchronize(s));  // the host vector may change after
+        d->layers_dirty = false;
+    }
+    PersistArgs a = {};
+    a.n_layer = c.n_layer;
+    a.hidden = c.hidden;
+    a.q_rows = c.q_rows;
+    a.kv_rows = c.kv_rows;
+    a.ffn = c.ffn;
+    a.vocab = c.vocab;
+    a.layers = d->layers_dev;
+    a.lm_w = d->lm_w;
+    a.lm_s = d->lm_s;
+    a.h_in = h_in;
+    a.h = d->h_res;
+    a.qkv = d->qkv;
+    a.aq = d->aq;
+    a.asx = d->asx;
+    a.asumq = d->asumq;
+    a.logits = logits;
+    a.argmax = argmax;
+    a.gbar = d->pctr;
+    a.ticket = d->pctr + 4 * c.n_layer;
+    a.best = d->pbest;
+    a.status = &ctx->scratch->status;
+    a.trace = trace;
+    if (int st = lalb_launch_persist(ctx, a, s)) return st;
+    if (h_out)
+        LALB_CUDA_TRY(ctx, cudaMemcpyAsync(h_out, c.n_layer > 0 ? d->h_res : h_in,
+                                           sizeof(float) * c.hidden, cudaMemcpyDeviceToDevice, s));
+    return LALB_OK;
+}
+
+int enqueue_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits,
+                  int32_t *argmax, cudaStream_t s) {
+    return use_persistent(d) ? launch_token_persistent(d, h_in, h_out, logits, argmax, s)
+                             : launch_token(d, h_in, h_out, logits, argmax, s);
+}
+
 void drop_graphs(lalb_decoder *d) {
     for (auto &kv : d->graphs) cudaGraphExecDestroy(kv.second);
     d->graphs.clear();
@@ -141,6 +202,9 @@ void free_decoder(lalb_decoder *d) {
     cudaFree(d->h_in_dev);
     cudaFree(d->argmax_dev);
     cudaFreeHost(d->argmax_host);
+    cudaFree(d->layers_dev);
+    cudaFree(d->pctr);
+    cudaFree(d->pbest);
     delete d;
 }
 
@@ -169,12 +233,28 @@ extern "C" int lalb_decoder_create(lalb_ctx *ctx, const lalb_decoder_cfg *cfg,
               cudaMalloc(&d->asumq, sizeof(int32_t) * (c.ffn / 32)) == cudaSuccess &&
               cudaMalloc(&d->h_in_dev, sizeof(float) * c.hidden) == cudaSuccess &&
               cudaMalloc(&d->argmax_dev, sizeof(int32_t)) == cudaSuccess &&
-              cudaMallocHost(&d->argmax_host, sizeof(int32_t)) == cudaSuccess;
+              cudaMallocHost(&d->argmax_host, sizeof(int32_t)) == cudaSuccess &&
+              cudaMalloc(&d->layers_dev, sizeof(lalb_layer_weights) * (c.n_layer + 1)) ==
+                  cudaSuccess &&
+              cudaMalloc(&d->pctr, sizeof(unsigned int) * (4 * c.n_layer + 1)) == cudaSuccess &&
+              cudaMalloc(&d->pbest, sizeof(unsigned long long)) == cudaSuccess &&
+              cudaMemset(d->pctr, 0, sizeof(unsigned int) * (4 * c.n_layer + 1)) == cudaSuccess &&
+              cudaMemset(d->pbest, 0, sizeof(unsigned long long)) == cudaSuccess &&
+              cudaDeviceSynchronize() == cudaSuccess;
     if (!ok) {
         cudaGetLastError();
         free_decoder(d);
         return lalb_fail(ctx, LALB_ERR_NOMEM, "decoder_create: activation buffers");
     }
+    // the persistent kernel's limits: activations in shared memory, gate/up
+    // tiles per CTA, one resident CTA per SM for the grid barriers
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device);
+    const long long gu_units = 2LL * c.ffn / 64;
+    d->persist_fits = coop && c.hidden <= kPersistMaxHidden && c.q_rows <= kPersistMaxHidden &&
+                      c.ffn <= kPersistMaxFfn && c.ffn % 32 == 0 &&
+                      (gu_units + ctx->sm_count - 1) / ctx->sm_count <= lalb_persist_max_tiles() &&
+                      (size_t)lalb_persist_smem_bytes() <= ctx->smem_optin;
     *out = d;
     return LALB_OK;
 }
@@ -183,7 +263,11 @@ extern "C" int lalb_decoder_set_layer(lalb_decoder *d, int layer, const lalb_lay
     if (!d) return LALB_ERR_INVALID;
     if (!w || layer < 0 || layer >= d->cfg.n_layer || !w->wqkv || !w->wo || !w->wgu || !w->wdown)
         return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_layer: bad layer %d", layer);
+    if (((uintptr_t)w->wqkv | (uintptr_t)w->wo | (uintptr_t)w->wgu | (uintptr_t)w->wdown) & 15u)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID,
+                         "decoder_set_layer: weights must be 16-byte aligned");
     d->layers[layer] = *w;
+    d->layers_dirty = true;
     drop_graphs(d);
     return LALB_OK;
 }
@@ -191,6 +275,8 @@ extern "C" int lalb_decoder_set_layer(lalb_decoder *d, int layer, const lalb_lay
 extern "C" int lalb_decoder_set_lm_head(lalb_decoder *d, const int8_t *w, const float *sw) {
     if (!d) return LALB_ERR_INVALID;
     if (!w || !sw) return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: null");
+    if (((uintptr_t)w & 15u) || ((uintptr_t)sw & 3u))
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: misaligned");
     d->lm_w = w;
     d->lm_s = sw;
     drop_graphs(d);
@@ -214,8 +300,11 @@ extern "C" int lalb_decoder_step(lalb_decoder *d, const float *h_in, float *h_ou
     cudaStream_t s = (cudaStream_t)stream;
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     if (s) LALB_CUDA_TRY(ctx, cudaStreamIsCapturing(s, &cap));
+    if (d->layers_dirty && cap != cudaStreamCaptureStatusNone && use_persistent(d))
+        return lalb_fail(ctx, LALB_ERR_INVALID,
+                         "decoder_step: run one step outside stream capture after set_layer");
     if (!d->use_graph || !s || cap != cudaStreamCaptureStatusNone)
-        return launch_token(d, h_in, h_out, logits, argmax, s);
+        return enqueue_token(d, h_in, h_out, logits, argmax, s);
 
     auto key = std::make_tuple((const void *)h_in, (void *)h_out, (void *)logits, (void *)argmax,
                                (void *)s);
@@ -223,11 +312,11 @@ extern "C" int lalb_decoder_step(lalb_decoder *d, const float *h_in, float *h_ou
     if (it == d->graphs.end()) {
         // first use of this pointer set: launch once directly (sets kernel
         // attributes outside capture), then capture the token into a graph
-        int st = launch_token(d, h_in, h_out, logits, argmax, s);
+        int st = enqueue_token(d, h_in, h_out, logits, argmax, s);
         if (st) return st;
         cudaGraph_t g = nullptr;
         LALB_CUDA_TRY(ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-        st = launch_token(d, h_in, h_out, logits, argmax, s);
+        st = enqueue_token(d, h_in, h_out, logits, argmax, s);
         cudaError_t e = cudaStreamEndCapture(s, &g);
         if (st) {
             if (g) cudaGraphDestroy(g);
@@ -314,9 +403,52 @@ extern "C" int lalb_decoder_profile_step(lalb_decoder *d, const float *h_in, flo
     return st;
 }
 
+extern "C" int lalb_decoder_trace_step(lalb_decoder *d, const float *h_in,
+                                       unsigned long long *trace_host, int trace_len,
+                                       int *n_cta, lalb_stream stream) {
+    if (!d) return LALB_ERR_INVALID;
+    lalb_ctx *ctx = d->ctx;
+    if (!h_in || !trace_host || !n_cta)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_trace_step: null argument");
+    if (int st = check_ready(d)) return st;
+    if (!use_persistent(d))
+        return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_trace_step: needs the persistent path");
+    const size_t n = (size_t)ctx->sm_count * (4 * d->cfg.n_layer + 1) * 8;
+    if ((size_t)trace_len < n)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_trace_step: trace_len < %zu", n);
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned long long *tr = nullptr;
+    LALB_CUDA_TRY(ctx, cudaMalloc(&tr, n * sizeof(unsigned long long)));
+    int st = launch_token_persistent(d, h_in, nullptr, nullptr, d->argmax_dev, s, tr);
+    if (!st && (cudaMemcpyAsync(trace_host, tr, n * sizeof(unsigned long long),
+                                cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+                cudaStreamSynchronize(s) != cudaSuccess))
+        st = lalb_cuda_fail(ctx, cudaGetLastError(), "decoder_trace_step: copy");
+    cudaFree(tr);
+    *n_cta = ctx->sm_count;
+    return st;
+}
+
+extern "C" int lalb_decoder_set_path(lalb_decoder *d, int path) {
+    if (!d) return LALB_ERR_INVALID;
+    if (path != LALB_DECODE_AUTO && path != LALB_DECODE_KERNELS && path != LALB_DECODE_PERSISTENT)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_path: unknown path %d", path);
+    if (path == LALB_DECODE_PERSISTENT && !d->persist_fits)
+        return lalb_fail(d->ctx, LALB_ERR_UNSUPPORTED,
+                         "decoder_set_path: shapes outside the persistent kernel's limits");
+    if (path != d->path) drop_graphs(d);
+    d->path = path;
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_path(const lalb_decoder *d) {
+    if (!d) return LALB_ERR_INVALID;
+    return use_persistent(d) ? LALB_DECODE_PERSISTENT : LALB_DECODE_KERNELS;
+}
+
 extern "C" int lalb_decoder_launches_per_step(const lalb_decoder *d) {
     if (!d) return LALB_ERR_INVALID;
-    return 4 * d->cfg.n_layer + 1;
+    return use_persistent(d) ? 1 : 4 * d->cfg.n_layer + 1;
 }
 
 extern "C" int lalb_decoder_destroy(lalb_decoder *d) {

@@ -86,6 +86,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar,
         : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t *bar,
                                                   uint32_t parity) {
     uint32_t ok;
@@ -139,6 +143,12 @@ __device__ __forceinline__ void bulk_g2s_plain(void *smem_dst, const void *gsrc,
             smem_u32(smem_dst)),
         "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// Bulk prefetch of global memory into L2 (no shared-memory destination, no
+// completion): address and size 16-byte aligned.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *gsrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
 }
 
 // ---- programmatic dependent launch -----------------------------------------

@@ -64,3 +64,34 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &a, int in, int epi,
                          cudaStream_t stream, bool pdl, int ctas_per_sm);
 int lalb_launch_q8_head(lalb_ctx *ctx, const Q8HeadArgs &a, int in, cudaStream_t stream,
                         bool pdl, int ctas_per_sm);
+
+// One decode token in a single persistent, cooperative kernel.
+struct PersistArgs {
+    int n_layer, hidden, q_rows, kv_rows, ffn, vocab;
+    const lalb_layer_weights *layers;  // device array [n_layer]
+    const int8_t *lm_w;
+    const float *lm_s;
+    const float *h_in;                  // [hidden]
+    float *h;                           // [hidden] residual stream
+    float *qkv;                         // [q_rows + 2*kv_rows]
+    int8_t *aq;                         // [ffn] quantized SwiGLU product
+    float *asx;                         // [ffn/32]
+    int32_t *asumq;                     // [ffn/32]
+    float *logits;                      // [vocab], nullable
+    int32_t *argmax;                    // nullable
+    unsigned int *gbar;                 // [4*n_layer] grid-barrier arrival counters (zero)
+    unsigned long long *best;           // argmax key (zero)
+    unsigned int *ticket;               // CTAs done with the LM head (zero)
+    unsigned int *status;
+    // nullable: per CTA and phase, the global timer (ns) when the CTA's
+    // consumers finished the phase's work and when they left its grid
+    // barrier: [gridDim.x][n_phase][2]
+    unsigned long long *trace;
+};
+
+// Limits of the persistent kernel (checked by the decoder).
+constexpr int kPersistMaxHidden = 4096;   // K of qkv, gate/up, head; q_rows
+constexpr int kPersistMaxFfn = 20480;     // K of down
+int lalb_persist_smem_bytes();
+int lalb_persist_max_tiles();
+int lalb_launch_persist(lalb_ctx *ctx, const PersistArgs &a, cudaStream_t stream);

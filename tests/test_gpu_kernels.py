@@ -194,14 +194,19 @@ def make_decoder_weights(cfg, seed, n_vocab):
     return layers, dev_layers, lq, ls
 
 
+@pytest.mark.parametrize("path", [lb.Decoder.KERNELS, lb.Decoder.PERSISTENT],
+                         ids=["kernels", "persistent"])
 @pytest.mark.parametrize("cfg", [
     dict(n_layer=2, hidden=512, q_rows=512, kv_rows=128, ffn=1024, vocab=3000),
     dict(n_layer=1, hidden=3584, q_rows=3584, kv_rows=512, ffn=18944, vocab=20000),
     dict(n_layer=3, hidden=1024, q_rows=1024, kv_rows=256, ffn=4096, vocab=5000),
+    dict(n_layer=0, hidden=768, q_rows=256, kv_rows=0, ffn=256, vocab=777),
 ])
-def test_decoder_step_matches_oracle_chain(ctx, cfg):
+def test_decoder_step_matches_oracle_chain(ctx, cfg, path):
     layers, dl, lq, ls = make_decoder_weights(cfg, seed=1000 + cfg["hidden"], n_vocab=cfg["vocab"])
     dec = lb.Decoder(ctx, **cfg)
+    dec.set_path(path)
+    assert dec.path() == path
     for l, w in enumerate(dl):
         dec.set_layer(l, w["wqkv"], w["wo"], w["wgu"], w["wdown"])
     lqd, lsd = dev(lq), dev(ls)
@@ -236,6 +241,48 @@ def test_decoder_step_matches_oracle_chain(ctx, cfg):
     with torch.cuda.stream(s):
         assert dec.step_host(pinned) == ref_am
         us = dec.profile_step(hd)
-    assert len(us) == dec.launches_per_step() == 4 * cfg["n_layer"] + 1
+    assert len(us) == 4 * cfg["n_layer"] + 1
+    assert dec.launches_per_step() == (1 if path == lb.Decoder.PERSISTENT else len(us))
     assert all(u > 0 for u in us)
+    dec.close()
+
+
+def test_decoder_persistent_two_tokens_and_path_switch(ctx):
+    """Counters left by one token do not leak into the next: alternate
+    inputs and paths on one decoder and compare each token with the oracle."""
+    cfg = dict(n_layer=2, hidden=1024, q_rows=512, kv_rows=256, ffn=2048, vocab=4099)
+    layers, dl, lq, ls = make_decoder_weights(cfg, seed=77, n_vocab=cfg["vocab"])
+    dec = lb.Decoder(ctx, **cfg)
+    assert dec.path() == lb.Decoder.PERSISTENT   # AUTO picks it when the shapes fit
+    for l, w in enumerate(dl):
+        dec.set_layer(l, w["wqkv"], w["wo"], w["wgu"], w["wdown"])
+    lqd, lsd = dev(lq), dev(ls)   # the decoder keeps the pointers: keep the tensors
+    dec.set_lm_head(lqd, lsd)
+    logits = torch.empty(cfg["vocab"], dtype=torch.float32, device="cuda")
+    am = torch.empty(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for i, path in enumerate([lb.Decoder.PERSISTENT, lb.Decoder.PERSISTENT,
+                                  lb.Decoder.KERNELS, lb.Decoder.PERSISTENT]):
+            dec.set_path(path)
+            h_in = O.normal(cfg["hidden"], seed=300 + i)
+            _, ref_logits, ref_am = O.decode_chain(layers, lq, ls, h_in, cfg)
+            hd = dev(h_in)
+            dec.step(hd, None, logits, am)
+            s.synchronize()
+            assert_fp32_parity(host(logits), ref_logits, exact_frac=0.99)
+            assert int(host(am)[0]) == ref_am
+    dec.close()
+
+
+def test_decoder_persistent_rejects_unfit_shapes(ctx):
+    cfg = dict(n_layer=1, hidden=512, q_rows=512, kv_rows=0, ffn=24576, vocab=100)
+    dec = lb.Decoder(ctx, **cfg)
+    assert dec.path() == lb.Decoder.KERNELS    # ffn above the shared-memory limit
+    with pytest.raises(lb.LalbError) as e:
+        dec.set_path(lb.Decoder.PERSISTENT)
+    assert e.value.status == -4
+    with pytest.raises(lb.LalbError) as e:
+        dec.set_path(7)
+    assert e.value.status == -1
     dec.close()
