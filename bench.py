@@ -129,8 +129,10 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 # the GPU arm
 # --------------------------------------------------------------------------
-def build_decoder(ctx, lb, torch, c, seed):
-    """Seeded N(0,0.02) weights drawn and quantized on the GPU."""
+def build_decoder(ctx, lb, torch, c, seed, n_rank=1, rank=0):
+    """Seeded N(0,0.02) weights drawn and quantized on the GPU.  With
+    n_rank > 1 every rank draws the same full matrices and keeps (quantizes)
+    only its row shard."""
     big = max(max(r * k for r, k in layer_mats(c)), c["vocab"] * c["hidden"])
     tmp = torch.empty(big, dtype=torch.float32, device="cuda")
     layers = []
@@ -139,18 +141,20 @@ def build_decoder(ctx, lb, torch, c, seed):
         for j, (rows, K) in enumerate(layer_mats(c)):
             w = tmp[: rows * K].view(rows, K)
             ctx.fill_normal(w, seed=seed + 16 * l + j, sigma=0.02)
-            mats.append(ctx.q4k_quantize(w))
+            r0, r1 = lb.tp_range(c, j, n_rank, rank)
+            mats.append(ctx.q4k_quantize(w[r0:r1]))
         layers.append(mats)
     w = tmp[: c["vocab"] * c["hidden"]].view(c["vocab"], c["hidden"])
     ctx.fill_normal(w, seed=seed + 9999, sigma=0.02)
-    lm_q, lm_s = ctx.q8_quantize_rows(w)
+    r0, r1 = lb.tp_range(c, 4, n_rank, rank)
+    lm_q, lm_s = ctx.q8_quantize_rows(w[r0:r1])
     torch.cuda.synchronize()
     del tmp, w
     torch.cuda.empty_cache()   # the fp32 staging buffer is not needed any more
-    dec = lb.Decoder(ctx, **c)
+    dec = lb.Decoder(ctx, **c, n_rank=n_rank, rank=rank)
     for l, m in enumerate(layers):
-        dec.set_layer(l, *m)
-    dec.set_lm_head(lm_q, lm_s)
+        dec.set_layer_shard(rank, l, *m)
+    dec.set_lm_head_shard(rank, lm_q, lm_s)
     return dec, layers, (lm_q, lm_s)
 
 
@@ -203,6 +207,49 @@ def run_gemv_case(args):
     ctx.close()
 
 
+def shard_bytes(lb, c, n_rank, rank):
+    """Weight and activation bytes that rank `rank` of `n_rank` streams per token."""
+    total = 0
+    for j, (rows, K) in enumerate(layer_mats(c)):
+        r0, r1 = lb.tp_range(c, j, n_rank, rank)
+        total += c["n_layer"] * (q4k_bytes(r1 - r0, K) + 4 * K + 4 * (r1 - r0))
+    r0, r1 = lb.tp_range(c, 4, n_rank, rank)
+    return total + (r1 - r0) * (c["hidden"] + 8) + 4 * c["hidden"] + 4
+
+
+def phase_chain(dec, lb, torch, stream, h_in, am, args, c, per_layer_b, head_b, q4k_launches,
+                q4k_bytes_tok):
+    """The per-phase kernel chain (one launch per matvec) on the same weights:
+    its step rate, and each kernel's duration from events between kernels."""
+    dec.set_path(lb.Decoder.KERNELS)
+    n_chain = max(20, min(args.steps, 300))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            dec.step(h_in, None, None, am)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(n_chain):
+            dec.step(h_in, None, None, am)
+        g1.record(stream)
+        prof = np.median(np.array([dec.profile_step(h_in) for _ in range(5)]), axis=0)
+    torch.cuda.synchronize()
+    chain_ms = g0.elapsed_time(g1) / n_chain
+    dec.set_path({"auto": lb.Decoder.AUTO, "kernels": lb.Decoder.KERNELS,
+                  "persistent": lb.Decoder.PERSISTENT}[args.path])
+    q4k_us = float(sum(prof[:q4k_launches]))
+    head_us = float(prof[-1])
+    kinds = ["qkv", "o", "gate_up", "down"]
+    per_kind = {k: round(float(np.mean(prof[i:q4k_launches:4])), 2) for i, k in enumerate(kinds)}
+    per_kind_gbs = {k: round(per_layer_b[i] / (per_kind[k] * 1e-6) / 1e9, 1)
+                    for i, k in enumerate(kinds)}
+    return {"tok_s": round(1000.0 / chain_ms, 2), "ms_per_step": round(chain_ms, 5),
+            "launches_per_step": q4k_launches + 1, "q4k_us": q4k_us,
+            "q4k_gbs": round(q4k_bytes_tok / (q4k_us * 1e-6) / 1e9, 1),
+            "us_by_kind": per_kind, "gbs_by_kind": per_kind_gbs,
+            "lm_head_us": round(head_us, 2),
+            "lm_head_gbs": round(head_b / (head_us * 1e-6) / 1e9, 1)}
+
+
 def run_gpu(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -215,9 +262,15 @@ def run_gpu(args, rank, world, local_rank):
                                 timeout=datetime.timedelta(seconds=300))
     c = CFG
     ctx = lb.Context(local_rank)
-    dec, layers, lm = build_decoder(ctx, lb, torch, c, seed=1234)
+    # tensor parallel over the ranks: each GPU holds a row shard of every
+    # matrix and all of them decode the same token
+    tp = world > 1
+    dec, layers, lm = build_decoder(ctx, lb, torch, c, seed=1234, n_rank=world, rank=rank)
+    if tp:
+        dec.connect(lb.exchange_handles(dec.ipc_handle()))
+        dist.barrier()
     h_in = torch.empty(c["hidden"], dtype=torch.float32, device="cuda")
-    ctx.fill_normal(h_in, seed=77 + rank, sigma=1.0)
+    ctx.fill_normal(h_in, seed=77, sigma=1.0)
     am = torch.empty(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.Stream()
     dec.set_path({"auto": lb.Decoder.AUTO, "kernels": lb.Decoder.KERNELS,
@@ -252,53 +305,30 @@ def run_gpu(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_per_step = ms_max / args.steps
-    value = world * args.steps / (ms_max / 1000.0)
+    value = args.steps / (ms_max / 1000.0)   # tokens: every rank works on the same one
 
     per_layer_b, head_b = algorithmic_bytes(c)
     q4k_launches = 4 * c["n_layer"]
     q4k_bytes_tok = c["n_layer"] * sum(per_layer_b)
     tok_bytes = q4k_bytes_tok + head_b
+    rank_bytes = shard_bytes(lb, c, world, rank)   # what this GPU streams per token
     peak, peak_kind = measured_peak()
 
-    # The per-phase kernel chain (one launch per matvec) on the same weights:
-    # its step rate, and each kernel's duration from events between kernels.
-    dec.set_path(lb.Decoder.KERNELS)
-    n_chain = max(20, min(args.steps, 300))
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            dec.step(h_in, None, None, am)
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for _ in range(n_chain):
-            dec.step(h_in, None, None, am)
-        g1.record(stream)
-        prof = np.median(np.array([dec.profile_step(h_in) for _ in range(5)]), axis=0)
-    torch.cuda.synchronize()
-    chain_ms = g0.elapsed_time(g1) / n_chain
-    dec.set_path({"auto": lb.Decoder.AUTO, "kernels": lb.Decoder.KERNELS,
-                  "persistent": lb.Decoder.PERSISTENT}[args.path])
-    q4k_us = float(sum(prof[:q4k_launches]))
-    head_us = float(prof[-1])
-    kinds = ["qkv", "o", "gate_up", "down"]
-    per_kind = {k: round(float(np.mean(prof[i:q4k_launches:4])), 2) for i, k in enumerate(kinds)}
-    per_kind_gbs = {k: round(per_layer_b[i] / (per_kind[k] * 1e-6) / 1e9, 1)
-                    for i, k in enumerate(kinds)}
-    chain = {"tok_s": round(1000.0 / chain_ms, 2), "ms_per_step": round(chain_ms, 5),
-             "launches_per_step": q4k_launches + 1,
-             "q4k_gbs": round(q4k_bytes_tok / (q4k_us * 1e-6) / 1e9, 1),
-             "us_by_kind": per_kind, "gbs_by_kind": per_kind_gbs,
-             "lm_head_us": round(head_us, 2),
-             "lm_head_gbs": round(head_b / (head_us * 1e-6) / 1e9, 1)}
+    chain = None
+    if not tp:
+        chain = phase_chain(dec, lb, torch, stream, h_in, am, args, c, per_layer_b, head_b,
+                            q4k_launches, q4k_bytes_tok)
     if persistent:
         # one launch per token: its duration is the step time measured above
-        achieved = tok_bytes / (ms_per_step * 1e-3) / 1e9
-        roofline = {"kernel": "decode_persistent_kernel (the whole token, one launch)",
+        achieved = rank_bytes / (ms_per_step * 1e-3) / 1e9
+        roofline = {"kernel": "decode_persistent_kernel (the whole token, one launch per GPU)",
                     "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                     "traffic": profile_traffic("decode_persistent_qwen7b_ncu.md",
-                                               "traffic_bytes_per_launch"),
-                    "bytes_per_launch": tok_bytes, "us_per_launch": round(ms_per_step * 1e3, 2)}
+                                               "traffic_bytes_per_launch") if not tp else None,
+                    "bytes_per_launch": rank_bytes, "us_per_launch": round(ms_per_step * 1e3, 2)}
     else:
+        q4k_us = chain["q4k_us"]
         achieved = q4k_bytes_tok / (q4k_us * 1e-6) / 1e9
         roofline = {"kernel": "q4k_gemv (the %d Q4_K matvec launches of a token)" % q4k_launches,
                     "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -307,7 +337,7 @@ def run_gpu(args, rank, world, local_rank):
                                                "traffic_bytes_per_launch"),
                     "bytes_per_launch_avg": q4k_bytes_tok / q4k_launches,
                     "us_per_launch_avg": round(q4k_us / q4k_launches, 3)}
-    roofline["step_gbs"] = round(tok_bytes / (ms_per_step * 1e-3) / 1e9, 1)
+    roofline["step_gbs"] = round(rank_bytes / (ms_per_step * 1e-3) / 1e9, 1)
 
     # end to end through the host-buffer entry point (H2D input, D2H argmax)
     pinned = h_in.cpu().pin_memory()
@@ -324,7 +354,7 @@ def run_gpu(args, rank, world, local_rank):
     t = torch.tensor([f0.elapsed_time(f1)], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * n_e2e / (float(t.item()) / 1000.0)
+    e2e_value = n_e2e / (float(t.item()) / 1000.0)
 
     gemv = gemv_standalone(ctx, torch, stream) if rank == 0 else None
     cpu = None
@@ -335,13 +365,14 @@ def run_gpu(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "int8 (q4 x i8 dp4a -> int32 per 32-block, fp32 terms, f64 row sum)",
             "data": "synthetic: seeded N(0,0.02) weights quantized on the GPU (Q4_K min-max, "
                     "int8 per-row LM head); seeded N(0,1) hidden state",
-            "config": {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": world,
+            "config": {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": 1,
                        "seq_len": 1,
-                       "parallelism": "replicas%d" % world if world > 1 else "single",
+                       "parallelism": "tp%d (row shards, in-kernel NVLink exchange)" % world
+                                      if tp else "single",
                        "path": "persistent" if persistent else "kernels",
                        "l2": "inputs larger than L2: %.2f GB of weights streamed per step"
                              % (tok_bytes / 1e9),
@@ -356,6 +387,8 @@ def run_gpu(args, rank, world, local_rank):
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()   # no rank unmaps its exchange buffer while a peer may still use it
     dec.close()
     ctx.close()
     if world > 1:

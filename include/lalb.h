@@ -233,6 +233,32 @@ LALB_API int lalb_decoder_profile_step(lalb_decoder *dec, const float *h_in,
 LALB_API int lalb_decoder_trace_step(lalb_decoder *dec, const float *h_in,
                                      unsigned long long *trace_host, int trace_len,
                                      int *n_cta, lalb_stream stream);
+/* ---- tensor parallelism ------------------------------------------------
+ * A decoder may hold one rank of n_rank (one process or thread per GPU) or
+ * every rank at once on one GPU (rank = -1: the ranks run as groups of CTAs
+ * of one launch; for tests and for GPUs short of peers).  Rank r holds rows
+ * lalb_tp_rows(cfg, n_rank, r, matrix) of every matrix: 0 qkv, 1 o,
+ * 2 gate/up (whole 64-row gate/up tiles), 3 down, 4 LM head.  Each rank's
+ * CTAs write their output rows into every rank's exchange buffer over
+ * NVLink and wait on every rank's phase counters; the argmax is the first
+ * maximum over all ranks' rows.  Steps run on the persistent path only. */
+#define LALB_IPC_HANDLE_BYTES 64
+LALB_API int lalb_tp_rows(const lalb_decoder_cfg *cfg, int n_rank, int rank, int matrix,
+                          int *row0, int *row1);
+LALB_API int lalb_decoder_create_tp(lalb_ctx *ctx, const lalb_decoder_cfg *cfg, int n_rank,
+                                    int rank, lalb_decoder **out);
+/* w: the rank's row shard of each matrix (rows lalb_tp_rows(...), Q4_K). */
+LALB_API int lalb_decoder_set_layer_shard(lalb_decoder *dec, int rank, int layer,
+                                          const lalb_layer_weights *w);
+LALB_API int lalb_decoder_set_lm_head_shard(lalb_decoder *dec, int rank, const int8_t *w,
+                                            const float *sw);
+/* One rank per decoder: export this rank's exchange buffer (handle:
+ * LALB_IPC_HANDLE_BYTES bytes), gather every rank's handle (rank order) by
+ * any host means, then map the peers' buffers.  Every rank must connect
+ * before the first step. */
+LALB_API int lalb_decoder_ipc_handle(lalb_decoder *dec, void *handle);
+LALB_API int lalb_decoder_connect(lalb_decoder *dec, const void *handles);
+
 /* Execution path of lalb_decoder_step.  AUTO takes the persistent path
  * (the whole token in one cooperative kernel, one CTA per SM) when the
  * shapes fit it -- hidden <= 4096, q_rows <= 4096, ffn <= 20480, at most

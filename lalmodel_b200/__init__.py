@@ -143,15 +143,84 @@ class Context:
         return logits, isum, am
 
 
+IPC_HANDLE_BYTES = 64   # LALB_IPC_HANDLE_BYTES
+
+
+def tp_range(cfg, matrix, n_rank, rank):
+    """Pure-Python statement of lalb_tp_rows (rows [r0, r1) of `matrix` that
+    `rank` of `n_rank` holds; cfg is a dict of the decoder shapes)."""
+    if matrix == 0:
+        units, unit = cfg["q_rows"] + 2 * cfg["kv_rows"], 1
+    elif matrix in (1, 3):
+        units, unit = cfg["hidden"], 1
+    elif matrix == 2:
+        units, unit = 2 * cfg["ffn"] // 64, 64
+    else:
+        units, unit = cfg["vocab"], 1
+    return rank * units // n_rank * unit, (rank + 1) * units // n_rank * unit
+
+
+def exchange_handles(handle, group=None):
+    """Every rank's exchange-buffer handle in rank order, gathered over a
+    torch.distributed process group (any backend)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    return out
+
+
+def shard_rows(t, r0, r1):
+    """Rows [r0, r1) of a row-major weight tensor (Q4_K bytes [rows][K/256*144],
+    int8 [rows][K] or per-row scales [rows]) as a contiguous view."""
+    return t[r0:r1]
+
+
 class Decoder:
     """The Qwen2.5-shape decode matmul set (include/lalb.h, lalb_decoder_*)."""
 
-    def __init__(self, ctx, n_layer, hidden, q_rows, kv_rows, ffn, vocab):
+    def __init__(self, ctx, n_layer, hidden, q_rows, kv_rows, ffn, vocab, n_rank=1, rank=0):
+        """n_rank > 1: tensor-parallel decoder holding rank `rank` (one GPU
+        per rank, peers connected with ipc_handle()/connect()), or every rank
+        on this GPU with rank=-1."""
         self.ctx = ctx
         self.cfg = DecoderCfg(n_layer, hidden, q_rows, kv_rows, ffn, vocab)
+        self.n_rank, self.rank = n_rank, rank
         h = ctypes.c_void_p()
-        ctx._call("lalb_decoder_create", ctx.h, ctypes.byref(self.cfg), ctypes.byref(h))
+        ctx._call("lalb_decoder_create_tp", ctx.h, ctypes.byref(self.cfg), n_rank, rank,
+                  ctypes.byref(h))
         self.h = h
+
+    # matrices of lalb_tp_rows
+    QKV, O, GU, DOWN, HEAD = 0, 1, 2, 3, 4
+
+    def tp_rows(self, rank, matrix):
+        """Rows [r0, r1) of `matrix` that `rank` holds (include/lalb.h)."""
+        r0, r1 = ctypes.c_int(), ctypes.c_int()
+        st = _abi.lib().lalb_tp_rows(ctypes.byref(self.cfg), self.n_rank, rank, matrix,
+                                     ctypes.byref(r0), ctypes.byref(r1))
+        if st:
+            raise LalbError("lalb_tp_rows", st)
+        return r0.value, r1.value
+
+    def set_layer_shard(self, rank, layer, wqkv, wo, wgu, wdown):
+        lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())
+        self.ctx._call("lalb_decoder_set_layer_shard", self.h, rank, layer, ctypes.byref(lw))
+
+    def set_lm_head_shard(self, rank, w, sw):
+        self.ctx._call("lalb_decoder_set_lm_head_shard", self.h, rank, _p(w), _p(sw))
+
+    def ipc_handle(self):
+        """This rank's exchange-buffer handle (bytes) for the other ranks."""
+        buf = (ctypes.c_ubyte * IPC_HANDLE_BYTES)()
+        self.ctx._call("lalb_decoder_ipc_handle", self.h, buf)
+        return bytes(buf)
+
+    def connect(self, handles):
+        """handles: every rank's ipc_handle() bytes, in rank order."""
+        blob = b"".join(handles)
+        assert len(blob) == IPC_HANDLE_BYTES * self.n_rank
+        buf = (ctypes.c_ubyte * len(blob)).from_buffer_copy(blob)
+        self.ctx._call("lalb_decoder_connect", self.h, buf)
 
     def set_layer(self, layer, wqkv, wo, wgu, wdown):
         lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())

@@ -52,6 +52,12 @@ SIGNATURES = {
     "lalb_decoder_step_host": (c_int, [P, P, P, P]),
     "lalb_decoder_profile_step": (c_int, [P, P, P, P]),
     "lalb_decoder_trace_step": (c_int, [P, P, P, c_int, P, P]),
+    "lalb_tp_rows": (c_int, [ctypes.POINTER(DecoderCfg), c_int, c_int, c_int, P, P]),
+    "lalb_decoder_create_tp": (c_int, [P, ctypes.POINTER(DecoderCfg), c_int, c_int, ctypes.POINTER(P)]),
+    "lalb_decoder_set_layer_shard": (c_int, [P, c_int, c_int, ctypes.POINTER(LayerWeights)]),
+    "lalb_decoder_set_lm_head_shard": (c_int, [P, c_int, P, P]),
+    "lalb_decoder_ipc_handle": (c_int, [P, P]),
+    "lalb_decoder_connect": (c_int, [P, P]),
     "lalb_decoder_set_path": (c_int, [P, c_int]),
     "lalb_decoder_path": (c_int, [P]),
     "lalb_decoder_launches_per_step": (c_int, [P]),

@@ -7,6 +7,7 @@
 // launch (each one starts streaming its weights while its predecessor is
 // still finishing) and the whole token is captured once into a CUDA graph
 // per set of buffer pointers, then replayed.
+#include <cstring>
 #include <map>
 #include <tuple>
 #include <vector>
@@ -17,10 +18,13 @@
 struct lalb_decoder {
     lalb_ctx *ctx;
     lalb_decoder_cfg cfg;
-    std::vector<lalb_layer_weights> layers;
-    const int8_t *lm_w = nullptr;
-    const float *lm_s = nullptr;
-    // activations (device, owned)
+    // tensor parallelism: this decoder holds ranks [rank0, rank0 + ranks_here)
+    // of n_rank (ranks_here is 1, or n_rank when one GPU runs every rank)
+    int n_rank = 1, rank0 = 0, ranks_here = 1;
+    std::vector<std::vector<lalb_layer_weights>> layers;   // [ranks_here][n_layer] row shards
+    std::vector<const int8_t *> lm_w;                     // [ranks_here]
+    std::vector<const float *> lm_s;
+    // activations of the per-phase kernel chain (device, owned; one rank only)
     float *qkv = nullptr;     // [q_rows + 2*kv_rows]
     float *h_res = nullptr;   // [hidden] residual stream
     int8_t *aq = nullptr;     // [ffn] quantized SwiGLU product
@@ -30,9 +34,12 @@ struct lalb_decoder {
     int32_t *argmax_dev = nullptr;
     int32_t *argmax_host = nullptr;  // pinned
     // persistent path
-    lalb_layer_weights *layers_dev = nullptr;  // [n_layer]
-    unsigned int *pctr = nullptr;              // grid-barrier counters [4*n_layer], ticket
-    unsigned long long *pbest = nullptr;       // argmax key
+    lalb_layer_weights *layers_dev = nullptr;  // [ranks_here][n_layer]
+    unsigned char *xb_own = nullptr;           // exchange buffers of the held ranks
+    size_t xb_bytes = 0;                       // one rank's exchange buffer
+    unsigned char *xb[kPersistMaxRanks] = {};  // every rank's (peer mappings for others)
+    bool xb_opened[kPersistMaxRanks] = {};     // mapped through CUDA IPC
+    bool connected = false;
     bool layers_dirty = true;
     bool persist_fits = false;
     int path = LALB_DECODE_AUTO;
@@ -59,7 +66,7 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
         return cudaEventRecordWithFlags((*ev)[mark_i++], s, cudaEventRecordExternal);
     };
     for (int l = 0; l < c.n_layer; ++l) {
-        const lalb_layer_weights &w = d->layers[l];
+        const lalb_layer_weights &w = d->layers[0][l];
         const float *resid = l == 0 ? h_in : d->h_res;
         int st;
         {
@@ -115,8 +122,8 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
         }
     }
     Q8HeadArgs a = {};
-    a.W = d->lm_w;
-    a.sw = d->lm_s;
+    a.W = d->lm_w[0];
+    a.sw = d->lm_s[0];
     a.K = c.hidden;
     a.row_begin = 0;
     a.row_end = c.vocab;
@@ -134,21 +141,23 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
 }
 
 bool use_persistent(const lalb_decoder *d) {
-    return d->persist_fits && d->path != LALB_DECODE_KERNELS;
+    return d->persist_fits && (d->n_rank > 1 || d->path != LALB_DECODE_KERNELS);
 }
 
-// The same token as launch_token, as one cooperative kernel.
+// The same token as launch_token, as one cooperative kernel (every held rank
+// as one group of CTAs).
 int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, float *logits,
                             int32_t *argmax, cudaStream_t s,
                             unsigned long long *trace = nullptr) {
     lalb_ctx *ctx = d->ctx;
     const lalb_decoder_cfg &c = d->cfg;
     if (d->layers_dirty) {
-        if (c.n_layer > 0)
-            LALB_CUDA_TRY(ctx, cudaMemcpyAsync(d->layers_dev, d->layers.data(),
+        for (int r = 0; r < d->ranks_here && c.n_layer > 0; ++r)
+            LALB_CUDA_TRY(ctx, cudaMemcpyAsync(d->layers_dev + (size_t)r * c.n_layer,
+                                               d->layers[r].data(),
                                                sizeof(lalb_layer_weights) * c.n_layer,
                                                cudaMemcpyHostToDevice, s));
-        LALB_CUDA_TRY(ctx, cudaStreamSynchronize(s));  // the host vector may change after
+        LALB_CUDA_TRY(ctx, cudaStreamSynchronize(s));  // the host vectors may change after
         d->layers_dirty = false;
     }
     PersistArgs a = {};
@@ -158,26 +167,29 @@ int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, fl
     a.kv_rows = c.kv_rows;
     a.ffn = c.ffn;
     a.vocab = c.vocab;
-    a.layers = d->layers_dev;
-    a.lm_w = d->lm_w;
-    a.lm_s = d->lm_s;
+    a.n_rank = d->n_rank;
+    a.rank0 = d->rank0;
+    a.ranks_here = d->ranks_here;
+    a.cta_per_rank = ctx->sm_count / d->ranks_here;
+    a.remote = d->ranks_here < d->n_rank;
+    for (int r = 0; r < d->ranks_here; ++r) {
+        a.rk[r].layers = d->layers_dev + (size_t)r * c.n_layer;
+        a.rk[r].lm_w = d->lm_w[r];
+        a.rk[r].lm_s = d->lm_s[r];
+    }
+    for (int j = 0; j < d->n_rank; ++j) a.xb[j] = d->xb[j];
     a.h_in = h_in;
-    a.h = d->h_res;
-    a.qkv = d->qkv;
-    a.aq = d->aq;
-    a.asx = d->asx;
-    a.asumq = d->asumq;
     a.logits = logits;
     a.argmax = argmax;
-    a.gbar = d->pctr;
-    a.ticket = d->pctr + 4 * c.n_layer;
-    a.best = d->pbest;
     a.status = &ctx->scratch->status;
     a.trace = trace;
     if (int st = lalb_launch_persist(ctx, a, s)) return st;
-    if (h_out)
-        LALB_CUDA_TRY(ctx, cudaMemcpyAsync(h_out, c.n_layer > 0 ? d->h_res : h_in,
-                                           sizeof(float) * c.hidden, cudaMemcpyDeviceToDevice, s));
+    if (h_out) {
+        const PersistXLayout L = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.ffn);
+        const float *hf = c.n_layer > 0 ? reinterpret_cast<const float *>(d->xb[d->rank0] + L.h) : h_in;
+        LALB_CUDA_TRY(ctx, cudaMemcpyAsync(h_out, hf, sizeof(float) * c.hidden,
+                                           cudaMemcpyDeviceToDevice, s));
+    }
     return LALB_OK;
 }
 
@@ -203,15 +215,25 @@ void free_decoder(lalb_decoder *d) {
     cudaFree(d->argmax_dev);
     cudaFreeHost(d->argmax_host);
     cudaFree(d->layers_dev);
-    cudaFree(d->pctr);
-    cudaFree(d->pbest);
+    for (int j = 0; j < kPersistMaxRanks; ++j)
+        if (d->xb_opened[j]) cudaIpcCloseMemHandle(d->xb[j]);
+    cudaFree(d->xb_own);
     delete d;
 }
 
 }  // namespace
 
-extern "C" int lalb_decoder_create(lalb_ctx *ctx, const lalb_decoder_cfg *cfg,
-                                   lalb_decoder **out) {
+extern "C" int lalb_tp_rows(const lalb_decoder_cfg *cfg, int n_rank, int rank, int matrix,
+                            int *row0, int *row1) {
+    if (!cfg || !row0 || !row1 || n_rank < 1 || n_rank > kPersistMaxRanks || rank < 0 ||
+        rank >= n_rank || matrix < 0 || matrix > 4)
+        return LALB_ERR_INVALID;
+    lalb_tp_range(*cfg, matrix, n_rank, rank, row0, row1);
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_create_tp(lalb_ctx *ctx, const lalb_decoder_cfg *cfg, int n_rank,
+                                      int rank, lalb_decoder **out) {
     if (!ctx) return LALB_ERR_INVALID;
     if (!cfg || !out) return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: null");
     *out = nullptr;
@@ -220,74 +242,163 @@ extern "C" int lalb_decoder_create(lalb_ctx *ctx, const lalb_decoder_cfg *cfg,
         c.kv_rows < 0 || c.ffn <= 0 || c.ffn % 256 || c.vocab <= 0 || c.hidden > 4096)
         return lalb_fail(ctx, LALB_ERR_INVALID,
                          "decoder_create: hidden/q_rows/ffn must be multiples of 256, hidden <= 4096");
+    if (c.vocab >= (1 << 24) || 2LL * c.ffn >= (1 << 24) || c.q_rows + 2LL * c.kv_rows >= (1 << 24))
+        return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: matrices must have < 2^24 rows");
+    if (n_rank < 1 || n_rank > kPersistMaxRanks || rank < -1 || rank >= n_rank)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: rank %d of %d", rank, n_rank);
     LALB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     lalb_decoder *d = new (std::nothrow) lalb_decoder();
     if (!d) return LALB_ERR_NOMEM;
     d->ctx = ctx;
     d->cfg = c;
-    d->layers.assign(c.n_layer, lalb_layer_weights{nullptr, nullptr, nullptr, nullptr});
-    bool ok = cudaMalloc(&d->qkv, sizeof(float) * (c.q_rows + 2 * c.kv_rows)) == cudaSuccess &&
-              cudaMalloc(&d->h_res, sizeof(float) * c.hidden) == cudaSuccess &&
-              cudaMalloc(&d->aq, c.ffn) == cudaSuccess &&
-              cudaMalloc(&d->asx, sizeof(float) * (c.ffn / 32)) == cudaSuccess &&
-              cudaMalloc(&d->asumq, sizeof(int32_t) * (c.ffn / 32)) == cudaSuccess &&
+    d->n_rank = n_rank;
+    d->rank0 = rank < 0 ? 0 : rank;
+    d->ranks_here = rank < 0 ? n_rank : 1;
+    d->layers.assign(d->ranks_here, std::vector<lalb_layer_weights>(
+                                        c.n_layer, lalb_layer_weights{nullptr, nullptr, nullptr, nullptr}));
+    d->lm_w.assign(d->ranks_here, nullptr);
+    d->lm_s.assign(d->ranks_here, nullptr);
+    d->xb_bytes = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.ffn).total;
+    const bool chain = n_rank == 1;   // the per-phase kernel chain runs on one GPU only
+    bool ok = (!chain || (cudaMalloc(&d->qkv, sizeof(float) * (c.q_rows + 2 * c.kv_rows)) == cudaSuccess &&
+                          cudaMalloc(&d->h_res, sizeof(float) * c.hidden) == cudaSuccess &&
+                          cudaMalloc(&d->aq, c.ffn) == cudaSuccess &&
+                          cudaMalloc(&d->asx, sizeof(float) * (c.ffn / 32)) == cudaSuccess &&
+                          cudaMalloc(&d->asumq, sizeof(int32_t) * (c.ffn / 32)) == cudaSuccess)) &&
               cudaMalloc(&d->h_in_dev, sizeof(float) * c.hidden) == cudaSuccess &&
               cudaMalloc(&d->argmax_dev, sizeof(int32_t)) == cudaSuccess &&
               cudaMallocHost(&d->argmax_host, sizeof(int32_t)) == cudaSuccess &&
-              cudaMalloc(&d->layers_dev, sizeof(lalb_layer_weights) * (c.n_layer + 1)) ==
+              cudaMalloc(&d->layers_dev, sizeof(lalb_layer_weights) * (d->ranks_here * c.n_layer + 1)) ==
                   cudaSuccess &&
-              cudaMalloc(&d->pctr, sizeof(unsigned int) * (4 * c.n_layer + 1)) == cudaSuccess &&
-              cudaMalloc(&d->pbest, sizeof(unsigned long long)) == cudaSuccess &&
-              cudaMemset(d->pctr, 0, sizeof(unsigned int) * (4 * c.n_layer + 1)) == cudaSuccess &&
-              cudaMemset(d->pbest, 0, sizeof(unsigned long long)) == cudaSuccess &&
+              cudaMalloc(&d->xb_own, d->xb_bytes * d->ranks_here) == cudaSuccess &&
+              cudaMemset(d->xb_own, 0, d->xb_bytes * d->ranks_here) == cudaSuccess &&
               cudaDeviceSynchronize() == cudaSuccess;
     if (!ok) {
         cudaGetLastError();
         free_decoder(d);
-        return lalb_fail(ctx, LALB_ERR_NOMEM, "decoder_create: activation buffers");
+        return lalb_fail(ctx, LALB_ERR_NOMEM, "decoder_create: device buffers");
     }
+    for (int r = 0; r < d->ranks_here; ++r) d->xb[d->rank0 + r] = d->xb_own + d->xb_bytes * r;
+    d->connected = d->ranks_here == n_rank;
     // the persistent kernel's limits: activations in shared memory, gate/up
-    // tiles per CTA, one resident CTA per SM for the grid barriers
+    // tiles per CTA, one resident CTA per SM (every rank of this GPU gets
+    // sm_count / ranks_here of them)
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device);
-    const long long gu_units = 2LL * c.ffn / 64;
-    d->persist_fits = coop && c.hidden <= kPersistMaxHidden && c.q_rows <= kPersistMaxHidden &&
-                      c.ffn <= kPersistMaxFfn && c.ffn % 32 == 0 &&
-                      (gu_units + ctx->sm_count - 1) / ctx->sm_count <= lalb_persist_max_tiles() &&
+    const int cta = ctx->sm_count / d->ranks_here;
+    int g0, g1;
+    lalb_tp_range(c, 2, n_rank, 0, &g0, &g1);
+    const long long gu_units = (g1 - g0) / 64 + 1;   // the largest shard
+    d->persist_fits = coop && cta >= 1 && c.hidden <= kPersistMaxHidden &&
+                      c.q_rows <= kPersistMaxHidden && c.ffn <= kPersistMaxFfn && c.ffn % 32 == 0 &&
+                      (gu_units + cta - 1) / cta <= lalb_persist_max_tiles() &&
                       (size_t)lalb_persist_smem_bytes() <= ctx->smem_optin;
+    if (n_rank > 1 && !d->persist_fits) {
+        free_decoder(d);
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED,
+                         "decoder_create: tensor parallelism needs the persistent kernel's limits");
+    }
     *out = d;
     return LALB_OK;
 }
 
-extern "C" int lalb_decoder_set_layer(lalb_decoder *d, int layer, const lalb_layer_weights *w) {
+extern "C" int lalb_decoder_create(lalb_ctx *ctx, const lalb_decoder_cfg *cfg,
+                                   lalb_decoder **out) {
+    return lalb_decoder_create_tp(ctx, cfg, 1, 0, out);
+}
+
+static int held(lalb_decoder *d, int rank) {
+    return rank >= d->rank0 && rank < d->rank0 + d->ranks_here;
+}
+
+extern "C" int lalb_decoder_set_layer_shard(lalb_decoder *d, int rank, int layer,
+                                            const lalb_layer_weights *w) {
     if (!d) return LALB_ERR_INVALID;
+    if (!held(d, rank))
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_layer: rank %d not held here", rank);
     if (!w || layer < 0 || layer >= d->cfg.n_layer || !w->wqkv || !w->wo || !w->wgu || !w->wdown)
         return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_layer: bad layer %d", layer);
     if (((uintptr_t)w->wqkv | (uintptr_t)w->wo | (uintptr_t)w->wgu | (uintptr_t)w->wdown) & 15u)
         return lalb_fail(d->ctx, LALB_ERR_INVALID,
                          "decoder_set_layer: weights must be 16-byte aligned");
-    d->layers[layer] = *w;
+    d->layers[rank - d->rank0][layer] = *w;
     d->layers_dirty = true;
+    drop_graphs(d);
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_set_layer(lalb_decoder *d, int layer, const lalb_layer_weights *w) {
+    if (!d) return LALB_ERR_INVALID;
+    if (d->n_rank != 1)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_layer: use the shard call");
+    return lalb_decoder_set_layer_shard(d, 0, layer, w);
+}
+
+extern "C" int lalb_decoder_set_lm_head_shard(lalb_decoder *d, int rank, const int8_t *w,
+                                              const float *sw) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!held(d, rank))
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: rank %d not held here", rank);
+    if (!w || !sw) return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: null");
+    if (((uintptr_t)w & 15u) || ((uintptr_t)sw & 3u))
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: misaligned");
+    d->lm_w[rank - d->rank0] = w;
+    d->lm_s[rank - d->rank0] = sw;
     drop_graphs(d);
     return LALB_OK;
 }
 
 extern "C" int lalb_decoder_set_lm_head(lalb_decoder *d, const int8_t *w, const float *sw) {
     if (!d) return LALB_ERR_INVALID;
-    if (!w || !sw) return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: null");
-    if (((uintptr_t)w & 15u) || ((uintptr_t)sw & 3u))
-        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: misaligned");
-    d->lm_w = w;
-    d->lm_s = sw;
+    if (d->n_rank != 1)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: use the shard call");
+    return lalb_decoder_set_lm_head_shard(d, 0, w, sw);
+}
+
+extern "C" int lalb_decoder_ipc_handle(lalb_decoder *d, void *handle) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!handle || d->ranks_here != 1)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_ipc_handle: one rank per decoder");
+    static_assert(sizeof(cudaIpcMemHandle_t) == LALB_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    LALB_CUDA_TRY(d->ctx, cudaIpcGetMemHandle(&h, d->xb_own));
+    memcpy(handle, &h, sizeof(h));
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_connect(lalb_decoder *d, const void *handles) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!handles || d->ranks_here != 1)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_connect: one rank per decoder");
+    if (d->connected) return LALB_OK;
+    LALB_CUDA_TRY(d->ctx, cudaSetDevice(d->ctx->device));
+    for (int j = 0; j < d->n_rank; ++j) {
+        if (j == d->rank0) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const unsigned char *>(handles) + (size_t)j * LALB_IPC_HANDLE_BYTES,
+               sizeof(h));
+        void *p = nullptr;
+        LALB_CUDA_TRY(d->ctx, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        d->xb[j] = static_cast<unsigned char *>(p);
+        d->xb_opened[j] = true;
+    }
+    d->connected = true;
     drop_graphs(d);
     return LALB_OK;
 }
 
 static int check_ready(lalb_decoder *d) {
-    if (!d->lm_w) return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: LM head not set");
-    for (int l = 0; l < d->cfg.n_layer; ++l)
-        if (!d->layers[l].wqkv)
-            return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: layer %d not set", l);
+    for (int r = 0; r < d->ranks_here; ++r) {
+        if (!d->lm_w[r])
+            return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: LM head of rank %d not set",
+                             d->rank0 + r);
+        for (int l = 0; l < d->cfg.n_layer; ++l)
+            if (!d->layers[r][l].wqkv)
+                return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: layer %d of rank %d not set", l,
+                                 d->rank0 + r);
+    }
+    if (!d->connected)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: peers not connected");
     return LALB_OK;
 }
 
@@ -358,6 +469,8 @@ extern "C" int lalb_decoder_profile_step(lalb_decoder *d, const float *h_in, flo
     lalb_ctx *ctx = d->ctx;
     if (!h_in || !kernel_us)
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_profile_step: null argument");
+    if (d->n_rank != 1)
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "decoder_profile_step: one GPU only");
     if (int st = check_ready(d)) return st;
     // The instrumented token is captured into a graph and replayed, so the
     // intervals hold device time only (no host launch latency between them).
@@ -425,7 +538,7 @@ extern "C" int lalb_decoder_trace_step(lalb_decoder *d, const float *h_in,
                 cudaStreamSynchronize(s) != cudaSuccess))
         st = lalb_cuda_fail(ctx, cudaGetLastError(), "decoder_trace_step: copy");
     cudaFree(tr);
-    *n_cta = ctx->sm_count;
+    *n_cta = (ctx->sm_count / d->ranks_here) * d->ranks_here;
     return st;
 }
 
@@ -436,6 +549,9 @@ extern "C" int lalb_decoder_set_path(lalb_decoder *d, int path) {
     if (path == LALB_DECODE_PERSISTENT && !d->persist_fits)
         return lalb_fail(d->ctx, LALB_ERR_UNSUPPORTED,
                          "decoder_set_path: shapes outside the persistent kernel's limits");
+    if (path == LALB_DECODE_KERNELS && d->n_rank != 1)
+        return lalb_fail(d->ctx, LALB_ERR_UNSUPPORTED,
+                         "decoder_set_path: the kernel chain runs on one GPU only");
     if (path != d->path) drop_graphs(d);
     d->path = path;
     return LALB_OK;

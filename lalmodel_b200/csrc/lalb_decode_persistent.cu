@@ -64,7 +64,8 @@ constexpr int kSlots = LALB_PERSIST_SLOTS;
 constexpr uint32_t kSlotBytes = LALB_PERSIST_SLOT_BYTES;
 constexpr int kMaxTiles = 8;                 // gate/up 64-row tiles per CTA
 constexpr int kMaxNS = kPersistMaxFfn / 32;
-constexpr uint32_t kGridSpinLimit = 1u << 22;
+constexpr unsigned long long kWaitLimitNs = 10ull * 1000 * 1000 * 1000;   // 10 s
+constexpr uint32_t kWaitIterCap = 1u << 28;   // safety net beside the time limit
 constexpr int kTraceFields = 8;
 constexpr int kPrefetchChunks = LALB_PERSIST_PREFETCH;   // L2 prefetch distance beyond the ring
 constexpr int kQuads = kConsThreads / 4;     // quantizer quads per pass
@@ -101,57 +102,102 @@ __host__ __device__ inline Layout make_layout() {
 enum : int { kQkv = 0, kO = 1, kGu = 2, kDown = 3, kHead = 4 };
 
 struct Phase {
-    const uint8_t *W;
+    const uint8_t *W;                   // this rank's row shard
     int kind, layer, K, rows_total, unit, row_bytes, R;
-    int r0, r1, nchunks;
+    int goff;                           // global index of the shard's first row
+    int r0, r1, nchunks;                // this CTA's rows, relative to the shard
 };
 
-__device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p) {
+// Where this CTA sits: its rank (group of cta_per_rank CTAs) and its index
+// within the rank's CTAs.
+struct Where {
+    int rl;        // rank - rank0
+    int rank;
+    int cb;        // CTA index within the rank
+};
+
+__device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const Where &w) {
     Phase d;
     d.layer = p >> 2;
+    const PersistRank &rk = a.rk[w.rl];
+    lalb_decoder_cfg c;
+    c.n_layer = a.n_layer;
+    c.hidden = a.hidden;
+    c.q_rows = a.q_rows;
+    c.kv_rows = a.kv_rows;
+    c.ffn = a.ffn;
+    c.vocab = a.vocab;
+    int g0, g1;
     if (p == 4 * a.n_layer) {
         d.kind = kHead;
-        d.W = reinterpret_cast<const uint8_t *>(a.lm_w);
+        d.W = reinterpret_cast<const uint8_t *>(rk.lm_w);
         d.K = a.hidden;
-        d.rows_total = a.vocab;
         d.unit = 1;
         d.row_bytes = a.hidden;
+        lalb_tp_range(c, 4, a.n_rank, w.rank, &g0, &g1);
     } else {
-        const lalb_layer_weights lw = a.layers[d.layer];
+        const lalb_layer_weights lw = rk.layers[d.layer];
         d.kind = p & 3;
         switch (d.kind) {
             case kQkv:
                 d.W = static_cast<const uint8_t *>(lw.wqkv);
                 d.K = a.hidden;
-                d.rows_total = a.q_rows + 2 * a.kv_rows;
                 break;
             case kO:
                 d.W = static_cast<const uint8_t *>(lw.wo);
                 d.K = a.q_rows;
-                d.rows_total = a.hidden;
                 break;
             case kGu:
                 d.W = static_cast<const uint8_t *>(lw.wgu);
                 d.K = a.hidden;
-                d.rows_total = 2 * a.ffn;
                 break;
             default:
                 d.W = static_cast<const uint8_t *>(lw.wdown);
                 d.K = a.ffn;
-                d.rows_total = a.hidden;
                 break;
         }
         d.unit = d.kind == kGu ? 64 : 1;
         d.row_bytes = (d.K >> 8) * 144;
+        lalb_tp_range(c, d.kind, a.n_rank, w.rank, &g0, &g1);
     }
+    d.goff = g0;
+    d.rows_total = g1 - g0;
     d.R = min(8, (int)(kSlotBytes / (uint32_t)d.row_bytes));
     if (d.kind == kGu) d.R = 1 << (31 - __clz(d.R));   // chunks never straddle a 64-row tile
     if (d.kind == kQkv || d.kind == kO) d.R = min(d.R, 4);   // small phases: every consumer gets rows
     const int units = d.rows_total / d.unit;
-    d.r0 = (int)((long long)blockIdx.x * units / gridDim.x) * d.unit;
-    d.r1 = (int)((long long)(blockIdx.x + 1) * units / gridDim.x) * d.unit;
+    const int G = a.cta_per_rank;
+    // 32-bit: units < 2^24 and cb < 256
+    d.r0 = (int)((unsigned)w.cb * (unsigned)units / (unsigned)G) * d.unit;
+    d.r1 = (int)((unsigned)(w.cb + 1) * (unsigned)units / (unsigned)G) * d.unit;
     d.nchunks = (d.r1 - d.r0 + d.R - 1) / d.R;
     return d;
+}
+
+// Views of one rank's exchange buffer.
+struct XView {
+    unsigned int *gbar, *seq, *ticket;
+    unsigned long long *best, *keys;
+    float *h, *q;
+    int8_t *aq;
+    float *asx;
+    int *asumq;
+};
+__device__ __forceinline__ XView xview(const PersistArgs &a, int rank) {
+    const PersistXLayout L = lalb_persist_xlayout(a.n_layer, a.hidden, a.q_rows, a.ffn);
+    unsigned char *b = a.xb[rank];
+    XView v;
+    v.gbar = reinterpret_cast<unsigned int *>(b + L.gbar);
+    v.seq = reinterpret_cast<unsigned int *>(b + L.seq);
+    v.ticket = reinterpret_cast<unsigned int *>(b + L.ticket);
+    v.best = reinterpret_cast<unsigned long long *>(b + L.best);
+    v.keys = reinterpret_cast<unsigned long long *>(b + L.keys);
+    v.h = reinterpret_cast<float *>(b + L.h);
+    v.q = reinterpret_cast<float *>(b + L.q);
+    v.aq = reinterpret_cast<int8_t *>(b + L.aq);
+    v.asx = reinterpret_cast<float *>(b + L.asx);
+    v.asumq = reinterpret_cast<int *>(b + L.asumq);
+    return v;
 }
 
 // Activations written by other CTAs in the previous phase: read at L2.
@@ -162,31 +208,87 @@ __device__ __forceinline__ void load8_cg(const float *x, float (&v)[8]) {
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 __device__ __forceinline__ void cons_bar() {
     asm volatile("bar.sync 1, %0;" ::"r"(kConsThreads) : "memory");
 }
 
-// Arrives at a grid-barrier counter and waits until `target` CTAs have.
-// Gives up at the spin limit or as soon as any CTA has raised the status
-// word (then every later wait of the token is skipped: a failed token ends
-// in seconds, not after one time-out per wait).  Returns false on failure.
-__device__ __forceinline__ bool grid_arrive_wait(unsigned int *ctr, unsigned int target,
-                                                 unsigned int *status) {
-    // the named barrier before this call orders the CTA's writes before the
-    // release; the acquire below orders every CTA's writes before the reads
-    // that follow the next named barrier
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+// Two-level phase barrier.  Every CTA arrives on its own rank's counter
+// lbar[ph] (GPU scope, release); the CTA whose arrival completes the rank
+// (it sees the count reach its target) acquires and then adds one to rbar[ph] of
+// every other rank with a system-scope release when ranks live on other
+// GPUs.  Its acquire saw every CTA of its rank, so the release also carries
+// their stores into the other ranks' buffers.  A CTA then waits until its
+// rank's lbar[ph] has all local CTAs and rbar[ph] all other ranks.  Both
+// counters grow across tokens (targets from the token count `seq`; the
+// comparisons survive wrap-around).  Gives up after kWaitLimitNs, or as soon
+// as this rank's status word is raised (then every later wait of the token
+// is skipped: a failed token ends in seconds, not one time-out per wait).
+// Returns false on failure.
+__device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &own, int rank,
+                                            int ph, unsigned int seq) {
+    const unsigned int nl = a.cta_per_rank, nr = a.n_rank - 1;
+    const unsigned int t_local = (seq + 1u) * nl;
+    unsigned int *lbar = own.gbar + ph;
+    if (nr == 0) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(lbar) : "memory");
+    } else {
+        unsigned int old;
+        asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(lbar) : "memory");
+        if (old + 1u == t_local) {
+            // the rank's last arrival: acquire every other CTA's release first
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+            for (int j = 0; j < a.n_rank; ++j) {
+                if (j == rank) continue;
+                unsigned int *ctr = xview(a, j).gbar + 4 * a.n_layer + ph;
+                if (a.remote)
+                    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+                else
+                    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ bool grid_wait(const PersistArgs &a, const XView &own, int ph,
+                                          unsigned int seq) {
+    const unsigned int nl = a.cta_per_rank, nr = a.n_rank - 1;
+    const unsigned int t_local = (seq + 1u) * nl, t_remote = (seq + 1u) * nr;
+    unsigned int *lbar = own.gbar + ph;
+    unsigned int *rbar = own.gbar + 4 * a.n_layer + ph;
     bool ok = true;
+    unsigned long long t0 = 0;
+    bool local_done = false;
     for (uint32_t k = 0;; ++k) {
         unsigned int v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-        if (v >= target) break;
-        if ((k & 15) == 15 && *(volatile unsigned int *)status) {
+        if (!local_done) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(lbar) : "memory");
+            local_done = (int)(v - t_local) >= 0;
+        }
+        if (local_done) {
+            if (nr == 0) break;
+            if (a.remote)
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(rbar) : "memory");
+            else
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(rbar) : "memory");
+            if ((int)(v - t_remote) >= 0) break;
+        }
+        if ((k & 15) == 15 && *(volatile unsigned int *)a.status) {
             ok = false;
             break;
         }
-        if (k > kGridSpinLimit) {
-            atomicOr(status, LALB_STATUS_WAIT_TIMEOUT);
+        if ((k & 255) == 255) {
+            const unsigned long long t = global_ns();
+            if (t0 == 0) t0 = t;
+            else if (t - t0 > kWaitLimitNs) k = kWaitIterCap;
+        }
+        if (k >= kWaitIterCap) {
+            atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
             ok = false;
             break;
         }
@@ -195,20 +297,60 @@ __device__ __forceinline__ bool grid_arrive_wait(unsigned int *ctr, unsigned int
     return ok;
 }
 
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
+// The ranks' LM-head keys: each rank's last CTA stored its key into every
+// rank's buffer, then arrives here once per rank (the counter after the
+// phase counters) and waits for all n_rank arrivals of this token.
+__device__ __forceinline__ bool keys_arrive_wait(const PersistArgs &a, const XView &own,
+                                                 unsigned int seq) {
+    for (int j = 0; j < a.n_rank; ++j) {
+        unsigned int *ctr = xview(a, j).gbar + 8 * a.n_layer;
+        if (a.remote)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+        else
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+    }
+    const unsigned int target = (seq + 1u) * (unsigned int)a.n_rank;
+    unsigned int *kb = own.gbar + 8 * a.n_layer;
+    unsigned long long t0 = 0;
+    for (uint32_t k = 0;; ++k) {
+        unsigned int v;
+        if (a.remote)
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(kb) : "memory");
+        else
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(kb) : "memory");
+        if ((int)(v - target) >= 0) return true;
+        if ((k & 15) == 15 && *(volatile unsigned int *)a.status) return false;
+        if ((k & 255) == 255) {
+            const unsigned long long t = global_ns();
+            if (t0 == 0) t0 = t;
+            else if (t - t0 > kWaitLimitNs) k = kWaitIterCap;
+        }
+        if (k >= kWaitIterCap) {
+            atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
+            return false;
+        }
+        if (k > 64) __nanosleep(32);
+    }
 }
 
 // Bounded mbarrier wait that is skipped once this thread has seen a failure.
 // Adds the number of polls to `polls`.
+// The limit is time-based (kWaitLimitNs on the global timer, with an
+// iteration cap as well): every wait of this kernel may depend, through the
+// grid barriers, on other GPUs whose launches can lag by a good fraction of
+// a second.
 __device__ __forceinline__ void pwait(uint64_t *bar, uint32_t parity, unsigned int *status,
                                       bool &dead, unsigned long long &polls) {
     if (dead) return;
-    for (uint32_t i = 0; i < LALB_SPIN_LIMIT; ++i) {
+    unsigned long long t0 = 0;
+    for (uint32_t i = 0; i < kWaitIterCap; ++i) {
         ++polls;
         if (mbar_try_wait(bar, parity)) return;
+        if ((i & 63) == 63) {
+            const unsigned long long t = global_ns();
+            if (t0 == 0) t0 = t;
+            else if (t - t0 > kWaitLimitNs) break;
+        }
     }
     if (status) atomicOr(status, LALB_STATUS_WAIT_TIMEOUT);
     dead = true;
@@ -238,7 +380,8 @@ struct Cons {
 // most one phase behind and the parity waits cannot match a stale phase.
 template <int KIND>
 __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase &d,
-                                              uint32_t g_base, Cons &cs) {
+                                              uint32_t g_base, const PersistXLayout &XL,
+                                              const XView &own, const PersistRank &rk, Cons &cs) {
     const int lane = cs.lane;
     const int NS = d.K >> 5, NH = d.K >> 7;
     const int myrow = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
@@ -301,11 +444,13 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
         const int rs = d.r0 + j * d.R;
         const int nr = min(d.R, d.r1 - rs);
         // per-row values needed by the epilogue, fetched before the math
+        // (the residual rows of o and down are this rank's own rows)
         float pre = 0.0f;
         if (lane < nr) {
-            if (KIND == kO) pre = __ldcg((d.layer == 0 ? a.h_in : a.h) + rs + lane);
-            if (KIND == kDown) pre = __ldcg(a.h + rs + lane);
-            if (KIND == kHead) pre = a.lm_s[rs + lane];
+            const int grow = d.goff + rs + lane;
+            if (KIND == kO) pre = __ldcg((d.layer == 0 ? a.h_in : own.h) + grow);
+            if (KIND == kDown) pre = __ldcg(own.h + grow);
+            if (KIND == kHead) pre = rk.lm_s[rs + lane];
         }
         if (KIND == kDown) {
             // K > 4096: activations from shared memory, one row at a time
@@ -333,7 +478,12 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                 }
                 acc = warp_sum_d(acc);
                 const float hv = __shfl_sync(0xffffffffu, pre, r);
-                if (lane == 0) a.h[rs + r] = __fadd_rn(hv, (float)acc);
+                // the new residual row goes to every rank
+                if (lane == 0) {
+                    const float hn = __fadd_rn(hv, (float)acc);
+                    for (int j = 0; j < a.n_rank; ++j)
+                        reinterpret_cast<float *>(a.xb[j] + XL.h)[d.goff + rs + r] = hn;
+                }
             }
         } else if (KIND == kHead) {
             const int h0 = (lane >> 2) & 1;
@@ -367,7 +517,7 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                 }
                 const double v = warp_sum_rows4(acc, lane);
                 const float swr = __shfl_sync(0xffffffffu, pre, (r4 + myrow) & 31);
-                const int row = rs + r4 + myrow;
+                const int row = d.goff + rs + r4 + myrow;   // global vocabulary row
                 if ((lane & 7) == 0 && r4 + myrow < nr) {
                     const float logit = (float)((double)swr * v);
                     if (a.logits) a.logits[row] = logit;
@@ -389,10 +539,18 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                 }
                 const double v = warp_sum_rows4(acc, lane);
                 const float prev = __shfl_sync(0xffffffffu, pre, (r4 + myrow) & 31);
-                const int lr = r4 + myrow, row = rs + lr;
+                const int lr = r4 + myrow, row = rs + lr, grow = d.goff + row;
                 if ((lane & 7) == 0 && lr < nr) {
-                    if (KIND == kQkv) a.qkv[row] = (float)v;
-                    if (KIND == kO) a.h[row] = __fadd_rn(prev, (float)v);
+                    // q and the residual rows go to every rank; k and v are not
+                    // read downstream (the attention is out of scope)
+                    if (KIND == kQkv && grow < a.q_rows)
+                        for (int j = 0; j < a.n_rank; ++j)
+                            reinterpret_cast<float *>(a.xb[j] + XL.q)[grow] = (float)v;
+                    if (KIND == kO) {
+                        const float hv = __fadd_rn(prev, (float)v);
+                        for (int j = 0; j < a.n_rank; ++j)
+                            reinterpret_cast<float *>(a.xb[j] + XL.h)[grow] = hv;
+                    }
                     if (KIND == kGu) cs.tile_s[row - d.r0] = (float)v;   // gate/up tile entry
                 }
             }
@@ -408,8 +566,21 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                 if (__shfl_sync(0xffffffffu, last, 0)) {
                     __threadfence_block();
                     const float av = silu_mul(cs.tile_s[t * 64 + lane], cs.tile_s[t * 64 + 32 + lane]);
-                    const int gt = (d.r0 >> 6) + t;
-                    quantize_block32(av, lane, a.aq + gt * 32, a.asx + gt, a.asumq + gt);
+                    const int gt = ((d.goff + d.r0) >> 6) + t;   // global 32-block of the product
+                    // quantized once (same operations as quantize_block32), stored to every rank
+                    const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av)));
+                    const float dsc = __fdiv_rn(__uint_as_float(amax), 127.0f);
+                    const float id = dsc != 0.0f ? __fdiv_rn(1.0f, dsc) : 0.0f;
+                    const float tq = roundf(__fmul_rn(av, id));
+                    const int q = tq > 127.0f ? 127 : (tq < -127.0f ? -127 : (int)tq);
+                    const int qsum = __reduce_add_sync(0xffffffffu, q);
+                    for (int j = 0; j < a.n_rank; ++j) {
+                        (reinterpret_cast<int8_t *>(a.xb[j] + XL.aq) + gt * 32)[lane] = (int8_t)q;
+                        if (lane == 0) {
+                            reinterpret_cast<float *>(a.xb[j] + XL.asx)[gt] = dsc;
+                            reinterpret_cast<int *>(a.xb[j] + XL.asumq)[gt] = qsum;
+                        }
+                    }
                 }
             }
         }
@@ -436,6 +607,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NP = 4 * a.n_layer + 1;
+    Where w;
+    w.rl = blockIdx.x / a.cta_per_rank;
+    w.rank = a.rank0 + w.rl;
+    w.cb = blockIdx.x % a.cta_per_rank;
+    const PersistXLayout XL = lalb_persist_xlayout(a.n_layer, a.hidden, a.q_rows, a.ffn);
+    const XView own = xview(a, w.rank);
+    const PersistRank &rk = a.rk[w.rl];
 
     if (tid == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -459,11 +637,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             // streaming while the ring is full across a phase boundary.
             int pf_p = 0, pf_j = 0;
             uint32_t pf_g = 0;
-            Phase pf_d = phase_desc(a, 0);
+            Phase pf_d = phase_desc(a, 0, w);
             auto prefetch_to = [&](uint32_t g_end) {
                 for (; pf_g < g_end; ++pf_g, ++pf_j) {
                     while (pf_p < NP && pf_j >= pf_d.nchunks) {
-                        if (++pf_p < NP) pf_d = phase_desc(a, pf_p);
+                        if (++pf_p < NP) pf_d = phase_desc(a, pf_p, w);
                         pf_j = 0;
                     }
                     if (pf_p >= NP) return;
@@ -477,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             prefetch_to(kPrefetchChunks);
             uint32_t g = 0;
             for (int p = 0; p < NP && !dead; ++p) {
-                const Phase d = phase_desc(a, p);
+                const Phase d = phase_desc(a, p, w);
                 for (int j = 0; j < d.nchunks; ++j, ++g) {
                     if (g % kNP != (uint32_t)warp) continue;
                     const int slot = g % kSlots;
@@ -524,9 +702,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     cs.best_r = -1;
     cs.wait_ns = cs.busy_ns = cs.polls = 0;
 
+    // the phase counters grow across tokens: their targets derive from seq
+    const unsigned int seq = *(volatile unsigned int *)own.seq;
+
     for (int p = 0; p < NP; ++p) {
-        const Phase d = phase_desc(a, p);
-        const int NS = d.K >> 5;
+        Phase d;
 
         // ---- every CTA must have finished phase p-1 --------------------------
         if (p > 0) {
@@ -541,18 +721,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     tr[7] = cs.polls;
                     cs.wait_ns = cs.busy_ns = cs.polls = 0;
                 }
-                *abort_s = !grid_arrive_wait(&a.gbar[p - 1], gridDim.x, a.status);
+                grid_arrive(a, own, w.rank, p - 1, seq);
+                d = phase_desc(a, p, w);   // while the arrivals propagate
+                *abort_s = !grid_wait(a, own, p - 1, seq);
                 if (tr) tr[1] = global_ns();
+            } else {
+                d = phase_desc(a, p, w);
             }
             cons_bar();
             if (*abort_s) cs.dead = true;
+        } else {
+            d = phase_desc(a, p, w);
         }
+        const int NS = d.K >> 5;
 
         // ---- the phase's activation in shared memory -------------------------
         if (d.kind == kDown) {
             // 16-byte chunk q of half-block c is stored at chunk q ^ (c & 7):
             // the eight lanes of a 128-bit load phase then hit distinct banks
-            const int4 *src = reinterpret_cast<const int4 *>(a.aq);
+            const int4 *src = reinterpret_cast<const int4 *>(own.aq);
             int4 *dst = reinterpret_cast<int4 *>(xq_s);
 #pragma unroll 4
             for (int i = ct; i < d.K / 16; i += kConsThreads) {
@@ -560,14 +747,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 dst[(c << 3) | ((i & 7) ^ (c & 7))] = __ldcg(src + i);
             }
             for (int i = ct; i < NS; i += kConsThreads) {
-                sx_s[i] = __ldcg(a.asx + i);
-                sq_s[i] = __ldcg(a.asumq + i);
+                sx_s[i] = __ldcg(own.asx + i);
+                sq_s[i] = __ldcg(own.asumq + i);
             }
         } else {
             // one round trip to L2: every thread loads its quads' elements,
             // then the RMS scale (sum of squares in double) and the quantizer
             // work from registers
-            const float *src = d.kind == kO ? a.qkv : ((p == 0) ? a.h_in : a.h);
+            const float *src = d.kind == kO ? own.q : ((p == 0) ? a.h_in : own.h);
             const int quad = ct >> 2, qi = ct & 3;
             float v[kPrepPasses][8];
             double ss = 0.0;
@@ -589,7 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 cons_bar();
                 if (ct == 0) {
                     double t = 0.0;
-                    for (int w = 0; w < kNC; ++w) t += red_s[w];
+                    for (int cw = 0; cw < kNC; ++cw) t += red_s[cw];
                     red_s[kNC] = (double)(float)(1.0 / sqrt(t / (double)d.K + 1e-6));
                 }
                 cons_bar();
@@ -612,11 +799,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         if (ct == 0 && a.trace) a.trace[((size_t)blockIdx.x * NP + p) * kTraceFields + 2] = global_ns();
 
         switch (d.kind) {
-            case kQkv: consume_phase<kQkv>(a, d, g_base, cs); break;
-            case kO: consume_phase<kO>(a, d, g_base, cs); break;
-            case kGu: consume_phase<kGu>(a, d, g_base, cs); break;
-            case kDown: consume_phase<kDown>(a, d, g_base, cs); break;
-            default: consume_phase<kHead>(a, d, g_base, cs); break;
+            case kQkv: consume_phase<kQkv>(a, d, g_base, XL, own, rk, cs); break;
+            case kO: consume_phase<kO>(a, d, g_base, XL, own, rk, cs); break;
+            case kGu: consume_phase<kGu>(a, d, g_base, XL, own, rk, cs); break;
+            case kDown: consume_phase<kDown>(a, d, g_base, XL, own, rk, cs); break;
+            default: consume_phase<kHead>(a, d, g_base, XL, own, rk, cs); break;
         }
         g_base += d.nchunks;
     }
@@ -658,10 +845,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         if (ct == 0) {
             float bv = 0.0f;
             int br = -1;
-            for (int w = 0; w < kNC; ++w) {
-                const int r = besti_s[w];
+            for (int cw = 0; cw < kNC; ++cw) {
+                const int r = besti_s[cw];
                 if (r < 0) continue;
-                const float v = bestv_s[w];
+                const float v = bestv_s[cw];
                 if (br < 0 || v > bv || (v == bv && r < br)) {
                     bv = v;
                     br = r;
@@ -670,17 +857,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             if (br >= 0) {
                 const unsigned long long key = ((unsigned long long)ordered_key(bv) << 32) |
                                                (unsigned long long)(0xFFFFFFFFu - (uint32_t)br);
-                atomicMax(a.best, key);
+                atomicMax(own.best, key);
             }
             __threadfence();
-            const unsigned int t = atomicAdd(a.ticket, 1u);
-            if (t == gridDim.x - 1) {
-                // every CTA is past every barrier: publish and reset for the next token
-                const unsigned long long key = atomicExch(a.best, 0ull);
-                if (a.argmax) *a.argmax = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
-                for (int q = 0; q < NP - 1; ++q) a.gbar[q] = 0;
+            const unsigned int t = atomicAdd(own.ticket, 1u);
+            if (t == (unsigned int)a.cta_per_rank - 1) {
+                // this rank's CTAs are all done: its key goes to every rank,
+                // then the ranks' keys meet (first maximum wins: the key holds
+                // ~row, so equal logits prefer the lower global row)
+                const unsigned long long key = atomicExch(own.best, 0ull);
+                unsigned long long kmax = key;
+                bool ok = true;
+                if (a.n_rank > 1) {
+                    for (int j = 0; j < a.n_rank; ++j) xview(a, j).keys[w.rank] = key;
+                    __threadfence_system();
+                    ok = keys_arrive_wait(a, own, seq);
+                    kmax = 0;
+                    for (int j = 0; j < a.n_rank; ++j) {
+                        const unsigned long long kj = __ldcg(own.keys + j);
+                        kmax = kj > kmax ? kj : kmax;
+                    }
+                }
+                if (a.argmax && w.rl == 0)
+                    *a.argmax = ok && kmax ? (int32_t)(0xFFFFFFFFu - (uint32_t)(kmax & 0xFFFFFFFFull)) : -1;
+                *own.ticket = 0u;
                 __threadfence();
-                atomicExch(a.ticket, 0u);
+                atomicAdd(own.seq, 1u);   // the next token's counter targets
             }
         }
     }
@@ -698,7 +900,7 @@ int lalb_launch_persist(lalb_ctx *ctx, const PersistArgs &a, cudaStream_t stream
         if (st) return st;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ctx->sm_count);
+    cfg.gridDim = dim3(a.cta_per_rank * a.ranks_here);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = stream;

@@ -65,29 +65,84 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &a, int in, int epi,
 int lalb_launch_q8_head(lalb_ctx *ctx, const Q8HeadArgs &a, int in, cudaStream_t stream,
                         bool pdl, int ctas_per_sm);
 
-// One decode token in a single persistent, cooperative kernel.
+// One decode token in a single persistent, cooperative kernel, optionally
+// tensor-parallel over n_rank GPUs.  Every rank holds a contiguous shard of
+// the rows of every matrix (lalb_tp_range) and an exchange buffer with the
+// full activations; a CTA stores its output rows into every rank's buffer
+// (peer memory over NVLink) and arrives on every rank's phase counter.
+constexpr int kPersistMaxRanks = 8;
+
+struct PersistRank {                    // one rank's weight shards (device)
+    const lalb_layer_weights *layers;   // [n_layer] row shards of the 4 matrices
+    const int8_t *lm_w;                 // LM-head row shard [rows][hidden]
+    const float *lm_s;
+};
+
 struct PersistArgs {
     int n_layer, hidden, q_rows, kv_rows, ffn, vocab;
-    const lalb_layer_weights *layers;  // device array [n_layer]
-    const int8_t *lm_w;
-    const float *lm_s;
-    const float *h_in;                  // [hidden]
-    float *h;                           // [hidden] residual stream
-    float *qkv;                         // [q_rows + 2*kv_rows]
-    int8_t *aq;                         // [ffn] quantized SwiGLU product
-    float *asx;                         // [ffn/32]
-    int32_t *asumq;                     // [ffn/32]
-    float *logits;                      // [vocab], nullable
+    int n_rank;                         // ranks in total (1: one GPU holds every row)
+    int rank0, ranks_here;              // the ranks this launch computes, one CTA group each
+    int cta_per_rank;                   // CTAs per rank (equal on every rank)
+    int remote;                         // nonzero: some ranks are other GPUs (system scope)
+    PersistRank rk[kPersistMaxRanks];   // [rank - rank0]
+    unsigned char *xb[kPersistMaxRanks];   // every rank's exchange buffer (peer pointers)
+    const float *h_in;                  // [hidden] token input, same on every rank
+    float *logits;                      // nullable: [vocab] (each rank writes its rows)
     int32_t *argmax;                    // nullable
-    unsigned int *gbar;                 // [4*n_layer] grid-barrier arrival counters (zero)
-    unsigned long long *best;           // argmax key (zero)
-    unsigned int *ticket;               // CTAs done with the LM head (zero)
     unsigned int *status;
-    // nullable: per CTA and phase, the global timer (ns) when the CTA's
-    // consumers finished the phase's work and when they left its grid
-    // barrier: [gridDim.x][n_phase][2]
+    // nullable: per CTA and phase, timeline and counters (lalb_decoder_trace_step)
     unsigned long long *trace;
 };
+
+// Layout of one rank's exchange buffer (byte offsets; identical on every rank).
+struct PersistXLayout {
+    size_t gbar;      // u32 [4*n_layer]: this rank's CTAs done with each phase (monotonic
+                      //   across tokens), then u32 [4*n_layer]: other ranks done (one
+                      //   arrival per rank per phase), then u32: ranks' LM-head keys in
+    size_t seq;       // u32: tokens completed by this rank
+    size_t ticket;    // u32: this rank's CTAs done with the LM head (reset per token)
+    size_t best;      // u64: this rank's argmax key (reset per token)
+    size_t keys;      // u64 [kPersistMaxRanks]: every rank's argmax key for the token
+    size_t h;         // f32 [hidden]: residual stream
+    size_t q;         // f32 [q_rows]
+    size_t aq;        // i8  [ffn]: quantized SwiGLU product
+    size_t asx;       // f32 [ffn/32]
+    size_t asumq;     // i32 [ffn/32]
+    size_t total;
+};
+__host__ __device__ inline PersistXLayout lalb_persist_xlayout(int n_layer, int hidden, int q_rows,
+                                                               int ffn) {
+    auto up = [](size_t v) { return (v + 127) / 128 * 128; };
+    PersistXLayout L;
+    L.gbar = 0;
+    L.seq = up((size_t)(8 * n_layer + 1) * 4);
+    L.ticket = L.seq + 4;
+    L.best = L.seq + 8;
+    L.keys = L.seq + 128;
+    L.h = L.keys + 128;
+    L.q = L.h + up((size_t)hidden * 4);
+    L.aq = L.q + up((size_t)q_rows * 4);
+    L.asx = L.aq + up((size_t)ffn);
+    L.asumq = L.asx + up((size_t)(ffn / 32) * 4);
+    L.total = L.asumq + up((size_t)(ffn / 32) * 4);
+    return L;
+}
+
+// Rows [row0, row1) of matrix `which` that rank r of n holds: 0 qkv, 1 o,
+// 2 gate/up (whole 64-row gate/up tiles), 3 down, 4 LM head.
+__host__ __device__ inline void lalb_tp_range(const lalb_decoder_cfg &c, int which, int n, int r,
+                                              int *row0, int *row1) {
+    int units, unit = 1;
+    switch (which) {
+        case 0: units = c.q_rows + 2 * c.kv_rows; break;
+        case 1: case 3: units = c.hidden; break;
+        case 2: units = 2 * c.ffn / 64; unit = 64; break;
+        default: units = c.vocab; break;
+    }
+    // 32-bit: units < 2^24 and r <= 8 (the decoder checks the shapes)
+    *row0 = (int)((unsigned)r * (unsigned)units / (unsigned)n) * unit;
+    *row1 = (int)((unsigned)(r + 1) * (unsigned)units / (unsigned)n) * unit;
+}
 
 // Limits of the persistent kernel (checked by the decoder).
 constexpr int kPersistMaxHidden = 4096;   // K of qkv, gate/up, head; q_rows
