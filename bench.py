@@ -194,6 +194,108 @@ def gemv_standalone(ctx, torch, stream, reps=200, ncopies=8):
             "gbs": round(nbytes / us / 1e3, 1)}
 
 
+STE = dict(n_layer=8, d=448, ffn=1792, vocab=32768, rows=1024)
+
+
+def run_ste_case(args):
+    """The seed STE model's forward matmuls (8 layers, d=448, FFN 1792, vocab
+    32768) on X 1024 x 448 fp32: per-element CORE/BINARY/PRUNE weights drawn
+    10/50/40, packed as int8 codes with a per-row scale; every matmul on the
+    tcgen05 tf32-part GEMM.  Prints its own JSON line (not the decode line)."""
+    import torch
+
+    import lalmodel_b200 as lb
+
+    c = STE
+    ctx = lb.Context(0)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(55)
+    M, d, f = c["rows"], c["d"], c["ffn"]
+    shapes = [(3 * d, d), (d, d), (f, d), (d, f)] * c["n_layer"] + [(c["vocab"], d)]
+    layers = []
+    for i, (rows, K) in enumerate(shapes):
+        W = torch.empty((rows, K), dtype=torch.float32, device="cuda")
+        ctx.fill_normal(W, seed=900 + i, sigma=0.02)
+        u = torch.rand((rows, K), generator=gen, device="cuda")
+        state = torch.where(u < 0.10, 0, torch.where(u < 0.60, 1, 2)).to(torch.uint8)
+        codes, srow = lb.LogicLayer.pack(ctx, W, state)
+        bias = torch.zeros(rows, dtype=torch.float32, device="cuda")
+        layers.append(lb.LogicLayer(ctx, codes, srow, bias, max_rows=M))
+        del W, u, state
+    X = torch.empty((M, d), dtype=torch.float32, device="cuda")
+    X2 = torch.empty((M, f), dtype=torch.float32, device="cuda")
+    ctx.fill_normal(X, seed=7, sigma=1.0)
+    ctx.fill_normal(X2, seed=8, sigma=1.0)
+    outs = [torch.empty((M, rows), dtype=torch.float32, device="cuda") for rows, _ in shapes]
+    flops = sum(2.0 * M * rows * K for rows, K in shapes)
+    stream = torch.cuda.Stream()
+
+    def step():
+        for L, (rows, K), Y in zip(layers, shapes, outs):
+            L.forward(X if K == d else X2, Y)
+
+    with torch.cuda.stream(stream):
+        step()   # first calls set kernel attributes outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    tflops = flops / (ms * 1e-3) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            bf16 = float(json.load(fh)["bf16_tflops"])
+        kind = "measured bf16 / 2 (tf32 runs at half the bf16 rate)"
+    except Exception:
+        bf16, kind = 1590.0, "fallback bf16 / 2"
+    tf32_peak = bf16 / 2
+    # the CPU port (the oracle's OpenMP restatement of the per-element forward)
+    # on a bounded sample: the first layer's qkv over 64 rows, repeated for
+    # ~cpu_seconds, scaled to the step's flops
+    cpu = None
+    if not args.no_cpu:
+        O = _cpu_lib()
+        codes, srow, bias = (t.cpu().numpy() for t in layers[0]._keep)
+        xs = X[:64].cpu().numpy()
+        rows, K = shapes[0]
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < args.cpu_seconds:
+            O.logic_forward(codes, srow, bias, xs)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        cpu_tflops = 2.0 * 64 * rows * K / dt / 1e12
+        cpu = {"value": round(cpu_tflops, 4), "unit": "TFLOP/s", "cores": os.cpu_count(),
+               "kind": "port",
+               "sample": "%d x layer-0 qkv (%dx%d codes) over 64 rows, %.2f ms each; step time "
+                         "at this rate %.1f ms" % (n, rows, K, dt * 1e3, flops / (cpu_tflops * 1e12) * 1e3)}
+    line = {"case": "seed-ste-forward", "metric": "seed STE forward matmuls TFLOPS",
+            "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "dtype": "fp32 as tf32 parts (hi+lo activations x int8 codes), fp32 accumulate",
+            "data": "synthetic: seeded N(0,0.02) weights, per-element states 10/50/40, X N(0,1)",
+            "config": {"workload": "seed STE forward: 8 x (qkv 1344x448, o 448x448, fc 1792x448, "
+                                   "down 448x1792) + LM head 32768x448 on X 1024x448",
+                       "flops_per_step": flops, "gemm_launches_per_step": len(shapes)},
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
+                         "tensor_work": round(2 * tflops, 2), "peak": tf32_peak,
+                         "peak_kind": kind, "unit": "TFLOP/s",
+                         "frac": round(2 * tflops / tf32_peak, 4)},
+            "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+    for L in layers:
+        L.close()
+    ctx.close()
+
+
 def run_gemv_case(args):
     """Only the single-GEMV workload (4 rotating copies, 153 MB > L2): a small
     case for profiler captures, not a bench line."""
@@ -512,8 +614,9 @@ def main():
                     help="smaller LM head: only for profiling captures, not a bench line")
     ap.add_argument("--path", default="auto", choices=["auto", "kernels", "persistent"],
                     help="decoder path: one persistent kernel per token, or one kernel per matvec")
-    ap.add_argument("--case", default="decode", choices=["decode", "gemv"],
-                    help="gemv: only the single 18944x3584 GEMV, for profiler captures")
+    ap.add_argument("--case", default="decode", choices=["decode", "gemv", "ste"],
+                    help="gemv: only the single 18944x3584 GEMV, for profiler captures; "
+                         "ste: the seed STE model's forward matmuls (its own line)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -526,6 +629,8 @@ def main():
         run_reference(args, rank, world)
     elif args.case == "gemv":
         run_gemv_case(args)
+    elif args.case == "ste":
+        run_ste_case(args)
     else:
         run_gpu(args, rank, world, local_rank)
 

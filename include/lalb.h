@@ -278,6 +278,42 @@ LALB_API int lalb_decoder_path(const lalb_decoder *dec);
 LALB_API int lalb_decoder_launches_per_step(const lalb_decoder *dec);
 LALB_API int lalb_decoder_destroy(lalb_decoder *dec);
 
+/* ---- the seed STE model's forward matmuls (tensor cores) -----------------
+ * A BinLayer (runtime/lal_runtime.h:171-197) with one CORE (0) / BINARY (1)
+ * / PRUNE (2) state per output row.  Built like bin_layer_init_logic
+ * (runtime/lal_runtime.c:1567-1676) from W [out][in] fp32 (row-major),
+ * bias [out] (nullable) and mask [out], all device buffers; alpha_repack = 1
+ * recomputes alpha as bin_layer_repack (:1703-1766) does.  max_rows bounds
+ * the M of a forward (the layer owns its workspace).  in_dim % 32 == 0. */
+typedef struct lalb_binlayer lalb_binlayer;
+LALB_API int lalb_binlayer_create(lalb_ctx *ctx, const float *W, const float *bias,
+                                  const uint8_t *mask, int in_dim, int out_dim,
+                                  int alpha_repack, float binary_scale, int max_rows,
+                                  lalb_binlayer **out);
+/* Y [M][out] = the layer over the M rows of X [M][in]: mode 0 bin_forward
+ * (:1852-1938, logic-mask path), mode 1 bin_forward_pure_float (:543-582).
+ * fp32 operands as sums of tf32 parts on tcgen05; within 1e-5 of the exact
+ * products. */
+LALB_API int lalb_binlayer_forward(lalb_binlayer *bl, const float *X, int M, float *Y,
+                                   int mode, lalb_stream stream);
+LALB_API int lalb_binlayer_alpha(lalb_binlayer *bl, float *alpha, lalb_stream stream);
+LALB_API int lalb_binlayer_destroy(lalb_binlayer *bl);
+
+/* Per-element states (state [rows][K]: 0 CORE, 1 BINARY, 2 PRUNE) packed as
+ * int8 codes with one fp32 scale per row: CORE weights quantized to +-127,
+ * BINARY weights +-(row's mean |w| in the same scale), PRUNE 0. */
+LALB_API int lalb_logic_pack(lalb_ctx *ctx, const float *W, const uint8_t *state, int rows,
+                             int K, int8_t *codes, float *srow, lalb_stream stream);
+/* Y [M][rows] = srow * (X . codes^T) + bias; bias nullable; the layer keeps
+ * pointers to srow and bias. */
+typedef struct lalb_logic_layer lalb_logic_layer;
+LALB_API int lalb_logic_layer_create(lalb_ctx *ctx, const int8_t *codes, const float *srow,
+                                     const float *bias, int rows, int K, int max_rows,
+                                     lalb_logic_layer **out);
+LALB_API int lalb_logic_layer_forward(lalb_logic_layer *L, const float *X, int M, float *Y,
+                                      lalb_stream stream);
+LALB_API int lalb_logic_layer_destroy(lalb_logic_layer *L);
+
 #ifdef __cplusplus
 }
 #endif

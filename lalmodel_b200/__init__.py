@@ -289,6 +289,86 @@ class Decoder:
             pass
 
 
+class BinLayer:
+    """The seed STE model's logic-masked layer on tensor cores (include/lalb.h,
+    lalb_binlayer_*): W [out][in] fp32, bias [out] or None, mask [out] uint8
+    (0 CORE, 1 BINARY, 2 PRUNE), all CUDA tensors."""
+
+    def __init__(self, ctx, W, bias, mask, alpha_repack=False, binary_scale=0.25, max_rows=1024):
+        self.ctx = ctx
+        self.out_dim, self.in_dim = W.shape
+        h = ctypes.c_void_p()
+        ctx._call("lalb_binlayer_create", ctx.h, _p(W), _p(bias), _p(mask), self.in_dim,
+                  self.out_dim, int(alpha_repack), ctypes.c_float(binary_scale), max_rows,
+                  ctypes.byref(h))
+        self.h = h
+
+    def forward(self, X, mode=0, Y=None):
+        """mode 0: bin_forward; mode 1: bin_forward_pure_float."""
+        M = X.shape[0]
+        if Y is None:
+            Y = torch.empty((M, self.out_dim), dtype=torch.float32, device=X.device)
+        self.ctx._call("lalb_binlayer_forward", self.h, _p(X), M, _p(Y), mode, _stream())
+        return Y
+
+    def alpha(self):
+        a = torch.empty(self.out_dim, dtype=torch.float32, device="cuda")
+        self.ctx._call("lalb_binlayer_alpha", self.h, _p(a), _stream())
+        return a
+
+    def close(self):
+        if getattr(self, "h", None):
+            _abi.lib().lalb_binlayer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class LogicLayer:
+    """Per-element CORE/BINARY/PRUNE weights as int8 codes with a per-row
+    scale (lalb_logic_*).  The layer keeps references to srow and bias."""
+
+    def __init__(self, ctx, codes, srow, bias=None, max_rows=1024):
+        self.ctx = ctx
+        self.rows, self.K = codes.shape
+        self._keep = (codes, srow, bias)
+        h = ctypes.c_void_p()
+        ctx._call("lalb_logic_layer_create", ctx.h, _p(codes), _p(srow), _p(bias), self.rows,
+                  self.K, max_rows, ctypes.byref(h))
+        self.h = h
+
+    @staticmethod
+    def pack(ctx, W, state):
+        rows, K = W.shape
+        codes = torch.empty((rows, K), dtype=torch.int8, device=W.device)
+        srow = torch.empty(rows, dtype=torch.float32, device=W.device)
+        ctx._call("lalb_logic_pack", ctx.h, _p(W), _p(state), rows, K, _p(codes), _p(srow),
+                  _stream())
+        return codes, srow
+
+    def forward(self, X, Y=None):
+        M = X.shape[0]
+        if Y is None:
+            Y = torch.empty((M, self.rows), dtype=torch.float32, device=X.device)
+        self.ctx._call("lalb_logic_layer_forward", self.h, _p(X), M, _p(Y), _stream())
+        return Y
+
+    def close(self):
+        if getattr(self, "h", None):
+            _abi.lib().lalb_logic_layer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 _default_ctx = {}
 
 

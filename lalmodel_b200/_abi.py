@@ -59,6 +59,15 @@ SIGNATURES = {
     "lalb_decoder_ipc_handle": (c_int, [P, P]),
     "lalb_decoder_connect": (c_int, [P, P]),
     "lalb_decoder_set_path": (c_int, [P, c_int]),
+    "lalb_binlayer_create": (c_int, [P, P, P, P, c_int, c_int, c_int, ctypes.c_float, c_int,
+                                     ctypes.POINTER(P)]),
+    "lalb_binlayer_forward": (c_int, [P, P, c_int, P, c_int, P]),
+    "lalb_binlayer_alpha": (c_int, [P, P, P]),
+    "lalb_binlayer_destroy": (c_int, [P]),
+    "lalb_logic_pack": (c_int, [P, P, P, c_int, c_int, P, P, P]),
+    "lalb_logic_layer_create": (c_int, [P, P, P, P, c_int, c_int, c_int, ctypes.POINTER(P)]),
+    "lalb_logic_layer_forward": (c_int, [P, P, c_int, P, P]),
+    "lalb_logic_layer_destroy": (c_int, [P]),
     "lalb_decoder_path": (c_int, [P]),
     "lalb_decoder_launches_per_step": (c_int, [P]),
     "lalb_decoder_destroy": (c_int, [P]),

@@ -1,0 +1,332 @@
+// lalb_tc_gemm.cu -- tcgen05 (5th-generation tensor core) GEMM with fp32
+// operands carried exactly as sums of tf32 parts.
+//
+//   Y[m][n] = rowscale[m] * colscale[n] * sum_k A[m][k] * B[n][k] + bias[n]
+//
+// A (activations, [M][K]) and B (weights, [N][K]) are row-major fp32 in HBM,
+// both K-major.  Each is given as one or two tf32 parts (x = hi + lo, each
+// part exactly representable in tf32, so |x - hi - lo| <= 2^-22 |x|); the
+// kernel accumulates hi*hi + lo*hi (+ hi*lo when B has two parts) in fp32 in
+// TMEM.  This is the seed STE model's forward (BinLayer) on tensor cores:
+// the reference computes it in fp32 on the CPU (runtime/lal_runtime.c
+// bin_forward :1852-1938, bin_forward_pure_float :543-582).
+//
+// One CTA per 128 x 128 output tile, 6 warps:
+//   warp 0  TMA producer: 2-D tiled bulk tensor copies (128-byte swizzle)
+//           of every part's 128 x 32 (A) and 128 x 32 (B) fp32 tiles into a
+//           3-stage ring, completion on a full mbarrier per stage;
+//   warp 1  allocates all 512 TMEM columns (4 accumulators of 128) and
+//           issues tcgen05.mma (kind::tf32, M=128, N=128, K=8 per
+//           instruction) from one lane, K-block kb into accumulator kb % 4;
+//           a tcgen05.commit per stage frees the stage, a final one signals
+//           the accumulators;
+//   warps 2-5  epilogue: each reads its 32 TMEM lanes (= rows) 32 columns at
+//           a time from every accumulator (tcgen05.ld 32x32b.x32), adds
+//           them, transposes through shared memory and writes 128-byte row
+//           segments with the scales and bias.
+// Every wait is bounded; on expiry the kernel raises the status word and
+// still commits, drains and frees its TMEM.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "lalb_internal.cuh"
+#include "lalb_tc_gemm.cuh"
+
+using namespace lalb;
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32;     // BK fp32 = 128 B: one 128-byte swizzle row
+constexpr int kStagesTc = 3;
+// K-blocks go round-robin to kAccs accumulators (BN TMEM columns each), so
+// each fp32 accumulation chain in the tensor core is kAccs times shorter;
+// the epilogue adds them
+constexpr int kAccs = 4;
+constexpr int kTmemCols = BN * kAccs;           // 512: the whole TMEM of the SM
+constexpr int kTcThreads = 192;
+constexpr uint32_t kATile = BM * BK * 4;       // 16 KB
+constexpr uint32_t kBTile = BN * BK * 4;       // 16 KB
+constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;   // up to 2 parts each
+constexpr uint32_t kEpiBytes = 4 * 32 * 33 * 4;             // per-warp 32x32 transpose
+constexpr uint32_t kTcSmem = 1024 /* alignment slack */ + kStagesTc * kStageBytes + kEpiBytes + 256;
+
+// K-major operand tile with 128-byte swizzle (the TMA layout): rows of
+// 128 bytes, 8-row groups 1024 bytes apart.  Descriptor fields: start
+// address >> 4, leading byte offset 1 (unused for this layout), stride byte
+// offset 1024 >> 4, version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::tf32 instruction descriptor: fp32 accumulator, tf32 A and B, both
+// K-major, M = 128, N = BN.
+constexpr uint32_t kIdescTf32 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdescTf32), "r"(accumulate)
+        : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes (lane = row).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+          "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+          "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+struct TcArgs {
+    int M, N, K;
+    int a_parts, b_parts;       // 1 or 2 each
+    float *Y;                   // [M][N]
+    const float *rowscale;      // [M] or null (1)
+    const float *colscale;      // [N] or null (1)
+    const float *bias;          // [N] or null (0)
+    unsigned int *status;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_tf32_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
+                        const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1,
+                        const TcArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled tiles
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    uint8_t *stages = smem;
+    float *epi = reinterpret_cast<float *>(smem + kStagesTc * kStageBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStagesTc * kStageBytes + kEpiBytes);
+    uint64_t *empty = full + kStagesTc;
+    uint64_t *acc_full = empty + kStagesTc;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int nk = a.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStagesTc; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    const uint32_t stage_tx = (uint32_t)(a.a_parts * kATile + a.b_parts * kBTile);
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer ----
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % kStagesTc;
+                const uint32_t use = kb / kStagesTc;
+                if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u, a.status)) break;
+                uint8_t *st = stages + (size_t)s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], stage_tx);
+                tma_load_2d(st, &mA0, kb * BK, m0, &full[s]);
+                if (a.a_parts > 1) tma_load_2d(st + kATile, &mA1, kb * BK, m0, &full[s]);
+                tma_load_2d(st + 2 * kATile, &mB0, kb * BK, n0, &full[s]);
+                if (a.b_parts > 1) tma_load_2d(st + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer ----
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % kStagesTc;
+                if (!mbar_wait_bounded(&full[s], (uint32_t)(kb / kStagesTc) & 1u, a.status)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t st = smem_u32(stages + (size_t)s * kStageBytes);
+                const uint32_t a0 = st, a1 = st + kATile, b0 = st + 2 * kATile, b1 = b0 + kBTile;
+                const uint32_t td = tmem + (uint32_t)((kb % kAccs) * BN);
+                uint32_t acc = kb >= kAccs;   // the first block of an accumulator overwrites it
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {   // 8 tf32 = 32 bytes per instruction
+                    const uint32_t ko = k * 32;
+                    mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), acc);
+                    acc = 1;
+                    if (a.a_parts > 1)
+                        mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), 1);
+                    if (a.b_parts > 1)
+                        mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), 1);
+                }
+                mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
+            }
+            mma_commit(acc_full);        // arrives when every issued MMA has completed
+        }
+    } else {
+        // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
+        const int q = warp & 3;
+        float *st = epi + (size_t)(warp - 2) * 32 * 33;
+        mbar_wait_bounded(acc_full, 0, a.status);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int nacc = nk < kAccs ? nk : kAccs;
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            float sum[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+            for (int ai = 0; ai < nacc; ++ai) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ai * BN + c0), r);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+            }
+            // lane holds row q*32 + lane, columns c0..c0+31
+#pragma unroll
+            for (int j = 0; j < 32; ++j) st[lane * 33 + j] = sum[j];
+            __syncwarp();
+            const int n = n0 + c0 + lane;
+            const bool ncol = n < a.N;
+            const float cs = ncol && a.colscale ? a.colscale[n] : 1.0f;
+            const float b = ncol && a.bias ? a.bias[n] : 0.0f;
+            for (int j = 0; j < 32; ++j) {
+                const int m = m0 + q * 32 + j;
+                if (m < a.M && ncol) {
+                    const float rs = a.rowscale ? a.rowscale[m] : 1.0f;
+                    a.Y[(size_t)m * a.N + n] = __fadd_rn(__fmul_rn(__fmul_rn(st[j * 33 + lane], rs), cs), b);
+                }
+            }
+            __syncwarp();
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+    __syncthreads();
+    if (warp == 1) {
+        // every MMA has completed before the columns go back (bounded)
+        if (lane == 0) mbar_wait_bounded(acc_full, 0, a.status);
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+// fp32 -> (hi, lo) tf32 parts: hi = tf32(x) (round to nearest, ties away),
+// lo = tf32(x - hi).
+__global__ void split_tf32_kernel(const float *__restrict__ x, float *__restrict__ hi,
+                                  float *__restrict__ lo, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        uint32_t h, l;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+        const float r = __fsub_rn(v, __uint_as_float(h));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+        hi[i] = __uint_as_float(h);
+        if (lo) lo[i] = __uint_as_float(l);
+    }
+}
+
+// ---- tensor maps ----------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Row-major fp32 [rows][K], box 32 (K) x box_rows, 128-byte swizzle; rows
+// past the end read as zeros.
+int make_map(lalb_ctx *ctx, CUtensorMap *m, const float *base, int rows, int K, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return lalb_fail(ctx, LALB_ERR_CUDA, "tc_gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
+                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return lalb_fail(ctx, LALB_ERR_CUDA, "tc_gemm: tensor map encode (%d)", (int)r);
+    return LALB_OK;
+}
+
+}  // namespace
+
+int lalb_split_tf32(lalb_ctx *ctx, const float *x, float *hi, float *lo, size_t n, cudaStream_t s) {
+    if (n == 0) return LALB_OK;
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
+    split_tf32_kernel<<<blocks, 256, 0, s>>>(x, hi, lo, n);
+    LALB_LAUNCH_CHECK(ctx, "split_tf32_kernel");
+    return LALB_OK;
+}
+
+int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
+    if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.K % BK || !p.a_hi || !p.b_hi || !p.Y)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "tc_gemm: M, N > 0, K a multiple of %d", BK);
+    if (((uintptr_t)p.a_hi | (uintptr_t)p.a_lo | (uintptr_t)p.b_hi | (uintptr_t)p.b_lo) & 15u)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "tc_gemm: operands must be 16-byte aligned");
+    CUtensorMap mA0, mA1, mB0, mB1;
+    int st;
+    if ((st = make_map(ctx, &mA0, p.a_hi, p.M, p.K, BM))) return st;
+    if ((st = make_map(ctx, &mA1, p.a_lo ? p.a_lo : p.a_hi, p.M, p.K, BM))) return st;
+    if ((st = make_map(ctx, &mB0, p.b_hi, p.N, p.K, BN))) return st;
+    if ((st = make_map(ctx, &mB1, p.b_lo ? p.b_lo : p.b_hi, p.N, p.K, BN))) return st;
+    if ((st = lalb_set_smem_attr(ctx, (const void *)tc_gemm_tf32_kernel, (int)kTcSmem))) return st;
+    TcArgs a;
+    a.M = p.M;
+    a.N = p.N;
+    a.K = p.K;
+    a.a_parts = p.a_lo ? 2 : 1;
+    a.b_parts = p.b_lo ? 2 : 1;
+    a.Y = p.Y;
+    a.rowscale = p.rowscale;
+    a.colscale = p.colscale;
+    a.bias = p.bias;
+    a.status = &ctx->scratch->status;
+    const dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+    tc_gemm_tf32_kernel<<<grid, kTcThreads, kTcSmem, s>>>(mA0, mA1, mB0, mB1, a);
+    LALB_LAUNCH_CHECK(ctx, "tc_gemm_tf32_kernel");
+    return LALB_OK;
+}

@@ -412,3 +412,60 @@ void lalb_o_logic_forward(const int8_t *codes, const float *srow,
         }
     }
 }
+
+/* bin_layer_init_logic (runtime/lal_runtime.c:1567-1676): alpha = mean |w|
+ * for BINARY rows, 0 for CORE and PRUNE; PRUNE rows lose their bias.
+ * bin_layer_repack (:1703-1766): alpha = mean |w| for every row.
+ * bin_forward logic path (:1852-1938): K = mean |x|; CORE
+ * (w.x) * min(1/(alpha+1e-8), 5) * K + b; BINARY (sign(w).x) * alpha * K *
+ * binary_scale + b with sign(w) = +1 iff w > 0; PRUNE 0.
+ * bin_forward_pure_float (:543-582): CORE w.x + b; BINARY
+ * b + (w.x) * binary_scale; PRUNE 0. */
+void lalb_o_binlayer_forward(const float *W, const float *bias,
+                             const uint8_t *mask, int in_dim, int out_dim,
+                             const float *X, int M, float *Y, int mode,
+                             int repack, float binary_scale, float *alpha_out) {
+    float *alpha = (float *)malloc(sizeof(float) * (size_t)out_dim);
+    for (int j = 0; j < out_dim; j++) {
+        const float *w = W + (size_t)j * in_dim;
+        double s = 0.0;
+        for (int i = 0; i < in_dim; i++) s += fabs((double)w[i]);
+        alpha[j] = (mask[j] == 1 || repack) ? (float)(s / in_dim) : 0.0f;
+        if (alpha_out) alpha_out[j] = alpha[j];
+    }
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; m++) {
+        const float *x = X + (size_t)m * in_dim;
+        double ks = 0.0;
+        for (int i = 0; i < in_dim; i++) ks += fabs((double)x[i]);
+        const double K = ks / in_dim;
+        for (int j = 0; j < out_dim; j++) {
+            const float *w = W + (size_t)j * in_dim;
+            const uint8_t st = mask[j];
+            const double b = (bias && st != 2) ? (double)bias[j] : 0.0;
+            double y = 0.0;
+            if (st == 0) {
+                double d = 0.0;
+                for (int i = 0; i < in_dim; i++) d += (double)w[i] * (double)x[i];
+                if (mode == 0) {
+                    double gain = 1.0 / ((double)alpha[j] + 1e-8);
+                    if (gain > 5.0) gain = 5.0;
+                    y = d * gain * K + b;
+                } else {
+                    y = d + b;
+                }
+            } else if (st == 1) {
+                double d = 0.0;
+                if (mode == 0) {
+                    for (int i = 0; i < in_dim; i++) d += (w[i] > 0.0f ? 1.0 : -1.0) * (double)x[i];
+                    y = d * (double)alpha[j] * K * (double)binary_scale + b;
+                } else {
+                    for (int i = 0; i < in_dim; i++) d += (double)w[i] * (double)x[i];
+                    y = b + d * (double)binary_scale;
+                }
+            }
+            Y[(size_t)m * out_dim + j] = (float)y;
+        }
+    }
+    free(alpha);
+}

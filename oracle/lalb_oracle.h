@@ -110,6 +110,18 @@ void lalb_o_logic_forward(const int8_t *codes, const float *srow,
                           const float *bias, int rows, int K, const float *X,
                           int M, float *Y);
 
+/* The reference's logic-masked BinLayer over M input rows, computed in
+ * double and rounded once per output: mode 0 bin_forward
+ * (runtime/lal_runtime.c:1852-1938), mode 1 bin_forward_pure_float
+ * (:543-582); alpha as bin_layer_init_logic (:1567-1676) leaves it, or, with
+ * repack, as bin_layer_repack (:1703-1766) recomputes it.  W [out][in],
+ * bias [out] (nullable), mask [out], X [M][in] -> Y [M][out]; alpha_out
+ * [out] nullable. */
+void lalb_o_binlayer_forward(const float *W, const float *bias,
+                             const uint8_t *mask, int in_dim, int out_dim,
+                             const float *X, int M, float *Y, int mode,
+                             int repack, float binary_scale, float *alpha_out);
+
 /* --- AVX2 + OpenMP CPU baseline (same integer results as the scalar code) - */
 int  lalb_cpu_threads(void);
 void lalb_cpu_quantize_act(const float *x, int M, int K, int8_t *xq, float *sx,

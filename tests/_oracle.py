@@ -32,6 +32,8 @@ _SIG = {
     "lalb_o_logic_state": (None, [c_u64, c_size_t, c_float, c_float, P]),
     "lalb_o_logic_pack": (None, [P, P, c_int, c_int, P, P]),
     "lalb_o_logic_forward": (None, [P, P, P, c_int, c_int, P, c_int, P]),
+    "lalb_o_binlayer_forward": (None, [P, P, P, c_int, c_int, P, c_int, P, c_int, c_int,
+                                       c_float, P]),
     "lalb_cpu_threads": (c_int, []),
     "lalb_cpu_quantize_act": (None, [P, c_int, c_int, P, P, P]),
     "lalb_cpu_q4k_gemv": (None, [P, c_int, c_int, P, P, P, P]),
@@ -168,3 +170,45 @@ def normwise_rel_err(a, b):
     b = np.asarray(b, np.float64)
     den = np.max(np.abs(b))
     return float(np.max(np.abs(a - b)) / (den if den > 0 else 1.0))
+
+
+def binlayer_forward(W, bias, mask, X, mode, repack=False, binary_scale=0.25):
+    """The reference's logic-masked BinLayer forward (double, one rounding)."""
+    W = np.ascontiguousarray(W, np.float32)
+    X = np.ascontiguousarray(X, np.float32)
+    mask = np.ascontiguousarray(mask, np.uint8)
+    out_dim, in_dim = W.shape
+    M = X.shape[0]
+    Y = np.zeros((M, out_dim), np.float32)
+    alpha = np.zeros(out_dim, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().lalb_o_binlayer_forward(_p(W), _p(b), _p(mask), in_dim, out_dim, _p(X), M, _p(Y), mode,
+                                int(repack), binary_scale, _p(alpha))
+    return Y, alpha
+
+
+def logic_state(seed, n, p_core, p_binary):
+    st = np.zeros(n, np.uint8)
+    lib().lalb_o_logic_state(seed, n, p_core, p_binary, _p(st))
+    return st
+
+
+def logic_pack(W, state):
+    W = np.ascontiguousarray(W, np.float32)
+    rows, K = W.shape
+    codes = np.zeros((rows, K), np.int8)
+    srow = np.zeros(rows, np.float32)
+    lib().lalb_o_logic_pack(_p(W), _p(np.ascontiguousarray(state, np.uint8)), rows, K, _p(codes),
+                          _p(srow))
+    return codes, srow
+
+
+def logic_forward(codes, srow, bias, X):
+    rows, K = codes.shape
+    X = np.ascontiguousarray(X, np.float32)
+    M = X.shape[0]
+    Y = np.zeros((M, rows), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().lalb_o_logic_forward(_p(np.ascontiguousarray(codes)), _p(srow), _p(b), rows, K, _p(X), M,
+                             _p(Y))
+    return Y

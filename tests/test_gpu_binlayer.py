@@ -1,0 +1,89 @@
+"""The seed STE model's forward matmuls on tensor cores (tcgen05, tf32 parts)
+against the reference's goldens and the oracle.  Tolerance: 1e-5 normwise
+(max |diff| / max |ref|) for every fp32 output; PRUNE rows exactly 0; the
+per-element codes and row scales bit-exact."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import _oracle as O
+import lalmodel_b200 as lb
+from test_gpu_kernels import dev, host
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+TOL = 1e-5
+
+
+@pytest.mark.parametrize("ci", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("repack", [0, 1])
+def test_binlayer_matches_reference_goldens(ctx, ci, mode, repack):
+    g = np.load(os.path.join(GOLD, "binlayer_ref.npz"))
+    W, b, mask, X = (g[f"bl{ci}_{k}"] for k in ("W", "b", "mask", "X"))
+    bl = lb.BinLayer(ctx, dev(W), dev(b), dev(mask), alpha_repack=bool(repack), max_rows=64)
+    Y = host(bl.forward(dev(X), mode=mode))
+    ref = g[f"bl{ci}_m{mode}_r{repack}_Y"]
+    assert O.normwise_rel_err(Y, ref) < TOL
+    np.testing.assert_allclose(host(bl.alpha()), g[f"bl{ci}_m{mode}_r{repack}_alpha"], rtol=2e-6, atol=0)
+    assert np.all(Y[:, mask == 2] == 0.0)
+    bl.close()
+
+
+def test_binlayer_rejects_unaligned_in_dim(ctx):
+    g = np.load(os.path.join(GOLD, "binlayer_ref.npz"))
+    W, b, mask = (g[f"bl2_{k}"] for k in ("W", "b", "mask"))   # in = 100
+    with pytest.raises(lb.LalbError) as e:
+        lb.BinLayer(ctx, dev(W), dev(b), dev(mask))
+    assert e.value.status == -4
+
+
+# the seed model's phase-0 shapes (d = 448, FFN 1792, vocab 32768), X rows 1024
+SHAPES = [(448, 1344, 1024), (448, 448, 1024), (448, 1792, 1024), (1792, 448, 1024),
+          (448, 32768, 96), (448, 300, 100)]
+
+
+@pytest.mark.parametrize("in_dim,out_dim,M", SHAPES)
+@pytest.mark.parametrize("mode", [0, 1])
+def test_binlayer_phase0_shapes_match_oracle(ctx, in_dim, out_dim, M, mode):
+    rng = np.random.default_rng(in_dim * 7 + out_dim + M)
+    W = O.normal(out_dim * in_dim, seed=out_dim, sigma=0.02).reshape(out_dim, in_dim)
+    b = O.normal(out_dim, seed=out_dim + 1, sigma=0.01)
+    mask = rng.choice(np.array([0, 1, 2], np.uint8), size=out_dim, p=[0.15, 0.60, 0.25])
+    X = O.normal(M * in_dim, seed=M + 3).reshape(M, in_dim)
+    ref, _ = O.binlayer_forward(W, b, mask, X, mode, repack=True)
+    bl = lb.BinLayer(ctx, dev(W), dev(b), dev(mask), alpha_repack=True, max_rows=M)
+    Y = host(bl.forward(dev(X), mode=mode))
+    assert O.normwise_rel_err(Y, ref) < TOL
+    assert np.all(Y[:, mask == 2] == 0.0)
+    bl.close()
+
+
+@pytest.mark.parametrize("rows,K,M", [(1344, 448, 1024), (448, 1792, 1024), (32768, 448, 64),
+                                      (200, 64, 130)])
+def test_logic_codes_pack_and_forward_match_oracle(ctx, rows, K, M):
+    W = O.normal(rows * K, seed=rows + K, sigma=0.02).reshape(rows, K)
+    st = O.logic_state(rows * 31 + K, rows * K, 0.10, 0.50).reshape(rows, K)
+    codes, srow = O.logic_pack(W, st)
+    gcodes, gsrow = lb.LogicLayer.pack(ctx, dev(W), dev(st))
+    assert np.array_equal(host(gcodes), codes)
+    assert np.array_equal(host(gsrow).view(np.uint32), srow.view(np.uint32))
+    bias = O.normal(rows, seed=5, sigma=0.01)
+    X = O.normal(M * K, seed=M).reshape(M, K)
+    ref = O.logic_forward(codes, srow, bias, X)
+    L = lb.LogicLayer(ctx, gcodes, gsrow, dev(bias), max_rows=M)
+    Y = host(L.forward(dev(X)))
+    assert O.normwise_rel_err(Y, ref) < TOL
+    L.close()
+
+
+def test_logic_layer_rejects_too_many_rows(ctx):
+    codes = torch.zeros((64, 64), dtype=torch.int8, device="cuda")
+    srow = torch.ones(64, dtype=torch.float32, device="cuda")
+    L = lb.LogicLayer(ctx, codes, srow, None, max_rows=8)
+    with pytest.raises(lb.LalbError) as e:
+        L.forward(torch.zeros((9, 64), dtype=torch.float32, device="cuda"))
+    assert e.value.status == -1
+    L.close()

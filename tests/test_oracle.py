@@ -169,3 +169,38 @@ def test_normal_generator_moments():
     assert abs(z.mean()) < 5e-3 and abs(z.std() - 1) < 5e-3
     a = O.normal(1000, seed=1, offset=500)
     assert np.array_equal(a[:10], z[500:510])
+
+
+def test_binlayer_oracle_matches_reference_goldens():
+    """The restated BinLayer forward against the reference's own compiled
+    bin_forward / bin_forward_pure_float (tests/golden/binlayer_ref.npz)."""
+    g = np.load(os.path.join(GOLD, "binlayer_ref.npz"))
+    for ci in range(3):
+        W, b, mask, X = (g[f"bl{ci}_{k}"] for k in ("W", "b", "mask", "X"))
+        for mode in (0, 1):
+            for repack in (0, 1):
+                Y, alpha = O.binlayer_forward(W, b, mask, X, mode, repack=bool(repack))
+                ref = g[f"bl{ci}_m{mode}_r{repack}_Y"]
+                assert O.normwise_rel_err(Y, ref) < 1e-5, (ci, mode, repack)
+                np.testing.assert_allclose(alpha, g[f"bl{ci}_m{mode}_r{repack}_alpha"], rtol=2e-6,
+                                           atol=0)
+
+
+def test_logic_pack_and_forward_oracle():
+    rows, K, M = 40, 96, 3
+    W = O.normal(rows * K, seed=11, sigma=0.02).reshape(rows, K)
+    st = O.logic_state(12, rows * K, 0.10, 0.50).reshape(rows, K)
+    frac = np.bincount(st.ravel(), minlength=3) / st.size
+    assert abs(frac[0] - 0.10) < 0.03 and abs(frac[1] - 0.50) < 0.04
+    codes, srow = O.logic_pack(W, st)
+    assert np.all(codes[st == 2] == 0) and np.all(np.abs(codes) <= 127)
+    # BINARY codes are +-b per row, sign of w
+    for j in range(rows):
+        bj = np.abs(codes[j][st[j] == 1])
+        assert bj.size == 0 or (np.all(bj == bj[0]) and bj[0] >= 1)
+        assert np.all(np.sign(codes[j][st[j] == 1]) == np.where(W[j][st[j] == 1] > 0, 1, -1))
+    X = O.normal(M * K, seed=13).reshape(M, K)
+    bias = O.normal(rows, seed=14, sigma=0.01)
+    Y = O.logic_forward(codes, srow, bias, X)
+    ref = (X.astype(np.float64) @ codes.T.astype(np.float64)) * srow + bias
+    assert O.normwise_rel_err(Y, ref) < 1e-6
