@@ -278,6 +278,21 @@ LALB_API int lalb_decoder_path(const lalb_decoder *dec);
 LALB_API int lalb_decoder_launches_per_step(const lalb_decoder *dec);
 LALB_API int lalb_decoder_destroy(lalb_decoder *dec);
 
+/* ---- prefill: the Q4_K x Q8 matmul for T tokens at once (tcgen05 int8) -----
+ * Y [T][rows] fp32 = lal_matmul_q4_k (README.md:130,210) applied to each of
+ * the T rows of X [T][K] fp32: per-32 activation quantizer, exact int32 sums
+ * per 32-weight sub-block (one tcgen05.mma kind::i8 instruction each), the
+ * sub-block scale and min corrections applied in fp32 (within 1e-5).  The
+ * weights are first unpacked once into `packed` (weight_bytes: int8 quants
+ * + per-sub-block scales); `ws` holds the quantized tokens (ws_bytes).
+ * K % 256 == 0; packed and ws 256-byte aligned. */
+LALB_API int lalb_prefill_sizes(int rows, int K, int T, size_t *weight_bytes, size_t *ws_bytes);
+LALB_API int lalb_q4k_prefill_pack(lalb_ctx *ctx, const void *W, int rows, int K, void *packed,
+                                   lalb_stream stream);
+LALB_API int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *packed, int rows, int K,
+                                      const float *X, int T, void *ws, float *Y,
+                                      lalb_stream stream);
+
 /* ---- the seed STE model's forward matmuls (tensor cores) -----------------
  * A BinLayer (runtime/lal_runtime.h:171-197) with one CORE (0) / BINARY (1)
  * / PRUNE (2) state per output row.  Built like bin_layer_init_logic

@@ -65,3 +65,16 @@ def test_null_arguments_rejected_without_device():
     assert L.lalb_unpack_scales_6bit(None, None) == -1
     assert L.lalb_matmul_q4_k(None, None, 1, 256, None, None, None) == -1
     assert L.lalb_decoder_step(None, None, None, None, None, None) == -1
+
+
+def test_prefill_sizes_host_only():
+    wb, ws = lb.prefill_sizes(3584, 3584, 512)
+    # int8 quants + {d*sc, dmin*m} per 32-weight sub-block
+    assert wb == 3584 * 3584 + 3584 * 112 * 8
+    # int8 tokens + 256 alignment slack + {sx, sx*sumq} per (block, token tile row)
+    assert ws == 512 * 3584 + 256 + 512 * 112 * 8
+    assert lb.prefill_sizes(1, 256, 1)[1] == 256 + 256 + 64 * 8 * 8   # tokens padded to 64
+    L = _abi.lib()
+    a, b = ctypes.c_size_t(), ctypes.c_size_t()
+    for rows, K, T in [(0, 256, 1), (8, 100, 1), (8, 256, 0)]:
+        assert L.lalb_prefill_sizes(rows, K, T, ctypes.byref(a), ctypes.byref(b)) != 0

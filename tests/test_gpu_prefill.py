@@ -1,0 +1,139 @@
+"""GPU parity of the prefill matmul (T tokens on the tcgen05 int8 tensor cores).
+
+The oracle computes the exact int32 sub-block sums isum[t][r][j] and the
+fp32 result of the exact dot; the prefill kernel produces the same int32
+sums on the tensor cores and combines them with the sub-block scales in fp32
+(one fma chain per output).  Bar: the unpacked weight layout bit-exact; every
+output within 1e-5 of the exact value, relative to the sum of the magnitudes
+of its sub-block terms (the fp32 combine's error scale), and the normwise
+relative error below 1e-5.
+"""
+import numpy as np
+import pytest
+import torch
+
+import _oracle as O
+import lalmodel_b200 as lb
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def block_fields(W, rows, K):
+    """Per sub-block (d*sc, dmin*m) in fp32 and the 4-bit quants, from the raw bytes."""
+    b = W.reshape(rows, K // 256, 144)
+    d = b[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
+    dmin = b[:, :, 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
+    s = b[:, :, 4:16].astype(np.int32)
+    sc = np.empty((rows, K // 256, 8), np.int32)
+    mn = np.empty_like(sc)
+    sc[..., :4] = s[..., 0:4] & 63
+    mn[..., :4] = s[..., 4:8] & 63
+    sc[..., 4:] = (s[..., 8:12] & 15) | ((s[..., 0:4] >> 6) << 4)
+    mn[..., 4:] = (s[..., 8:12] >> 4) | ((s[..., 4:8] >> 6) << 4)
+    qs = b[:, :, 16:].reshape(rows, K // 256, 4, 32)
+    q = np.empty((rows, K // 256, 8, 32), np.int8)
+    q[:, :, 0::2] = qs & 15
+    q[:, :, 1::2] = qs >> 4
+    dsc = (d[..., None] * sc.astype(np.float32)).astype(np.float32)
+    dmm = (dmin[..., None] * mn.astype(np.float32)).astype(np.float32)
+    return q.reshape(rows, K), dsc.reshape(rows, K // 32), dmm.reshape(rows, K // 32)
+
+
+def make(rows, K, T, seed):
+    w = O.normal(rows * K, seed=seed, sigma=0.02).reshape(rows, K)
+    W = O.q4k_quantize(w)
+    X = O.normal(T * K, seed=seed + 1).reshape(T, K)
+    return W, X
+
+
+def check(W, X, rows, K, Y):
+    T = X.shape[0]
+    xq, sx, sq = O.quantize_act(X)
+    yref, isum = O.q4k_matmul(W, rows, K, xq, sx, sq, want_isum=True)
+    _, dsc, dmm = block_fields(W, rows, K)
+    # magnitude of every fp32 sub-block term, summed: the combine's error scale
+    t1 = np.abs(sx[:, None, :].astype(np.float64) * dsc[None].astype(np.float64) * isum)
+    t2 = np.abs((sx * sq)[:, None, :].astype(np.float64) * dmm[None].astype(np.float64))
+    scale = (t1 + t2).sum(-1)
+    err = np.abs(Y.astype(np.float64) - yref.astype(np.float64))
+    assert np.all(err <= TOL * scale + 1e-30), float(np.max(err / (scale + 1e-30)))
+    assert O.normwise_rel_err(Y, yref) < TOL
+
+
+@pytest.mark.parametrize("rows,K", [(128, 256), (200, 3584), (64, 18944)])
+def test_prefill_pack_layout_bit_exact(ctx, rows, K):
+    W, _ = make(rows, K, 1, seed=rows + K)
+    packed = host(ctx.q4k_prefill_pack(dev(W), rows, K))
+    q, dsc, dmm = block_fields(W, rows, K)
+    assert np.array_equal(packed[: rows * K].view(np.int8).reshape(rows, K), q)
+    rs = packed[rows * K:].view(np.float32).reshape(rows, K // 32, 2)
+    assert np.array_equal(rs[..., 0].view(np.uint32), dsc.view(np.uint32))
+    assert np.array_equal(rs[..., 1].view(np.uint32), dmm.view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,K,T", [
+    (128, 256, 64),      # one tile
+    (128, 512, 64),      # several K-blocks in one stage ring pass
+    (256, 3584, 64),     # 28 K-blocks: the stage ring and TMEM slots wrap
+    (200, 3584, 100),    # ragged rows and tokens (partial tiles)
+    (96, 1024, 1),       # a single token
+    (512, 3584, 512),    # the prefill batch, q/o-shaped slice
+])
+def test_prefill_matmul_matches_exact(ctx, rows, K, T):
+    W, X = make(rows, K, T, seed=7 * rows + K + T)
+    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
+    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    check(W, X, rows, K, Y)
+
+
+def test_prefill_down_shape_long_k(ctx):
+    rows, K, T = 384, 18944, 128
+    W, X = make(rows, K, T, seed=31)
+    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
+    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    check(W, X, rows, K, Y)
+
+
+def test_prefill_zero_and_spike_tokens(ctx):
+    rows, K, T = 128, 512, 70
+    W, X = make(rows, K, T, seed=5)
+    X[3] = 0.0                 # all-zero token: every block scale 0
+    X[4, :32] = 0.0            # one zero block
+    X[5, 7] = 1e4              # a spike: that block quantizes to one +-127
+    X[6, 40] = -1e4
+    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
+    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    check(W, X, rows, K, Y)
+    assert np.all(Y[3] == 0.0)
+
+
+def test_prefill_matches_per_token_gemv(ctx):
+    """The batched path and the matvec path agree on every token."""
+    rows, K, T = 256, 3584, 8
+    W, X = make(rows, K, T, seed=77)
+    Wd = dev(W)
+    Y = host(ctx.matmul_q4_k_prefill(ctx.q4k_prefill_pack(Wd, rows, K), rows, K, dev(X)))
+    for t in range(T):
+        y = host(ctx.matmul_q4_k(Wd, dev(X[t]), rows, K))
+        assert O.normwise_rel_err(Y[t], y) < TOL
+
+
+def test_prefill_rejects_bad_arguments(ctx):
+    rows, K = 128, 256
+    W, X = make(rows, K, 4, seed=3)
+    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
+    with pytest.raises(lb.LalbError):
+        ctx.matmul_q4_k_prefill(packed, rows, 200, dev(X[:, :200]))
+    ws = torch.empty(lb.prefill_sizes(rows, K, 4)[1] + 256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(lb.LalbError):
+        ctx.matmul_q4_k_prefill(packed, rows, K, dev(X), ws=ws[16:])
