@@ -1,34 +1,55 @@
-// lalb_prefill.cu -- batched (prefill) Q4_K x Q8 matmul on tcgen05 int8 MMA.
+// lalb_prefill.cu -- batched (prefill) Q4_K x Q8 matmul on the tcgen05 tensor cores.
 //
 //   Y[t][r] = sum_j sx[t][j] * (d_r sc_rj * isum[t][r][j] - dmin_r m_rj * sumq[t][j])
 //
-// the same arithmetic as lal_matmul_q4_k (README.md:130,210) for T tokens at
-// once: isum[t][r][j] is the exact int32 dot of weight row r's sub-block j
-// (32 unsigned 4-bit quants) with token t's int8 activations.  Each
-// tcgen05.mma.kind::i8 instruction (M = 128 weight rows, N = 64 tokens,
-// K = 32 = one sub-block) produces exactly those int32 sums for one
-// sub-block into its own TMEM slot; the epilogue warps promote every slot
-// into fp32 register accumulators with the sub-block's scales (fp32 combine,
-// within 1e-5 of the exact dot).
+// the arithmetic of lal_matmul_q4_k (README.md:130,210) for T tokens at once:
+// isum[t][r][j] is the integer dot of weight row r's sub-block j (32 unsigned
+// 4-bit quants) with token t's int8 activations xq, sumq[t][j] the sum of
+// those activations, sx[t][j] their block scale.
 //
-// Layouts (prepared once: lalb_q4k_prefill_pack for the weights, per call
-// for the activations):
-//   weights   q  int8 [rows][K] (the 4-bit quants 0..15), rs fp32 [rows][K/32][2]
-//             = {d * sc_j, dmin * m_j}
-//   tokens    xq int8 [T][K], ts fp32 [K/32][T][2] = {sx_j, sx_j * sumq_j}
+// Rewritten per 256-weight super-block b (one d_r, dmin_r; sub-blocks j in b),
+// with D = d (1 where d = 0: every sc, and so every A below, is then 0):
 //
-// One CTA per 128-row x 64-token tile, 10 warps:
-//   warp 0     TMA producer: per 128-wide K-block, the 128 x 128 q tile and the
-//              64 x 128 xq tile (128-byte swizzle) and their scale tiles into a
-//              4-stage ring;
-//   warp 1     allocates 512 TMEM columns (8 slots of 64) and issues the MMAs:
-//              sub-block g into slot g % 8, one commit per slot;
-//   warps 2-9  epilogue, two groups of four (tokens 0-31 and 32-63), each warp
-//              on its TMEM lane quarter (32 weight rows): per sub-block, read
-//              the slot (tcgen05.ld 32x32b.x32), free it, promote.
-// A stage is free when its MMAs completed (commit) and all 8 epilogue warps
-// have read its scales.  Every wait is bounded.
+//   Y[t][r] = sum_b D_rb * S_b[t][r],
+//   S_b[t][r] = sum_{i in b} (sc_rj q_ri) (xq_ti sx_tj) + sum_{j in b} c_rj a_tj,
+//   c_rj = -dmin_rb m_rj / D_rb,   a_tj = sx_tj sumq_tj.
+//
+// S_b is one fp32 tensor-core accumulation in a TMEM slot:
+//   sc * q            fp16, exact (integers <= 63 * 15 = 945);
+//   xq * sx * 2^e_t   two fp16 parts (hi + lo, 22 significant bits), e_t a
+//                     per-token power of two that puts the token's largest
+//                     |xq sx| in [2^14, 2^15) (exact to apply and to undo);
+//   c and a * 2^e_t   three bf16 parts each (24 bits, fp32 range); the six
+//                     part products with weight >= 2^-16 of the whole, as one
+//                     16-wide bf16 MMA per two sub-blocks;
+// per 64 weights: 8 kind::f16 MMAs (4 K-steps x {B_hi, B_lo}) and one bf16 MMA
+// for the two sub-blocks' min terms.  The epilogue only adds D * S_b (paired
+// __ffma2_rn) and undoes 2^e_t.  Within 1e-5 of the exact dot.
+//
+// Layouts (the weights prepared once by lalb_q4k_prefill_pack, the tokens per
+// call):
+//   weights  A    fp16 [rows][K] = sc_j * q
+//            Ax   bf16 [rows][K/4]: per 64 weights 16 values, for their two
+//                 sub-blocks {c0 c0 c1 c0 c1 c2} each, then 4 zeros
+//            rs   fp32 [K/256][rows128] = D
+//   tokens   Bhi, Blo  fp16 [T][K]
+//            Bx   bf16 [T][K/4]: per 64 weights, for their two sub-blocks
+//                 {a0 a1 a0 a2 a1 a0} (parts of a 2^e_t) each, then 4 zeros
+//            inv  fp32 [Tp] = 2^-e_t   (Tp = T rounded up to 128)
+//
+// One CTA per 128-row x 128-token tile, 18 warps:
+//   warp 0     TMA producer: per 64-wide K-block the A, B_hi, B_lo (128-byte
+//              swizzle), Ax and Bx (32-byte swizzle) tiles into a 4-stage
+//              ring; per super-block the rows' D into a 2-slot ring;
+//   warp 1     allocates 512 TMEM columns (4 super-block slots of 128) and
+//              issues the MMAs, one commit per stage and one per super-block;
+//   warps 2-17 epilogue, four groups of four (32 tokens each), each warp on its
+//              TMEM lane quarter (32 weight rows): per super-block, read the
+//              slot (tcgen05.ld 32x32b.x16 twice), free it, acc += D * S.
+// Every wait is bounded.
 #include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <mutex>
@@ -40,25 +61,38 @@ using namespace lalb;
 
 namespace {
 
-constexpr int PM = 128, PN = 64, PK = 128;   // PK int8 = 128 B: one swizzle row = 4 sub-blocks
+constexpr int PM = 128, PN = 128, PK = 64;   // PK fp16 = 128 B: one swizzle row
 constexpr int kPStages = 4;
-constexpr int kSlotsT = 8;                   // TMEM accumulator slots (PN columns each)
-constexpr int kEpiWarps = 8;
+constexpr int kSlotsT = 4;                   // TMEM super-block slots (PN columns each)
+constexpr int kTmemCols = kSlotsT * PN;
+constexpr int kEpiWarps = 16;
 constexpr int kPThreads = 32 * (2 + kEpiWarps);
-constexpr uint32_t kPA = PM * PK;            // 16 KB
-constexpr uint32_t kPB = PN * PK;            // 8 KB
-constexpr uint32_t kPRS = PM * 8 * 4;        // 4 KB: 128 rows x 4 sub-blocks x {dsc, dmm}
-constexpr uint32_t kPTS = 4 * PN * 2 * 4;    // 2 KB: 4 sub-blocks x 64 tokens x {sx, a}
-constexpr uint32_t kPStage = kPA + kPB + kPRS + kPTS;   // 30 KB (1024-multiple)
-constexpr uint32_t kPSmem = 1024 + kPStages * kPStage + 512;
+constexpr uint32_t kPA = PM * PK * 2;        // 16 KB
+constexpr uint32_t kPB = PN * PK * 2;        // 16 KB (each of B_hi, B_lo)
+constexpr uint32_t kPAX = PM * 16 * 2;       // 4 KB: 128 rows x 16 bf16
+constexpr uint32_t kPBX = PN * 16 * 2;       // 4 KB
+constexpr uint32_t kOffBh = kPA, kOffBl = kPA + kPB, kOffAx = kPA + 2 * kPB, kOffBx = kOffAx + kPAX;
+constexpr uint32_t kPStage = kOffBx + kPBX;  // 56 KB
+constexpr uint32_t kSbBytes = PM * 4;        // the tile rows' D of one super-block
+constexpr int kSbSlots = 2;
+constexpr uint32_t kPSmem = 1024 + kPStages * kPStage + kSbSlots * kSbBytes + 512;
+static_assert(kPStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+static_assert(kPSmem <= 232448, "fits the 227 KB opt-in shared memory");
 
-// kind::i8: s32 accumulator, signed A and B, both K-major, M = 128, N = 64.
-constexpr uint32_t kIdescI8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PN >> 3) << 17) |
-                              ((uint32_t)(PM >> 4) << 24);
+// kind::f16: f32 accumulator, fp16 A and B, both K-major, M = 128, N = 128.
+constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
+// the same with bf16 A and B (the min-term MMA)
+constexpr uint32_t kIdescBF16 = kIdescF16 | (1u << 7) | (1u << 10);
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// K-major, 32-byte swizzle (one 16-element bf16 K-step per row): 8-row atoms of 256 B.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
 }
 
 __device__ __forceinline__ void tma2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -69,12 +103,12 @@ __device__ __forceinline__ void tma2d(void *dst, const CUtensorMap *map, int x, 
         : "memory");
 }
 
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc) {
-    // every sub-block starts its own slot: no accumulation across sub-blocks
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 0, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdescI8)
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -84,46 +118,68 @@ __device__ __forceinline__ void commit(uint64_t *bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32_i(uint32_t taddr, int (&r)[32]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
         "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
         "%28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-          "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-          "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]),
+          "=f"(r[7]), "=f"(r[8]), "=f"(r[9]), "=f"(r[10]), "=f"(r[11]), "=f"(r[12]), "=f"(r[13]),
+          "=f"(r[14]), "=f"(r[15]), "=f"(r[16]), "=f"(r[17]), "=f"(r[18]), "=f"(r[19]), "=f"(r[20]),
+          "=f"(r[21]), "=f"(r[22]), "=f"(r[23]), "=f"(r[24]), "=f"(r[25]), "=f"(r[26]), "=f"(r[27]),
+          "=f"(r[28]), "=f"(r[29]), "=f"(r[30]), "=f"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]),
+          "=f"(r[7]), "=f"(r[8]), "=f"(r[9]), "=f"(r[10]), "=f"(r[11]), "=f"(r[12]), "=f"(r[13]),
+          "=f"(r[14]), "=f"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+
 struct PfArgs {
     int rows, K, T;
+    const float *inv;       // [Tp] 2^-e_t
     float *Y;               // [T][rows]
     unsigned int *status;
 };
 
 __global__ void __launch_bounds__(kPThreads, 1)
-    prefill_i8_kernel(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mX,
-                      const __grid_constant__ CUtensorMap mRS, const __grid_constant__ CUtensorMap mTS,
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mBh,
+                      const __grid_constant__ CUtensorMap mBl, const __grid_constant__ CUtensorMap mAx,
+                      const __grid_constant__ CUtensorMap mBx, const __grid_constant__ CUtensorMap mRS,
                       const PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kPStages * kPStage);
+    float *sbring = reinterpret_cast<float *>(smem + kPStages * kPStage);   // [2][128] D
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kPStages * kPStage + kSbSlots * kSbBytes);
     uint64_t *empty = full + kPStages;
-    uint64_t *sfull = empty + kPStages;       // TMEM slot holds a sub-block's sums
+    uint64_t *sbfull = empty + kPStages;      // a super-block's D arrived
+    uint64_t *sbempty = sbfull + kSbSlots;    // every epilogue warp is done with it
+    uint64_t *sfull = sbempty + kSbSlots;     // TMEM slot holds a super-block's sums
     uint64_t *sempty = sfull + kSlotsT;       // the epilogue has read the slot
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sempty + kSlotsT);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = blockIdx.y * PM, t0 = blockIdx.x * PN;
     const int nkb = a.K / PK;
+    const int nsb = a.K / 256;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1 + kEpiWarps);   // the MMA commit and every epilogue warp
+            mbar_init(&empty[s], 1);              // the MMA commit
+        }
+        for (int s = 0; s < kSbSlots; ++s) {
+            mbar_init(&sbfull[s], 1);
+            mbar_init(&sbempty[s], kEpiWarps);
         }
         for (int s = 0; s < kSlotsT; ++s) {
             mbar_init(&sfull[s], 1);
@@ -134,7 +190,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(kSlotsT * PN)
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -146,39 +202,48 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             for (int kb = 0; kb < nkb; ++kb) {
+                if ((kb & 3) == 0) {   // a new super-block: its rows' D
+                    const int sb = kb >> 2, slot = sb & 1;
+                    if (sb >= kSbSlots && !mbar_wait_bounded(&sbempty[slot], ((sb >> 1) - 1) & 1u, a.status))
+                        break;
+                    mbar_arrive_expect_tx(&sbfull[slot], kSbBytes);
+                    tma2d(sbring + slot * PM, &mRS, r0, sb, &sbfull[slot]);
+                }
                 const int s = kb % kPStages;
                 const uint32_t use = kb / kPStages;
                 if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u, a.status)) break;
                 uint8_t *st = smem + (size_t)s * kPStage;
                 mbar_arrive_expect_tx(&full[s], kPStage);
-                tma2d(st, &mQ, kb * PK, r0, &full[s]);
-                tma2d(st + kPA, &mX, kb * PK, t0, &full[s]);
-                tma2d(st + kPA + kPB, &mRS, kb * 8, r0, &full[s]);
-                tma2d(st + kPA + kPB + kPRS, &mTS, t0 * 2, kb * 4, &full[s]);
+                tma2d(st, &mA, kb * PK, r0, &full[s]);
+                tma2d(st + kOffBh, &mBh, kb * PK, t0, &full[s]);
+                tma2d(st + kOffBl, &mBl, kb * PK, t0, &full[s]);
+                tma2d(st + kOffAx, &mAx, kb * 16, r0, &full[s]);
+                tma2d(st + kOffBx, &mBx, kb * 16, t0, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kPStages;
+                const int sb = kb >> 2;
+                const uint32_t slot = sb % kSlotsT;
+                if ((kb & 3) == 0 && sb >= kSlotsT &&
+                    !mbar_wait_bounded(&sempty[slot], (uint32_t)(sb / kSlotsT - 1) & 1u, a.status))
+                    break;
                 if (!mbar_wait_bounded(&full[s], (uint32_t)(kb / kPStages) & 1u, a.status)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t st = smem_u32(smem + (size_t)s * kPStage);
-                bool ok = true;
+                const uint32_t d = tmem + slot * PN;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {   // one sub-block (32 bytes of K) per instruction
-                    const uint32_t g = kb * 4 + j;
-                    const uint32_t slot = g % kSlotsT, use = g / kSlotsT;
-                    if (use > 0 && !mbar_wait_bounded(&sempty[slot], (use - 1) & 1u, a.status)) {
-                        ok = false;
-                        break;
-                    }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    mma_i8(tmem + slot * PN, sw128_desc(st + j * 32), sw128_desc(st + kPA + j * 32));
-                    commit(&sfull[slot]);
+                for (int kk = 0; kk < 4; ++kk) {   // 16 weights per step, B_hi then B_lo
+                    const uint64_t ad = sw128_desc(st + kk * 32);
+                    mma_f16(d, ad, sw128_desc(st + kOffBh + kk * 32), kIdescF16, ((kb & 3) | kk) != 0 ? 1u : 0u);
+                    mma_f16(d, ad, sw128_desc(st + kOffBl + kk * 32), kIdescF16, 1u);
                 }
-                commit(&empty[s]);   // the stage's A/B tiles are read once these MMAs complete
-                if (!ok) break;
+                // the two sub-blocks' min terms
+                mma_f16(d, sw32_desc(st + kOffAx), sw32_desc(st + kOffBx), kIdescBF16, 1u);
+                commit(&empty[s]);                         // the stage's tiles are read once these complete
+                if ((kb & 3) == 3) commit(&sfull[slot]);   // the super-block's sums are complete
             }
         }
     } else {
@@ -187,116 +252,174 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int q = warp & 3;              // lane quarter
         const int grp = ew >> 2;             // tokens 32*grp .. 32*grp + 31
         const int row = q * 32 + lane;       // weight row within the tile
-        float acc[32];
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + grp * 32;
+        float2 acc[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
         bool ok = true;
-        for (int kb = 0; kb < nkb && ok; ++kb) {
-            const int s = kb % kPStages;
-            const uint8_t *st = smem + (size_t)s * kPStage;
-            const float *rs = reinterpret_cast<const float *>(st + kPA + kPB);         // [128][8]
-            const float *ts = reinterpret_cast<const float *>(st + kPA + kPB + kPRS);  // [4][64][2]
-            // the scale tiles came in with the stage's TMA copies
-            if (!mbar_wait_bounded(&full[s], (uint32_t)(kb / kPStages) & 1u, a.status)) break;
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t g = kb * 4 + j;
-                const uint32_t slot = g % kSlotsT;
-                if (!mbar_wait_bounded(&sfull[slot], (g / kSlotsT) & 1u, a.status)) {
-                    ok = false;
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                int isum[32];
-                tmem_ld32_i(tmem + ((uint32_t)(q * 32) << 16) + slot * PN + grp * 32, isum);
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sempty[slot]);
-                const float dsc = rs[row * 8 + 2 * j], dmm = rs[row * 8 + 2 * j + 1];
-                const float *tj = ts + (j * PN + grp * 32) * 2;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float sx = tj[2 * i], am = tj[2 * i + 1];
-                    acc[i] = fmaf(sx * dsc, (float)isum[i], acc[i]);
-                    acc[i] = fmaf(-am, dmm, acc[i]);
-                }
+        for (int sb = 0; sb < nsb; ++sb) {
+            const int sslot = sb & 1;
+            const uint32_t slot = sb % kSlotsT;
+            if (!mbar_wait_bounded(&sbfull[sslot], (uint32_t)(sb >> 1) & 1u, a.status) ||
+                !mbar_wait_bounded(&sfull[slot], (uint32_t)(sb / kSlotsT) & 1u, a.status)) {
+                ok = false;
+                break;
             }
-            // this warp is done with the stage's scales (its MMAs completed:
-            // their sums were read above)
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const float D = sbring[sslot * PM + row];
+            const float2 D2 = make_float2(D, D);
+            float S[32];
+            tmem_ld16(tbase + slot * PN, *reinterpret_cast<float(*)[16]>(S));
+            tmem_ld16(tbase + slot * PN + 16, *reinterpret_cast<float(*)[16]>(S + 16));
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        // rows are the fast dimension of Y: lane = row gives 128-byte stores
-        const int r = r0 + row;
-        if (r < a.rows)
-            for (int i = 0; i < 32; ++i) {
-                const int t = t0 + grp * 32 + i;
-                if (t < a.T) a.Y[(size_t)t * a.rows + r] = acc[i];
+            if (lane == 0) {
+                mbar_arrive(&sempty[slot]);
+                mbar_arrive(&sbempty[sslot]);
             }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = __ffma2_rn(make_float2(S[2 * i], S[2 * i + 1]), D2, acc[i]);
+        }
+        // undo 2^e_t; rows are the fast dimension of Y: lane = row gives 128-byte stores
+        const int r = r0 + row;
+        if (ok && r < a.rows) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int t = t0 + grp * 32 + 2 * i;
+                if (t < a.T) a.Y[(size_t)t * a.rows + r] = acc[i].x * __ldg(a.inv + t);
+                if (t + 1 < a.T) a.Y[(size_t)(t + 1) * a.rows + r] = acc[i].y * __ldg(a.inv + t + 1);
+            }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     }
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(kSlotsT * PN)
+                     "r"(kTmemCols)
                      : "memory");
     }
 }
 
-// Q4_K rows -> int8 quants and per-(row, sub-block) {d*sc, dmin*m}: one
-// warp per 256-weight super-block.
-__global__ void prefill_pack_kernel(const uint8_t *__restrict__ W, long long nsb, int8_t *__restrict__ q,
+// x = p0 + p1 + p2, three bf16 parts (each the round-to-nearest of what is left).
+__device__ __forceinline__ void split3_bf16(float x, __nv_bfloat16 &p0, __nv_bfloat16 &p1, __nv_bfloat16 &p2) {
+    p0 = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(p0);
+    p1 = __float2bfloat16_rn(r1);
+    p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+}
+
+// Q4_K rows -> fp16 A = sc_j * q, the min-term parts Ax and the rows' D:
+// one warp per 256-weight super-block.
+__global__ void prefill_pack_kernel(const uint8_t *__restrict__ W, int rows, int K, int rows128,
+                                    __half *__restrict__ A, __nv_bfloat16 *__restrict__ Ax,
                                     float *__restrict__ rs) {
     const int lane = threadIdx.x & 31;
+    const int nsr = K / 256;
+    const long long nsb = (long long)rows * nsr;
     const long long w0 = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
     for (long long b = w0; b < nsb; b += nw) {
         const uint8_t *blk = W + b * 144;
-        // lane handles quant bytes 4*lane .. 4*lane+3 of the 128: group g = lane / 8
-        const uint32_t qs = *reinterpret_cast<const uint32_t *>(blk + 16 + 4 * lane);
-        const int g = lane >> 3, off = (lane & 7) * 4;
+        const uint32_t s0 = *reinterpret_cast<const uint32_t *>(blk + 4);
+        const uint32_t s1 = *reinterpret_cast<const uint32_t *>(blk + 8);
+        const uint32_t s2 = *reinterpret_cast<const uint32_t *>(blk + 12);
+        const ScaleWords sw = unpack_scale_words(s0, s1, s2);
+        // lane handles quant bytes 4*lane .. 4*lane+3 of the 128: group g = lane / 8;
         // low nibbles -> sub-block 2g, high nibbles -> sub-block 2g+1
-        const uint32_t lo = qs & 0x0F0F0F0Fu, hi = (qs >> 4) & 0x0F0F0F0Fu;
-        *reinterpret_cast<uint32_t *>(q + b * 256 + (2 * g) * 32 + off) = lo;
-        *reinterpret_cast<uint32_t *>(q + b * 256 + (2 * g + 1) * 32 + off) = hi;
-        if (lane < 8) {
-            const uint32_t s0 = *reinterpret_cast<const uint32_t *>(blk + 4);
-            const uint32_t s1 = *reinterpret_cast<const uint32_t *>(blk + 8);
-            const uint32_t s2 = *reinterpret_cast<const uint32_t *>(blk + 12);
-            const ScaleWords sw = unpack_scale_words(s0, s1, s2);
-            const uint32_t scw = lane < 4 ? sw.sc_lo : sw.sc_hi, mnw = lane < 4 ? sw.mn_lo : sw.mn_hi;
-            const int sc = (scw >> (8 * (lane & 3))) & 0xFF, mn = (mnw >> (8 * (lane & 3))) & 0xFF;
-            const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
-            const float d = f16_bits_to_f32(dd & 0xFFFFu), dmin = f16_bits_to_f32(dd >> 16);
-            rs[(b * 8 + lane) * 2] = __fmul_rn(d, (float)sc);
-            rs[(b * 8 + lane) * 2 + 1] = __fmul_rn(dmin, (float)mn);
+        const int g = lane >> 3, off = (lane & 7) * 4;
+        const uint32_t scw = g < 2 ? sw.sc_lo : sw.sc_hi;
+        const int sc_lo = (scw >> (16 * (g & 1))) & 0xFF, sc_hi = (scw >> (16 * (g & 1) + 8)) & 0xFF;
+        const uint32_t qs = *reinterpret_cast<const uint32_t *>(blk + 16 + 4 * lane);
+        __align__(8) __half lo[4], hi[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            lo[i] = __int2half_rn(sc_lo * (int)((qs >> (8 * i)) & 0xF));
+            hi[i] = __int2half_rn(sc_hi * (int)((qs >> (8 * i + 4)) & 0xF));
+        }
+        __half *dst = A + b * 256;
+        *reinterpret_cast<uint2 *>(dst + (2 * g) * 32 + off) = *reinterpret_cast<const uint2 *>(lo);
+        *reinterpret_cast<uint2 *>(dst + (2 * g + 1) * 32 + off) = *reinterpret_cast<const uint2 *>(hi);
+        const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
+        float D = f16_bits_to_f32(dd & 0xFFFFu);
+        if (D == 0.0f) D = 1.0f;   // every sc is 0: only the min terms count
+        __nv_bfloat16 *ax = Ax + b * 64;
+        if (lane < 8) {            // sub-block j = lane: c = -dmin m_j / D as three bf16 parts
+            const uint32_t mnw = lane < 4 ? sw.mn_lo : sw.mn_hi;
+            const int mn = (mnw >> (8 * (lane & 3))) & 0xFF;
+            const float c = -__fdiv_rn(__fmul_rn(f16_bits_to_f32(dd >> 16), (float)mn), D);
+            __nv_bfloat16 c0, c1, c2;
+            split3_bf16(c, c0, c1, c2);
+            __nv_bfloat16 *o = ax + (lane >> 1) * 16 + (lane & 1) * 6;
+            o[0] = c0; o[1] = c0; o[2] = c1; o[3] = c0; o[4] = c1; o[5] = c2;
+        } else if (lane < 24) {    // the four zeros after each pair of sub-blocks
+            const int k = lane - 8;
+            ax[(k >> 2) * 16 + 12 + (k & 3)] = __float2bfloat16_rn(0.0f);
+        } else if (lane == 24) {
+            const long long r = b / nsr, sbi = b % nsr;
+            rs[sbi * rows128 + r] = D;
         }
     }
 }
 
-// Tokens: fp32 [T][K] -> xq int8 [T][K] and ts [K/32][Tp][2] = {sx, sx * sumq}
-// (Tp = T rounded up to the token tile)
-// (the activation quantizer of quantize_act_kernel, one warp per 32-block).
-__global__ void prefill_act_kernel(const float *__restrict__ X, int T, int Tp, int K,
-                                   int8_t *__restrict__ xq, float *__restrict__ ts) {
-    const int lane = threadIdx.x & 31;
+// Tokens: one CTA per token.  The activation quantizer of quantize_act_kernel
+// per 32-block (sx = amax / 127, xq = round(x / sx)), then the token's power
+// of two e (largest block amax * 2^e in [2^14, 2^15)), and
+//   Bhi + Blo = xq * sx * 2^e (fp16 parts),  Bx = the parts of sx * sumq * 2^e,
+//   inv[t] = 2^-e.
+__global__ void prefill_act_kernel(const float *__restrict__ X, int T, int K, __half *__restrict__ Bh,
+                                   __half *__restrict__ Bl, __nv_bfloat16 *__restrict__ Bx,
+                                   float *__restrict__ inv) {
+    __shared__ float s_amax[32];
+    __shared__ float s_scale;
+    const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
     const int nb = K / 32;
-    const long long nblk = (long long)T * nb;
-    const long long w0 = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
-    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
-    for (long long b = w0; b < nblk; b += nw) {
-        const long long t = b / nb, j = b % nb;
-        const float v = X[b * 32 + lane];
+    const float *x = X + (size_t)t * K;
+    // pass 1: the token's largest |x|
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
+    m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+    if (lane == 0) s_amax[warp] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = 0.0f;
+        for (int w = 0; w < nwarp; ++w) mm = fmaxf(mm, s_amax[w]);
+        int e = 0;
+        if (mm > 0.0f) {
+            int ex;
+            frexpf(mm, &ex);          // mm in [2^(ex-1), 2^ex)
+            e = min(15 - ex, 126);    // mm * 2^e in [2^14, 2^15); 2^e and 2^-e stay normal
+        }
+        s_scale = ldexpf(1.0f, e);
+        inv[t] = ldexpf(1.0f, -e);
+    }
+    __syncthreads();
+    const float sc2 = s_scale;
+    __nv_bfloat16 *bx = Bx + (size_t)t * (K / 4);
+    // pass 2: one warp per 32-block
+    for (int j = warp; j < nb; j += nwarp) {
+        const float v = x[j * 32 + lane];
         const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
         const float d = __fdiv_rn(__uint_as_float(amax), 127.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
         const float tq = roundf(__fmul_rn(v, id));
         const int qv = tq > 127.0f ? 127 : (tq < -127.0f ? -127 : (int)tq);
-        xq[b * 32 + lane] = (int8_t)qv;
         const int s = __reduce_add_sync(0xffffffffu, qv);
+        const float b = __fmul_rn(__fmul_rn((float)qv, d), sc2);
+        const __half bh = __float2half_rn(b);
+        Bh[(size_t)t * K + j * 32 + lane] = bh;
+        Bl[(size_t)t * K + j * 32 + lane] = __float2half_rn(b - __half2float(bh));
+        // this sub-block's min-term parts: 16 values per pair of sub-blocks
+        __nv_bfloat16 *o = bx + (j >> 1) * 16;
         if (lane == 0) {
-            ts[(j * Tp + t) * 2] = d;
-            ts[(j * Tp + t) * 2 + 1] = __fmul_rn(d, (float)s);
+            __nv_bfloat16 a0, a1, a2;
+            split3_bf16(__fmul_rn(__fmul_rn(d, (float)s), sc2), a0, a1, a2);
+            __nv_bfloat16 *p = o + (j & 1) * 6;
+            p[0] = a0; p[1] = a1; p[2] = a0; p[3] = a2; p[4] = a1; p[5] = a0;
+        } else if ((j & 1) == 0 && lane < 5) {
+            o[12 + lane - 1] = __float2bfloat16_rn(0.0f);
         }
     }
 }
@@ -319,8 +442,8 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D row-major map: dims {inner, outer}, box {bi, bo}; outer rows past the
-// end (and inner columns past the end) read as zeros.
+// 2-D row-major map: dims {inner, outer}, box {bi, bo}; rows and columns past
+// the end read as zeros.
 int map2d(lalb_ctx *ctx, CUtensorMap *m, const void *base, CUtensorMapDataType dt, int esize,
           long long inner, long long outer, int bi, int bo, CUtensorMapSwizzle sw) {
     EncodeTiledFn fn = encode_fn();
@@ -336,65 +459,87 @@ int map2d(lalb_ctx *ctx, CUtensorMap *m, const void *base, CUtensorMapDataType d
     return LALB_OK;
 }
 
+int rows_padded(int rows) { return (rows + PM - 1) / PM * PM; }
+int tokens_padded(int T) { return (T + PN - 1) / PN * PN; }
+size_t up256(size_t n) { return (n + 255) / 256 * 256; }
+
+// packed weights: A | Ax | rs
+size_t weight_a_bytes(int rows, int K) { return (size_t)rows * K * sizeof(__half); }
+size_t weight_ax_bytes(int rows, int K) { return up256((size_t)rows * (K / 4) * sizeof(__nv_bfloat16)); }
+// workspace: Bh | Bl | Bx | inv
+size_t act_b_bytes(int T, int K) { return up256((size_t)T * K * sizeof(__half)); }
+size_t act_bx_bytes(int T, int K) { return up256((size_t)T * (K / 4) * sizeof(__nv_bfloat16)); }
+
 }  // namespace
 
 size_t lalb_prefill_weight_bytes(int rows, int K) {
-    return (size_t)rows * K + (size_t)rows * (K / 32) * 2 * sizeof(float);
+    return weight_a_bytes(rows, K) + weight_ax_bytes(rows, K) +
+           (size_t)(K / 256) * rows_padded(rows) * sizeof(float);
 }
 
-static int tokens_padded(int T) { return (T + PN - 1) / PN * PN; }
-
 size_t lalb_prefill_act_bytes(int T, int K) {
-    return (size_t)T * K + 256 + (size_t)tokens_padded(T) * (K / 32) * 2 * sizeof(float);
+    return 2 * act_b_bytes(T, K) + act_bx_bytes(T, K) + (size_t)tokens_padded(T) * sizeof(float);
 }
 
 int lalb_prefill_pack(lalb_ctx *ctx, const void *W, int rows, int K, void *packed, cudaStream_t s) {
-    int8_t *q = static_cast<int8_t *>(packed);
-    float *rs = reinterpret_cast<float *>(q + (size_t)rows * K);
+    uint8_t *p = static_cast<uint8_t *>(packed);
+    __half *A = reinterpret_cast<__half *>(p);
+    __nv_bfloat16 *Ax = reinterpret_cast<__nv_bfloat16 *>(p + weight_a_bytes(rows, K));
+    float *rs = reinterpret_cast<float *>(p + weight_a_bytes(rows, K) + weight_ax_bytes(rows, K));
+    LALB_CUDA_TRY(ctx, cudaMemsetAsync(rs, 0, (size_t)(K / 256) * rows_padded(rows) * sizeof(float), s));
     const long long nsb = (long long)rows * (K / 256);
     const int blocks = (int)std::min<long long>((nsb * 32 + 255) / 256, (long long)ctx->sm_count * 16);
-    prefill_pack_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t *>(W), nsb, q, rs);
+    prefill_pack_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t *>(W), rows, K, rows_padded(rows),
+                                                A, Ax, rs);
     LALB_LAUNCH_CHECK(ctx, "prefill_pack_kernel");
     return LALB_OK;
 }
 
 int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, const float *X, int T,
                         void *ws, float *Y, cudaStream_t s) {
-    const int8_t *q = static_cast<const int8_t *>(packed);
-    const float *rs = reinterpret_cast<const float *>(q + (size_t)rows * K);
-    int8_t *xq = static_cast<int8_t *>(ws);
-    float *ts = reinterpret_cast<float *>(
-        (reinterpret_cast<uintptr_t>(xq + (size_t)T * K) + 255) & ~(uintptr_t)255);
-    {
-        const long long nblk = (long long)T * (K / 32);
-        const int blocks = (int)std::min<long long>((nblk * 32 + 255) / 256, (long long)ctx->sm_count * 16);
-        prefill_act_kernel<<<blocks, 256, 0, s>>>(X, T, tokens_padded(T), K, xq, ts);
-        LALB_LAUNCH_CHECK(ctx, "prefill_act_kernel");
-    }
-    CUtensorMap mQ, mX, mRS, mTS;
+    const uint8_t *p = static_cast<const uint8_t *>(packed);
+    const __half *A = reinterpret_cast<const __half *>(p);
+    const __nv_bfloat16 *Ax = reinterpret_cast<const __nv_bfloat16 *>(p + weight_a_bytes(rows, K));
+    const float *rs = reinterpret_cast<const float *>(p + weight_a_bytes(rows, K) + weight_ax_bytes(rows, K));
+    uint8_t *w = static_cast<uint8_t *>(ws);
+    __half *Bh = reinterpret_cast<__half *>(w);
+    __half *Bl = reinterpret_cast<__half *>(w + act_b_bytes(T, K));
+    __nv_bfloat16 *Bx = reinterpret_cast<__nv_bfloat16 *>(w + 2 * act_b_bytes(T, K));
+    float *inv = reinterpret_cast<float *>(w + 2 * act_b_bytes(T, K) + act_bx_bytes(T, K));
+    const int Tp = tokens_padded(T);
+    prefill_act_kernel<<<T, 256, 0, s>>>(X, T, K, Bh, Bl, Bx, inv);
+    LALB_LAUNCH_CHECK(ctx, "prefill_act_kernel");
+    CUtensorMap mA, mBh, mBl, mAx, mBx, mRS;
     int st;
-    if ((st = map2d(ctx, &mQ, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, rows, PK, PM,
+    if ((st = map2d(ctx, &mA, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, rows, PK, PM,
                     CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = map2d(ctx, &mX, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, T, PK, PN,
+    if ((st = map2d(ctx, &mBh, Bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, T, PK, PN,
                     CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = map2d(ctx, &mRS, rs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (long long)(K / 32) * 2, rows, 8,
-                    PM, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    if ((st = map2d(ctx, &mBl, Bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, T, PK, PN,
+                    CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = map2d(ctx, &mTS, ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (long long)tokens_padded(T) * 2,
-                    K / 32, 2 * PN, 4, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    if ((st = map2d(ctx, &mAx, Ax, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K / 4, rows, 16, PM,
+                    CU_TENSOR_MAP_SWIZZLE_32B)))
         return st;
-    if ((st = lalb_set_smem_attr(ctx, (const void *)prefill_i8_kernel, (int)kPSmem))) return st;
+    if ((st = map2d(ctx, &mBx, Bx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K / 4, T, 16, PN,
+                    CU_TENSOR_MAP_SWIZZLE_32B)))
+        return st;
+    if ((st = map2d(ctx, &mRS, rs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows_padded(rows), K / 256, PM, 1,
+                    CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return st;
+    if ((st = lalb_set_smem_attr(ctx, (const void *)prefill_tc_kernel, (int)kPSmem))) return st;
     PfArgs a;
     a.rows = rows;
     a.K = K;
     a.T = T;
+    a.inv = inv;
     a.Y = Y;
     a.status = &ctx->scratch->status;
-    const dim3 grid((T + PN - 1) / PN, (rows + PM - 1) / PM);
-    prefill_i8_kernel<<<grid, kPThreads, kPSmem, s>>>(mQ, mX, mRS, mTS, a);
-    LALB_LAUNCH_CHECK(ctx, "prefill_i8_kernel");
+    const dim3 grid(Tp / PN, (rows + PM - 1) / PM);
+    prefill_tc_kernel<<<grid, kPThreads, kPSmem, s>>>(mA, mBh, mBl, mAx, mBx, mRS, a);
+    LALB_LAUNCH_CHECK(ctx, "prefill_tc_kernel");
     return LALB_OK;
 }
 

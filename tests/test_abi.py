@@ -69,11 +69,12 @@ def test_null_arguments_rejected_without_device():
 
 def test_prefill_sizes_host_only():
     wb, ws = lb.prefill_sizes(3584, 3584, 512)
-    # int8 quants + {d*sc, dmin*m} per 32-weight sub-block
-    assert wb == 3584 * 3584 + 3584 * 112 * 8
-    # int8 tokens + 256 alignment slack + {sx, sx*sumq} per (block, token tile row)
-    assert ws == 512 * 3584 + 256 + 512 * 112 * 8
-    assert lb.prefill_sizes(1, 256, 1)[1] == 256 + 256 + 64 * 8 * 8   # tokens padded to 64
+    # fp16 sc*q per weight + bf16 min-term parts (16 per 64 weights) + D per
+    # (super-block, row), rows padded to 128
+    assert wb == 3584 * 3584 * 2 + 3584 * 896 * 2 + 14 * 3584 * 4
+    # two fp16 parts per token element + bf16 min-term parts + 2^-e per token
+    assert ws == 2 * 512 * 3584 * 2 + 512 * 896 * 2 + 512 * 4
+    assert lb.prefill_sizes(1, 256, 1) == (512 + 256 + 128 * 4, 2 * 512 + 256 + 128 * 4)
     L = _abi.lib()
     a, b = ctypes.c_size_t(), ctypes.c_size_t()
     for rows, K, T in [(0, 256, 1), (8, 100, 1), (8, 256, 0)]:

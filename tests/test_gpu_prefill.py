@@ -1,9 +1,10 @@
 """GPU parity of the prefill matmul (T tokens on the tcgen05 int8 tensor cores).
 
 The oracle computes the exact int32 sub-block sums isum[t][r][j] and the
-fp32 result of the exact dot; the prefill kernel produces the same int32
-sums on the tensor cores and combines them with the sub-block scales in fp32
-(one fma chain per output).  Bar: the unpacked weight layout bit-exact; every
+fp32 result of the exact dot.  The prefill kernel accumulates each 256-weight
+super-block, min terms included, on the tensor cores (fp16 sc * q exact,
+xq * sx in two fp16 parts, the min terms in three bf16 parts each) and scales
+it by the super-block's d in fp32.  Bar: the unpacked weight layout bit-exact; every
 output within 1e-5 of the exact value, relative to the sum of the magnitudes
 of its sub-block terms (the fp32 combine's error scale), and the normwise
 relative error below 1e-5.
@@ -28,18 +29,24 @@ def host(t):
     return t.cpu().numpy()
 
 
-def block_fields(W, rows, K):
-    """Per sub-block (d*sc, dmin*m) in fp32 and the 4-bit quants, from the raw bytes."""
-    b = W.reshape(rows, K // 256, 144)
-    d = b[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
-    dmin = b[:, :, 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
-    s = b[:, :, 4:16].astype(np.int32)
+def scales_mins(W, rows, K):
+    """The 6-bit scales and mins [rows][K/256][8] of every super-block."""
+    s = W.reshape(rows, K // 256, 144)[:, :, 4:16].astype(np.int32)
     sc = np.empty((rows, K // 256, 8), np.int32)
     mn = np.empty_like(sc)
     sc[..., :4] = s[..., 0:4] & 63
     mn[..., :4] = s[..., 4:8] & 63
     sc[..., 4:] = (s[..., 8:12] & 15) | ((s[..., 0:4] >> 6) << 4)
     mn[..., 4:] = (s[..., 8:12] >> 4) | ((s[..., 4:8] >> 6) << 4)
+    return sc, mn
+
+
+def block_fields(W, rows, K):
+    """Per sub-block (d*sc, dmin*m) in fp32 and the 4-bit quants, from the raw bytes."""
+    b = W.reshape(rows, K // 256, 144)
+    d = b[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
+    dmin = b[:, :, 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
+    sc, mn = scales_mins(W, rows, K)
     qs = b[:, :, 16:].reshape(rows, K // 256, 4, 32)
     q = np.empty((rows, K // 256, 8, 32), np.int8)
     q[:, :, 0::2] = qs & 15
@@ -70,15 +77,38 @@ def check(W, X, rows, K, Y):
     assert O.normwise_rel_err(Y, yref) < TOL
 
 
+def bf16_to_f64(u16):
+    return (u16.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+
+
 @pytest.mark.parametrize("rows,K", [(128, 256), (200, 3584), (64, 18944)])
 def test_prefill_pack_layout_bit_exact(ctx, rows, K):
+    """A = sc * q in fp16 (exact); Ax = per 64 weights, for each of their two
+    sub-blocks, the bf16 parts {c0 c0 c1 c0 c1 c2} of c = -dmin m / D, then 4
+    zeros; rs = D per (super-block, row) (D = d, or 1 where d = 0)."""
     W, _ = make(rows, K, 1, seed=rows + K)
+    W.reshape(rows, K // 256, 144)[0, 0, 0:2] = 0          # one super-block with d = 0
     packed = host(ctx.q4k_prefill_pack(dev(W), rows, K))
-    q, dsc, dmm = block_fields(W, rows, K)
-    assert np.array_equal(packed[: rows * K].view(np.int8).reshape(rows, K), q)
-    rs = packed[rows * K:].view(np.float32).reshape(rows, K // 32, 2)
-    assert np.array_equal(rs[..., 0].view(np.uint32), dsc.view(np.uint32))
-    assert np.array_equal(rs[..., 1].view(np.uint32), dmm.view(np.uint32))
+    q, _, _ = block_fields(W, rows, K)
+    b = W.reshape(rows, K // 256, 144)
+    d = b[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
+    dmin = b[:, :, 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
+    sc, mn = scales_mins(W, rows, K)
+    na = rows * K * 2
+    A = packed[:na].view(np.float16).reshape(rows, K)
+    assert np.array_equal(A.astype(np.int32), (np.repeat(sc, 32, axis=2).reshape(rows, K) * q))
+    nx = (rows * K // 4 * 2 + 255) // 256 * 256
+    Ax = packed[na:na + rows * K // 4 * 2].view(np.uint16).reshape(rows, K // 256, 4, 16)
+    rows128 = (rows + 127) // 128 * 128
+    D = packed[na + nx:].view(np.float32).reshape(K // 256, rows128)[:, :rows].T
+    Dref = np.where(d == 0, np.float32(1), d)
+    assert np.array_equal(D.view(np.uint32), Dref.view(np.uint32))
+    c = -((dmin[..., None] * mn.astype(np.float32)).astype(np.float32) / Dref[..., None])
+    parts = bf16_to_f64(Ax[..., :12]).reshape(rows, K // 256, 8, 6)
+    assert np.all(Ax[..., 12:] == 0)
+    assert np.array_equal(parts[..., 0], parts[..., 1]) and np.array_equal(parts[..., 0], parts[..., 3])
+    assert np.array_equal(parts[..., 2], parts[..., 4])
+    assert np.array_equal(parts[..., 0] + parts[..., 2] + parts[..., 5], c.astype(np.float32).astype(np.float64))
 
 
 @pytest.mark.parametrize("rows,K,T", [
@@ -102,6 +132,22 @@ def test_prefill_down_shape_long_k(ctx):
     packed = ctx.q4k_prefill_pack(dev(W), rows, K)
     Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
     check(W, X, rows, K, Y)
+
+
+def test_prefill_token_magnitudes(ctx):
+    """Tokens scaled by 2^-60 .. 2^40: the per-token power of two keeps B in
+    fp16 range, so the relative error does not depend on the magnitude."""
+    rows, K, T = 128, 1024, 6
+    W, X = make(rows, K, T, seed=8)
+    for t, e in enumerate([-60, -20, 0, 13, 25, 40]):
+        X[t] *= np.float32(2.0 ** e)
+    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
+    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    check(W, X, rows, K, Y)
+    xq, sx, sq = O.quantize_act(X)
+    yref, _ = O.q4k_matmul(W, rows, K, xq, sx, sq)
+    for t in range(T):
+        assert O.normwise_rel_err(Y[t], yref[t]) < TOL
 
 
 def test_prefill_zero_and_spike_tokens(ctx):
