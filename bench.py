@@ -296,6 +296,178 @@ def run_ste_case(args):
     ctx.close()
 
 
+PREFILL_T = 512
+
+
+def run_prefill_case(args):
+    """Qwen2.5-7B-shape prefill: T = 512 tokens through every Q4_K matrix of
+    the 28 layers (qkv 4608x3584, o 3584x3584, gate/up 37888x3584, down
+    3584x18944) on the tcgen05 prefill kernel.  One step = the 112 matmuls;
+    the metric is int8-equivalent ops (2 T rows K) per second.  Prints its own
+    JSON line (not the decode line)."""
+    import torch
+
+    import lalmodel_b200 as lb
+
+    c = CFG
+    T = PREFILL_T
+    ctx = lb.Context(0)
+    mats = layer_mats(c)
+    big = max(r * k for r, k in mats)
+    tmp = torch.empty(big, dtype=torch.float32, device="cuda")
+    packed, q4k_o = [], None
+    for l in range(c["n_layer"]):
+        for j, (rows, K) in enumerate(mats):
+            w = tmp[: rows * K].view(rows, K)
+            ctx.fill_normal(w, seed=1234 + 16 * l + j, sigma=0.02)
+            q = ctx.q4k_quantize(w)
+            packed.append(ctx.q4k_prefill_pack(q, rows, K))
+            if l == 0 and j == 1:
+                q4k_o = q.cpu().numpy()   # the CPU sample's matrix
+            del q
+    torch.cuda.synchronize()
+    del tmp, w
+    torch.cuda.empty_cache()
+    X = {K: torch.empty((T, K), dtype=torch.float32, device="cuda") for K in {k for _, k in mats}}
+    for i, K in enumerate(sorted(X)):
+        ctx.fill_normal(X[K], seed=70 + i, sigma=1.0)
+    ws = torch.empty(max(lb.prefill_sizes(r, k, T)[1] for r, k in mats), dtype=torch.uint8,
+                     device="cuda")
+    Y = {r: torch.empty((T, r), dtype=torch.float32, device="cuda") for r in {r for r, _ in mats}}
+    calls = [(packed[4 * l + j], rows, K) for l in range(c["n_layer"]) for j, (rows, K) in enumerate(mats)]
+    ops = sum(2.0 * T * rows * K for _, rows, K in calls)
+    stream = torch.cuda.Stream()
+
+    def step():
+        for P, rows, K in calls:
+            ctx.matmul_q4_k_prefill(P, rows, K, X[K], ws=ws, out=Y[rows])
+
+    with torch.cuda.stream(stream):
+        step()   # first calls set kernel attributes outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    props = torch.cuda.get_device_properties(0)
+    sampler = ClockSampler("%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id,
+                                                 props.pci_device_id))
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            g.replay()
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    tops = ops / (ms * 1e-3) / 1e12
+
+    # the tensor-core kernel alone: one gate/up launch, by events around it
+    P, rows, K = calls[2]
+    with torch.cuda.stream(stream):
+        ctx.matmul_q4_k_prefill(P, rows, K, X[K], ws=ws, out=Y[rows])   # tokens prepared
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_k = 20
+        gk = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gk, stream=stream):
+        for _ in range(n_k):
+            ctx.matmul_q4_k_prefill(P, rows, K, X[K], ws=ws, out=Y[rows])
+    with torch.cuda.stream(stream):
+        gk.replay()
+        k0.record(stream)
+        gk.replay()
+        k1.record(stream)
+    torch.cuda.synchronize()
+    gu_us = k0.elapsed_time(k1) * 1e3 / n_k
+
+    # end to end through the public entry point: the step's token activations
+    # copied in from pinned host memory, the last output copied back
+    hx = {K: v.cpu().pin_memory() for K, v in X.items()}
+    hy = torch.empty(Y[mats[-1][0]].shape, dtype=torch.float32).pin_memory()
+    n_e2e = max(5, min(args.steps, 30))
+    with torch.cuda.stream(stream):
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(n_e2e):
+            for K, v in hx.items():
+                X[K].copy_(v, non_blocking=True)
+            g.replay()
+            hy.copy_(Y[mats[-1][0]], non_blocking=True)
+        f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_tops = ops * n_e2e / (f0.elapsed_time(f1) * 1e-3) / 1e12
+
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            bf16 = float(json.load(fh)["bf16_tflops"])
+        kind = "measured bf16 burst (cuBLAS)"
+    except Exception:
+        bf16, kind = 1590.0, "fallback bf16"
+    # tensor work actually issued: per 64 weights 8 fp16 MMAs (two B parts)
+    # + 1 bf16 min-term MMA of the same width = 2.25 x the int8-equivalent ops
+    work = 2.25 * tops
+
+    cpu = None
+    if not args.no_cpu:
+        O = _cpu_lib()
+        L = O.lib()
+        rows, K = mats[1]
+        xs = X[K][:64].cpu().numpy()
+        xq = np.empty(K, np.int8)
+        sx = np.empty(K // 32, np.float32)
+        sq = np.empty(K // 32, np.int32)
+        y = np.empty(rows, np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < args.cpu_seconds:
+            L.lalb_cpu_quantize_act(O._p(np.ascontiguousarray(xs[n % 64])), 1, K, O._p(xq), O._p(sx),
+                                    O._p(sq))
+            L.lalb_cpu_q4k_gemv(O._p(q4k_o), rows, K, O._p(xq), O._p(sx), O._p(sq), O._p(y))
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        cpu_tops = 2.0 * rows * K / dt / 1e12
+        cpu = {"value": round(cpu_tops, 5), "unit": "TOPS", "cores": L.lalb_cpu_threads(),
+               "kind": "port",
+               "sample": "%d tokens x the layer-0 o matrix (%dx%d Q4_K), one AVX2 GEMV per token "
+                         "(the reference has no batched kernel), %.2f ms each; step time at this "
+                         "rate %.1f s" % (n, rows, K, dt * 1e3, ops / (cpu_tops * 1e12))}
+    in_bytes = sum(v.numel() * 4 for v in hx.values())
+    line = {"case": "prefill-7b", "metric": "Qwen2.5-7B-shape prefill int8 TOPS (M=512)",
+            "value": round(tops, 2), "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x uint4 semantics; tensor cores: fp16 sc*q (exact) x xq*sx in two fp16 "
+                     "parts, min terms in three bf16 parts, fp32 accumulate",
+            "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_K on the GPU, seeded "
+                    "N(0,1) activations",
+            "config": {"workload": "qwen2.5-7b-shape prefill: %d tokens x %d layers x (qkv 4608x3584, "
+                                   "o 3584x3584, gate/up 37888x3584, down 3584x18944) Q4_K"
+                                   % (T, c["n_layer"]),
+                       "tokens": T, "matmuls_per_step": len(calls), "ops_per_step": ops,
+                       "l2": "inputs larger than L2: %.1f GB of packed weights per step"
+                             % (sum(lb.prefill_sizes(r, k, T)[0] for _, r, k in calls) / 1e9)},
+            "roofline": {"kernel": "prefill_tc_kernel", "bound": "tensor",
+                         "achieved": round(work, 1), "peak": bf16, "peak_kind": kind,
+                         "unit": "TFLOP/s", "frac": round(work / bf16, 4),
+                         "note": "achieved = issued fp16/bf16 tensor work (2.25 x the int8-"
+                                 "equivalent ops) over the whole step",
+                         "gate_up_launch_us": round(gu_us, 2),
+                         "gate_up_tensor_tflops": round(2.25 * 2 * T * mats[2][0] * mats[2][1]
+                                                        / (gu_us * 1e-6) / 1e12, 1),
+                         "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_tops, 2), "unit": "TOPS", "h2d_bytes_per_step": in_bytes,
+                    "d2h_bytes_per_step": hy.numel() * 4},
+            "gpu_launches": args.steps * 2 * len(calls),
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def run_gemv_case(args):
     """Only the single-GEMV workload (4 rotating copies, 153 MB > L2): a small
     case for profiler captures, not a bench line."""
@@ -614,9 +786,10 @@ def main():
                     help="smaller LM head: only for profiling captures, not a bench line")
     ap.add_argument("--path", default="auto", choices=["auto", "kernels", "persistent"],
                     help="decoder path: one persistent kernel per token, or one kernel per matvec")
-    ap.add_argument("--case", default="decode", choices=["decode", "gemv", "ste"],
+    ap.add_argument("--case", default="decode", choices=["decode", "gemv", "ste", "prefill"],
                     help="gemv: only the single 18944x3584 GEMV, for profiler captures; "
-                         "ste: the seed STE model's forward matmuls (its own line)")
+                         "ste: the seed STE model's forward matmuls (its own line); "
+                         "prefill: the 7B-shape prefill of 512 tokens (its own line)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -631,6 +804,8 @@ def main():
         run_gemv_case(args)
     elif args.case == "ste":
         run_ste_case(args)
+    elif args.case == "prefill":
+        run_prefill_case(args)
     else:
         run_gpu(args, rank, world, local_rank)
 
