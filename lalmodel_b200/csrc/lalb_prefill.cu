@@ -78,6 +78,7 @@ constexpr int kSbSlots = 2;
 constexpr uint32_t kPSmem = 1024 + kPStages * kPStage + kSbSlots * kSbBytes + 512;
 static_assert(kPStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 static_assert(kPSmem <= 232448, "fits the 227 KB opt-in shared memory");
+constexpr int kActThreads = 1024, kActUnroll = 2;   // token preparation: 32 warps x 2 x 4 blocks in flight
 
 // kind::f16: f32 accumulator, fp16 A and B, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
@@ -377,9 +378,13 @@ __global__ void prefill_act_kernel(const float *__restrict__ X, int T, int K, __
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
     const int nb = K / 32;
     const float *x = X + (size_t)t * K;
-    // pass 1: the token's largest |x|
+    // pass 1: the token's largest |x| (rows are 16-byte aligned: K % 256 == 0)
     float m = 0.0f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        const float4 v = x4[i];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
     m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
     if (lane == 0) s_amax[warp] = m;
     __syncthreads();
@@ -398,28 +403,52 @@ __global__ void prefill_act_kernel(const float *__restrict__ X, int T, int K, __
     __syncthreads();
     const float sc2 = s_scale;
     __nv_bfloat16 *bx = Bx + (size_t)t * (K / 4);
-    // pass 2: one warp per 32-block
-    for (int j = warp; j < nb; j += nwarp) {
-        const float v = x[j * 32 + lane];
-        const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
-        const float d = __fdiv_rn(__uint_as_float(amax), 127.0f);
-        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        const float tq = roundf(__fmul_rn(v, id));
-        const int qv = tq > 127.0f ? 127 : (tq < -127.0f ? -127 : (int)tq);
-        const int s = __reduce_add_sync(0xffffffffu, qv);
-        const float b = __fmul_rn(__fmul_rn((float)qv, d), sc2);
-        const __half bh = __float2half_rn(b);
-        Bh[(size_t)t * K + j * 32 + lane] = bh;
-        Bl[(size_t)t * K + j * 32 + lane] = __float2half_rn(b - __half2float(bh));
-        // this sub-block's min-term parts: 16 values per pair of sub-blocks
-        __nv_bfloat16 *o = bx + (j >> 1) * 16;
-        if (lane == 0) {
-            __nv_bfloat16 a0, a1, a2;
-            split3_bf16(__fmul_rn(__fmul_rn(d, (float)s), sc2), a0, a1, a2);
-            __nv_bfloat16 *p = o + (j & 1) * 6;
-            p[0] = a0; p[1] = a1; p[2] = a0; p[3] = a2; p[4] = a1; p[5] = a0;
-        } else if ((j & 1) == 0 && lane < 5) {
-            o[12 + lane - 1] = __float2bfloat16_rn(0.0f);
+    // pass 2: a warp takes 4 consecutive 32-blocks (128 elements), a lane 4
+    // consecutive elements, so a block is 8 lanes; kActUnroll groups per round
+    const int ngrp = nb / 4;                 // K % 256 == 0: whole groups
+    const int sub = lane & 7;                // lane within its block
+    for (int g0 = warp; g0 < ngrp; g0 += nwarp * kActUnroll) {
+#pragma unroll
+        for (int u = 0; u < kActUnroll; ++u) {
+            const int g = g0 + u * nwarp;
+            if (g >= ngrp) break;
+            const int j = g * 4 + (lane >> 3);   // this lane's block
+            const float4 v = x4[g * 32 + lane];
+            float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+            const float d = __fdiv_rn(a, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+            int qv[4], sq = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float tq = roundf(__fmul_rn(vv[e], id));
+                qv[e] = tq > 127.0f ? 127 : (tq < -127.0f ? -127 : (int)tq);
+                sq += qv[e];
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            __align__(8) __half hh[4], hl[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float b = __fmul_rn(__fmul_rn((float)qv[e], d), sc2);
+                hh[e] = __float2half_rn(b);
+                hl[e] = __float2half_rn(b - __half2float(hh[e]));
+            }
+            const size_t off = (size_t)t * K + (size_t)g * 128 + lane * 4;
+            *reinterpret_cast<uint2 *>(Bh + off) = *reinterpret_cast<const uint2 *>(hh);
+            *reinterpret_cast<uint2 *>(Bl + off) = *reinterpret_cast<const uint2 *>(hl);
+            // the block's min-term parts: 16 values per pair of blocks
+            __nv_bfloat16 *o = bx + (j >> 1) * 16;
+            if (sub == 0) {
+                __nv_bfloat16 a0, a1, a2;
+                split3_bf16(__fmul_rn(__fmul_rn(d, (float)sq), sc2), a0, a1, a2);
+                __nv_bfloat16 *p = o + (j & 1) * 6;
+                p[0] = a0; p[1] = a1; p[2] = a0; p[3] = a2; p[4] = a1; p[5] = a0;
+            } else if ((j & 1) == 0 && sub < 5) {
+                o[12 + sub - 1] = __float2bfloat16_rn(0.0f);
+            }
         }
     }
 }
@@ -507,7 +536,7 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, cons
     __nv_bfloat16 *Bx = reinterpret_cast<__nv_bfloat16 *>(w + 2 * act_b_bytes(T, K));
     float *inv = reinterpret_cast<float *>(w + 2 * act_b_bytes(T, K) + act_bx_bytes(T, K));
     const int Tp = tokens_padded(T);
-    prefill_act_kernel<<<T, 256, 0, s>>>(X, T, K, Bh, Bl, Bx, inv);
+    prefill_act_kernel<<<T, kActThreads, 0, s>>>(X, T, K, Bh, Bl, Bx, inv);
     LALB_LAUNCH_CHECK(ctx, "prefill_act_kernel");
     CUtensorMap mA, mBh, mBl, mAx, mBx, mRS;
     int st;
