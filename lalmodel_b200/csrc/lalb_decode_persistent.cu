@@ -399,8 +399,10 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
         for (int k = 0; k < 4; ++k) {
             const int c = lane + 32 * k;
             if (c < NS) {
-                const int4 lo = *reinterpret_cast<const int4 *>(cs.xq_s + 32 * c);
-                const int4 hi = *reinterpret_cast<const int4 *>(cs.xq_s + 32 * c + 16);
+                // block c = chunks 2(c%4), 2(c%4)+1 of half-block c/4 (swizzled layout)
+                const int4 *xs = reinterpret_cast<const int4 *>(cs.xq_s);
+                const int4 lo = xs[xq_swz_chunk(c >> 2, 2 * (c & 3))];
+                const int4 hi = xs[xq_swz_chunk(c >> 2, 2 * (c & 3) + 1)];
                 xv[8 * k + 0] = lo.x; xv[8 * k + 1] = lo.y;
                 xv[8 * k + 2] = lo.z; xv[8 * k + 3] = lo.w;
                 xv[8 * k + 4] = hi.x; xv[8 * k + 5] = hi.y;
@@ -415,16 +417,20 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
         const int4 *pp = reinterpret_cast<const int4 *>(cs.xq_s + 128 * c);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int4 v = pp[j];
+            const int4 v = pp[j ^ (c & 7)];   // swizzled: conflict-free across lanes
             xv[4 * j] = v.x;
             xv[4 * j + 1] = v.y;
             xv[4 * j + 2] = v.z;
             xv[4 * j + 3] = v.w;
         }
+        const float4 sx4 = reinterpret_cast<const float4 *>(cs.sx_s)[c];   // one 16-byte load each
+        const int4 sq4 = reinterpret_cast<const int4 *>(cs.sq_s)[c];
+        const float sxa[4] = {sx4.x, sx4.y, sx4.z, sx4.w};
+        const int sqa[4] = {sq4.x, sq4.y, sq4.z, sq4.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            sxd[j] = (double)cs.sx_s[4 * c + j];
-            ad[j] = sxd[j] * (double)cs.sq_s[4 * c + j];
+            sxd[j] = (double)sxa[j];
+            ad[j] = sxd[j] * (double)sqa[j];
         }
     }
     const int cc = min(lane, NH - 1);
@@ -791,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 const int blk = ps * kQuads + quad;
                 // whole warps take part (the quad shuffles need every lane)
                 if (ps * kQuads + (ct & ~31) / 4 < NS)
-                    quantize_block_quad(v[ps], qi, blk < NS, xq_s + blk * 32, sx_s + blk, sq_s + blk);
+                    quantize_block_quad_swz(v[ps], qi, blk < NS, xq_s, blk, sx_s + blk, sq_s + blk);
             }
         }
         if (d.kind == kGu && ct < kMaxTiles) tcnt_s[ct] = 0;

@@ -67,6 +67,21 @@ __device__ __forceinline__ void quantize_block_quad(const float (&v)[8], int qi,
     }
 }
 
+// Shared-memory layout of a quantized activation read back per 128-element
+// half-block (one lane's 8 x 16-byte loads): 16-byte chunk q of half-block c
+// is stored at chunk q ^ (c & 7) of that half-block, so that the lanes of a
+// 128-bit load phase (consecutive c) hit distinct banks.
+__device__ __forceinline__ int xq_swz_chunk(int c, int q) { return (c << 3) | (q ^ (c & 7)); }
+
+// quantize_block_quad writing block blk of the swizzled layout at xq_s.
+__device__ __forceinline__ void quantize_block_quad_swz(const float (&v)[8], int qi, bool store,
+                                                        int8_t *xq_s, int blk, float *sx, int *sumq) {
+    // this thread's 8 bytes: byte 8*qi of block blk = half-block blk/4, chunk
+    // 2*(blk%4) + qi/2, offset 8*(qi%2); quantize_block_quad adds 8*qi itself
+    int8_t *dst = xq_s + 16 * xq_swz_chunk(blk >> 2, 2 * (blk & 3) + (qi >> 1)) + 8 * (qi & 1) - 8 * qi;
+    quantize_block_quad(v, qi, store, dst, sx, sumq);
+}
+
 __device__ __forceinline__ void load8(const float *x, bool vec, float (&v)[8]) {
     if (vec) {
         const float4 a = reinterpret_cast<const float4 *>(x)[0];

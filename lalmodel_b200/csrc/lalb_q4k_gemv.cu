@@ -154,23 +154,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
 
     // ---- activation prologue -------------------------------------------------
     if (IN == kInQ8) {
+        // the int8 activation goes into the swizzled layout (xq_swz_chunk)
         if (a.act_bulk) {
             if (tid == 0) {
-                mbar_arrive_expect_tx(act_bar, (uint32_t)K + 8u * NS);
-                bulk_g2s_plain(xq_s, a.xq, (uint32_t)K, act_bar);
+                mbar_arrive_expect_tx(act_bar, 8u * NS);
                 bulk_g2s_plain(sx_s, a.sx, 4u * NS, act_bar);
                 bulk_g2s_plain(sq_s, a.sumq, 4u * NS, act_bar);
             }
-            mbar_wait_bounded(act_bar, 0, a.status);
         } else {
-            const int4 *src = reinterpret_cast<const int4 *>(a.xq);
-            int4 *dst = reinterpret_cast<int4 *>(xq_s);
-            for (int i = tid; i < K / 16; i += nthreads) dst[i] = src[i];
             for (int i = tid; i < NS; i += nthreads) {
                 sx_s[i] = a.sx[i];
                 sq_s[i] = a.sumq[i];
             }
         }
+        const int4 *src = reinterpret_cast<const int4 *>(a.xq);
+        int4 *dst = reinterpret_cast<int4 *>(xq_s);
+        for (int i = tid; i < K / 16; i += nthreads) dst[xq_swz_chunk(i >> 3, i & 7)] = src[i];
+        if (a.act_bulk) mbar_wait_bounded(act_bar, 0, a.status);
     } else {
         const bool vec = a.act_bulk;  // x is 16-byte aligned
         // a quad of lanes per 32-block; whole warps per pass so the quad
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
             }
             // whole warps take part (the quad shuffles need every lane)
             if (blk0 + (tid & ~31) / 4 < NS)
-                quantize_block_quad(v, qi, have, xq_s + blk * 32, sx_s + blk, sq_s + blk);
+                quantize_block_quad_swz(v, qi, have, xq_s, blk, sx_s + blk, sq_s + blk);
         }
     }
     __syncthreads();
@@ -232,16 +232,20 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
         const int4 *p = reinterpret_cast<const int4 *>(xq_s + 128 * c);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int4 v = p[j];
+            const int4 v = p[j ^ (c & 7)];   // swizzled: conflict-free across lanes
             xv[4 * j + 0] = v.x;
             xv[4 * j + 1] = v.y;
             xv[4 * j + 2] = v.z;
             xv[4 * j + 3] = v.w;
         }
+        const float4 sx4 = reinterpret_cast<const float4 *>(sx_s)[c];   // one 16-byte load each
+        const int4 sq4 = reinterpret_cast<const int4 *>(sq_s)[c];
+        const float sxa[4] = {sx4.x, sx4.y, sx4.z, sx4.w};
+        const int sqa[4] = {sq4.x, sq4.y, sq4.z, sq4.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            sxd[j] = (double)sx_s[4 * c + j];
-            ad[j] = sxd[j] * (double)sq_s[4 * c + j];
+            sxd[j] = (double)sxa[j];
+            ad[j] = sxd[j] * (double)sqa[j];
         }
     } else {
 #pragma unroll
