@@ -7,27 +7,33 @@
 // both K-major.  Each is given as one or two tf32 parts (x = hi + lo, each
 // part exactly representable in tf32, so |x - hi - lo| <= 2^-22 |x|); the
 // kernel accumulates hi*hi + lo*hi (+ hi*lo when B has two parts) in fp32 in
-// TMEM.  This is the seed STE model's forward (BinLayer) on tensor cores:
-// the reference computes it in fp32 on the CPU (runtime/lal_runtime.c
-// bin_forward :1852-1938, bin_forward_pure_float :543-582).
+// TMEM.  This is the seed STE model's
+// forward (BinLayer) on tensor cores: the reference computes it in fp32 on
+// the CPU (runtime/lal_runtime.c bin_forward :1852-1938,
+// bin_forward_pure_float :543-582).
 //
-// One CTA per 128 x 128 output tile, 6 warps:
-//   warp 0  TMA producer: 2-D tiled bulk tensor copies (128-byte swizzle)
-//           of every part's 128 x 32 (A) and 128 x 32 (B) fp32 tiles into a
-//           3-stage ring, completion on a full mbarrier per stage;
-//   warp 1  allocates all 512 TMEM columns (4 accumulators of 128) and
-//           issues tcgen05.mma (kind::tf32, M=128, N=128, K=8 per
-//           instruction) from one lane, K-block kb into accumulator kb % 4;
-//           a tcgen05.commit per stage frees the stage, a final one signals
-//           the accumulators;
-//   warps 2-5  epilogue: each reads its 32 TMEM lanes (= rows) 32 columns at
-//           a time from every accumulator (tcgen05.ld 32x32b.x32), adds
-//           them, transposes through shared memory and writes 128-byte row
-//           segments with the scales and bias.
+// Persistent: one CTA per SM walks the 128 x 128 output tiles (tile t,
+// t + grid, ...), 6 warps:
+//   warp 0     TMA producer: per 32-wide K-block, 2-D tiled copies
+//              (128-byte swizzle) of every part's A and B tiles into a
+//              3-stage ring (full mbarrier per stage);
+//   warp 1     allocates all 512 TMEM columns and issues tcgen05.mma
+//              (kind::tf32, M=128, N=128, K=8 per instruction) from one lane.
+//              K-block kb of a tile goes to accumulator kb % nacc of the
+//              tile's accumulator group; with short K there are two groups
+//              of two accumulators, so the next tile's MMAs run while the
+//              epilogue drains the previous tile; long K uses one group of
+//              four (shorter fp32 accumulation chains in the tensor core);
+//   warps 2-5  epilogue: wait for the group (commit), read each warp's 32
+//              TMEM lanes (= rows) 32 columns at a time from every
+//              accumulator (tcgen05.ld 32x32b.x32), add them, free the group,
+//              transpose through shared memory and write 128-byte row
+//              segments with the scales and bias.
 // Every wait is bounded; on expiry the kernel raises the status word and
-// still commits, drains and frees its TMEM.
+// still drains and frees its TMEM.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "lalb_internal.cuh"
@@ -39,15 +45,14 @@ namespace {
 
 constexpr int BM = 128, BN = 128, BK = 32;     // BK fp32 = 128 B: one 128-byte swizzle row
 constexpr int kStagesTc = 3;
-// K-blocks go round-robin to kAccs accumulators (BN TMEM columns each), so
-// each fp32 accumulation chain in the tensor core is kAccs times shorter;
-// the epilogue adds them
-constexpr int kAccs = 4;
-constexpr int kTmemCols = BN * kAccs;           // 512: the whole TMEM of the SM
-constexpr int kTcThreads = 192;
+constexpr int kTmemCols = 512;                  // the whole TMEM of the SM: 4 accumulators of BN
+constexpr int kLongK = 16;                      // K-blocks above which one group of 4 accumulators is used
+constexpr int kEpiWarpsTc = 4;
+constexpr int kTcThreads = 32 * (2 + kEpiWarpsTc);
 constexpr uint32_t kATile = BM * BK * 4;       // 16 KB
 constexpr uint32_t kBTile = BN * BK * 4;       // 16 KB
-constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;   // up to 2 parts each
+// stage: A hi | A lo | B hi | B lo
+constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
 constexpr uint32_t kEpiBytes = 4 * 32 * 33 * 4;             // per-warp 32x32 transpose
 constexpr uint32_t kTcSmem = 1024 /* alignment slack */ + kStagesTc * kStageBytes + kEpiBytes + 256;
 
@@ -107,6 +112,8 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 struct TcArgs {
     int M, N, K;
     int a_parts, b_parts;       // 1 or 2 each
+    int tiles_n, tiles;         // output tiles along N, in all
+    int nacc, ngroups;          // accumulators per tile, accumulator groups in TMEM
     float *Y;                   // [M][N]
     const float *rowscale;      // [M] or null (1)
     const float *colscale;      // [N] or null (1)
@@ -124,20 +131,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t *stages = smem;
     float *epi = reinterpret_cast<float *>(smem + kStagesTc * kStageBytes);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStagesTc * kStageBytes + kEpiBytes);
-    uint64_t *empty = full + kStagesTc;
-    uint64_t *acc_full = empty + kStagesTc;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    uint64_t *empty = full + kStagesTc;         // the stage's MMAs completed
+    uint64_t *acc_full = empty + kStagesTc;     // [2] a tile's accumulators are complete
+    uint64_t *acc_empty = acc_full + 2;         // [2] the epilogue has read them
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int nk = a.K / BK;
 
     if (threadIdx.x == 0) {
+        // the TMA unit fetches the descriptors while the barriers and TMEM are set up
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA1)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB1)) : "memory");
         for (int s = 0; s < kStagesTc; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(&acc_full[g], 1);
+            mbar_init(&acc_empty[g], kEpiWarpsTc);
+        }
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -156,104 +171,115 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer ----
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % kStagesTc;
-                const uint32_t use = kb / kStagesTc;
-                if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u, a.status)) break;
-                uint8_t *st = stages + (size_t)s * kStageBytes;
-                mbar_arrive_expect_tx(&full[s], stage_tx);
-                tma_load_2d(st, &mA0, kb * BK, m0, &full[s]);
-                if (a.a_parts > 1) tma_load_2d(st + kATile, &mA1, kb * BK, m0, &full[s]);
-                tma_load_2d(st + 2 * kATile, &mB0, kb * BK, n0, &full[s]);
-                if (a.b_parts > 1) tma_load_2d(st + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[s]);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
+                const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % kStagesTc;
+                    const uint32_t use = it / kStagesTc;
+                    if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = stages + (size_t)s * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], stage_tx);
+                    tma_load_2d(st, &mA0, kb * BK, m0, &full[s]);
+                    if (a.a_parts > 1) tma_load_2d(st + kATile, &mA1, kb * BK, m0, &full[s]);
+                    tma_load_2d(st + 2 * kATile, &mB0, kb * BK, n0, &full[s]);
+                    if (a.b_parts > 1) tma_load_2d(st + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---- MMA issuer ----
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % kStagesTc;
-                if (!mbar_wait_bounded(&full[s], (uint32_t)(kb / kStagesTc) & 1u, a.status)) break;
+            uint32_t it = 0, ti = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x, ++ti) {
+                const int g = ti % a.ngroups;
+                const uint32_t gu = ti / a.ngroups;
+                if (gu > 0 && !mbar_wait_bounded(&acc_empty[g], (gu - 1) & 1u, a.status)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t st = smem_u32(stages + (size_t)s * kStageBytes);
-                const uint32_t a0 = st, a1 = st + kATile, b0 = st + 2 * kATile, b1 = b0 + kBTile;
-                const uint32_t td = tmem + (uint32_t)((kb % kAccs) * BN);
-                uint32_t acc = kb >= kAccs;   // the first block of an accumulator overwrites it
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % kStagesTc;
+                    if (!mbar_wait_bounded(&full[s], (it / kStagesTc) & 1u, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t st = smem_u32(stages + (size_t)s * kStageBytes);
+                    const uint32_t a0 = st, a1 = st + kATile, b0 = st + 2 * kATile, b1 = b0 + kBTile;
+                    const uint32_t td = tmem + (uint32_t)((g * a.nacc + kb % a.nacc) * BN);
+                    uint32_t acc = kb >= a.nacc;   // the first block of an accumulator overwrites it
 #pragma unroll
-                for (int k = 0; k < BK / 8; ++k) {   // 8 tf32 = 32 bytes per instruction
-                    const uint32_t ko = k * 32;
-                    mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), acc);
-                    acc = 1;
-                    if (a.a_parts > 1)
-                        mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), 1);
-                    if (a.b_parts > 1)
-                        mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), 1);
+                    for (int k = 0; k < BK / 8; ++k) {   // 8 tf32 = 32 bytes per instruction
+                        const uint32_t ko = k * 32;
+                        mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), acc);
+                        acc = 1;
+                        if (a.a_parts > 1)
+                            mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), 1);
+                        if (a.b_parts > 1)
+                            mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), 1);
+                    }
+                    mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
                 }
-                mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
+                mma_commit(&acc_full[g]);    // arrives when every MMA of the tile has completed
             }
-            mma_commit(acc_full);        // arrives when every issued MMA has completed
         }
     } else {
         // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
         const int q = warp & 3;
         float *st = epi + (size_t)(warp - 2) * 32 * 33;
-        mbar_wait_bounded(acc_full, 0, a.status);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int nacc = nk < kAccs ? nk : kAccs;
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            float sum[32];
+        const int nacc = nk < a.nacc ? nk : a.nacc;
+        uint32_t ti = 0;
+        for (int t = blockIdx.x; t < a.tiles; t += gridDim.x, ++ti) {
+            const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * BN;
+            const int g = ti % a.ngroups;
+            if (!mbar_wait_bounded(&acc_full[g], (ti / a.ngroups) & 1u, a.status)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float sum[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
-            for (int ai = 0; ai < nacc; ++ai) {
-                uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ai * BN + c0), r);
+                for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+                for (int ai = 0; ai < nacc; ++ai) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((g * a.nacc + ai) * BN + c0), r);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
-            }
-            // lane holds row q*32 + lane, columns c0..c0+31
-#pragma unroll
-            for (int j = 0; j < 32; ++j) st[lane * 33 + j] = sum[j];
-            __syncwarp();
-            const int n = n0 + c0 + lane;
-            const bool ncol = n < a.N;
-            const float cs = ncol && a.colscale ? a.colscale[n] : 1.0f;
-            const float b = ncol && a.bias ? a.bias[n] : 0.0f;
-            for (int j = 0; j < 32; ++j) {
-                const int m = m0 + q * 32 + j;
-                if (m < a.M && ncol) {
-                    const float rs = a.rowscale ? a.rowscale[m] : 1.0f;
-                    a.Y[(size_t)m * a.N + n] = __fadd_rn(__fmul_rn(__fmul_rn(st[j * 33 + lane], rs), cs), b);
+                    for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
                 }
+                if (c0 == BN - 32) {   // the group's last columns are in registers: free it
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[g]);
+                }
+                // lane holds row q*32 + lane, columns c0..c0+31
+#pragma unroll
+                for (int j = 0; j < 32; ++j) st[lane * 33 + j] = sum[j];
+                __syncwarp();
+                const int n = n0 + c0 + lane;
+                const bool ncol = n < a.N;
+                const float cs = ncol && a.colscale ? a.colscale[n] : 1.0f;
+                const float b = ncol && a.bias ? a.bias[n] : 0.0f;
+                for (int j = 0; j < 32; ++j) {
+                    const int m = m0 + q * 32 + j;
+                    if (m < a.M && ncol) {
+                        const float rs = a.rowscale ? a.rowscale[m] : 1.0f;
+                        a.Y[(size_t)m * a.N + n] = __fadd_rn(__fmul_rn(__fmul_rn(st[j * 33 + lane], rs), cs), b);
+                    }
+                }
+                __syncwarp();
             }
-            __syncwarp();
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     }
     __syncthreads();
     if (warp == 1) {
-        // every MMA has completed before the columns go back (bounded)
-        if (lane == 0) mbar_wait_bounded(acc_full, 0, a.status);
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(kTmemCols)
                      : "memory");
-    }
-}
-
-// fp32 -> (hi, lo) tf32 parts: hi = tf32(x) (round to nearest, ties away),
-// lo = tf32(x - hi).
-__global__ void split_tf32_kernel(const float *__restrict__ x, float *__restrict__ hi,
-                                  float *__restrict__ lo, size_t n) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-         i += (size_t)gridDim.x * blockDim.x) {
-        const float v = x[i];
-        uint32_t h, l;
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
-        const float r = __fsub_rn(v, __uint_as_float(h));
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
-        hi[i] = __uint_as_float(h);
-        if (lo) lo[i] = __uint_as_float(l);
     }
 }
 
@@ -294,6 +320,22 @@ int make_map(lalb_ctx *ctx, CUtensorMap *m, const float *base, int rows, int K, 
 
 }  // namespace
 
+// fp32 -> (hi, lo) tf32 parts: hi = tf32(x) (round to nearest, ties away),
+// lo = tf32(x - hi).
+__global__ void split_tf32_kernel(const float *__restrict__ x, float *__restrict__ hi,
+                                  float *__restrict__ lo, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        uint32_t h, l;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+        const float r = __fsub_rn(v, __uint_as_float(h));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+        hi[i] = __uint_as_float(h);
+        if (lo) lo[i] = __uint_as_float(l);
+    }
+}
+
 int lalb_split_tf32(lalb_ctx *ctx, const float *x, float *hi, float *lo, size_t n, cudaStream_t s) {
     if (n == 0) return LALB_OK;
     const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
@@ -320,12 +362,17 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     a.K = p.K;
     a.a_parts = p.a_lo ? 2 : 1;
     a.b_parts = p.b_lo ? 2 : 1;
+    a.tiles_n = (p.N + BN - 1) / BN;
+    a.tiles = a.tiles_n * ((p.M + BM - 1) / BM);
+    const bool long_k = p.K / BK > kLongK;
+    a.nacc = long_k ? 4 : 2;
+    a.ngroups = long_k ? 1 : 2;
     a.Y = p.Y;
     a.rowscale = p.rowscale;
     a.colscale = p.colscale;
     a.bias = p.bias;
     a.status = &ctx->scratch->status;
-    const dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+    const int grid = std::min(a.tiles, ctx->sm_count);
     tc_gemm_tf32_kernel<<<grid, kTcThreads, kTcSmem, s>>>(mA0, mA1, mB0, mB1, a);
     LALB_LAUNCH_CHECK(ctx, "tc_gemm_tf32_kernel");
     return LALB_OK;
