@@ -237,10 +237,12 @@ LALB_API int lalb_decoder_trace_step(lalb_decoder *dec, const float *h_in,
  * A decoder may hold one rank of n_rank (one process or thread per GPU) or
  * every rank at once on one GPU (rank = -1: the ranks run as groups of CTAs
  * of one launch; for tests and for GPUs short of peers).  Rank r holds rows
- * lalb_tp_rows(cfg, n_rank, r, matrix) of every matrix: 0 qkv, 1 o,
- * 2 gate/up (whole 64-row gate/up tiles), 3 down, 4 LM head.  Each rank's
- * CTAs write their output rows into every rank's exchange buffer over
- * NVLink and wait on every rank's phase counters; the argmax is the first
+ * lalb_tp_rows(cfg, n_rank, r, matrix) of every matrix: 0 qkv and 1 o in
+ * full (every rank computes q and the residual update itself), 2 gate/up
+ * (whole 64-row gate/up tiles), 3 down and 4 LM head split.  Each rank's
+ * CTAs write their gate/up and down output rows into every rank's exchange
+ * buffer over NVLink and wait on every rank's phase counters after those
+ * phases (two cross-GPU exchanges per layer); the argmax is the first
  * maximum over all ranks' rows.  Steps run on the persistent path only. */
 #define LALB_IPC_HANDLE_BYTES 64
 LALB_API int lalb_tp_rows(const lalb_decoder_cfg *cfg, int n_rank, int rank, int matrix,

@@ -175,10 +175,14 @@ IPC_HANDLE_BYTES = 64   # LALB_IPC_HANDLE_BYTES
 
 def tp_range(cfg, matrix, n_rank, rank):
     """Pure-Python statement of lalb_tp_rows (rows [r0, r1) of `matrix` that
-    `rank` of `n_rank` holds; cfg is a dict of the decoder shapes)."""
-    if matrix == 0:
-        units, unit = cfg["q_rows"] + 2 * cfg["kv_rows"], 1
-    elif matrix in (1, 3):
+    `rank` of `n_rank` holds; cfg is a dict of the decoder shapes).  qkv (0)
+    and o (1) are held whole by every rank; gate/up (2, whole 64-row tiles),
+    down (3) and the LM head (4) are split."""
+    if matrix == 0:   # qkv and o: every rank holds all rows
+        return 0, cfg["q_rows"] + 2 * cfg["kv_rows"]
+    if matrix == 1:
+        return 0, cfg["hidden"]
+    if matrix == 3:
         units, unit = cfg["hidden"], 1
     elif matrix == 2:
         units, unit = 2 * cfg["ffn"] // 64, 64

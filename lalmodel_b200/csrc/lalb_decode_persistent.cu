@@ -230,9 +230,14 @@ __device__ __forceinline__ void cons_bar() {
 // as this rank's status word is raised (then every later wait of the token
 // is skipped: a failed token ends in seconds, not one time-out per wait).
 // Returns false on failure.
+// Phases whose outputs go to other ranks (gate/up, down): their barrier waits
+// for every rank; after qkv and o (computed whole on every rank) a rank only
+// waits for its own CTAs.
+__device__ __forceinline__ bool cross_phase(int ph) { return (ph & 3) >= 2; }
+
 __device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &own, int rank,
                                             int ph, unsigned int seq) {
-    const unsigned int nl = a.cta_per_rank, nr = a.n_rank - 1;
+    const unsigned int nl = a.cta_per_rank, nr = cross_phase(ph) ? a.n_rank - 1 : 0;
     const unsigned int t_local = (seq + 1u) * nl;
     unsigned int *lbar = own.gbar + ph;
     if (nr == 0) {
@@ -257,7 +262,7 @@ __device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &o
 
 __device__ __forceinline__ bool grid_wait(const PersistArgs &a, const XView &own, int ph,
                                           unsigned int seq) {
-    const unsigned int nl = a.cta_per_rank, nr = a.n_rank - 1;
+    const unsigned int nl = a.cta_per_rank, nr = cross_phase(ph) ? a.n_rank - 1 : 0;
     const unsigned int t_local = (seq + 1u) * nl, t_remote = (seq + 1u) * nr;
     unsigned int *lbar = own.gbar + ph;
     unsigned int *rbar = own.gbar + 4 * a.n_layer + ph;
@@ -547,16 +552,11 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                 const float prev = __shfl_sync(0xffffffffu, pre, (r4 + myrow) & 31);
                 const int lr = r4 + myrow, row = rs + lr, grow = d.goff + row;
                 if ((lane & 7) == 0 && lr < nr) {
-                    // q and the residual rows go to every rank; k and v are not
-                    // read downstream (the attention is out of scope)
-                    if (KIND == kQkv && grow < a.q_rows)
-                        for (int j = 0; j < a.n_rank; ++j)
-                            reinterpret_cast<float *>(a.xb[j] + XL.q)[grow] = (float)v;
-                    if (KIND == kO) {
-                        const float hv = __fadd_rn(prev, (float)v);
-                        for (int j = 0; j < a.n_rank; ++j)
-                            reinterpret_cast<float *>(a.xb[j] + XL.h)[grow] = hv;
-                    }
+                    // every rank computes all of q and of the residual update, so
+                    // they stay in its own buffer; k and v are not read downstream
+                    // (the attention is out of scope)
+                    if (KIND == kQkv && grow < a.q_rows) own.q[grow] = (float)v;
+                    if (KIND == kO) own.h[grow] = __fadd_rn(prev, (float)v);
                     if (KIND == kGu) cs.tile_s[row - d.r0] = (float)v;   // gate/up tile entry
                 }
             }

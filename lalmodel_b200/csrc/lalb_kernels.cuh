@@ -67,9 +67,11 @@ int lalb_launch_q8_head(lalb_ctx *ctx, const Q8HeadArgs &a, int in, cudaStream_t
 
 // One decode token in a single persistent, cooperative kernel, optionally
 // tensor-parallel over n_rank GPUs.  Every rank holds a contiguous shard of
-// the rows of every matrix (lalb_tp_range) and an exchange buffer with the
-// full activations; a CTA stores its output rows into every rank's buffer
-// (peer memory over NVLink) and arrives on every rank's phase counter.
+// the rows of gate/up, down and the LM head, all rows of qkv and o
+// (lalb_tp_range), and an exchange buffer with the full activations.  A CTA
+// stores its gate/up and down output rows into every rank's buffer (peer
+// memory over NVLink); qkv and o outputs stay in the rank's own buffer, and
+// the barriers after them are the rank's own.
 constexpr int kPersistMaxRanks = 8;
 
 struct PersistRank {                    // one rank's weight shards (device)
@@ -134,8 +136,12 @@ __host__ __device__ inline void lalb_tp_range(const lalb_decoder_cfg &c, int whi
                                               int *row0, int *row1) {
     int units, unit = 1;
     switch (which) {
-        case 0: units = c.q_rows + 2 * c.kv_rows; break;
-        case 1: case 3: units = c.hidden; break;
+        // qkv and o are small (16 MB per layer at the 7B shape): every rank
+        // holds all their rows and computes q and the residual update
+        // itself, so only gate/up, down and the head exchange across GPUs
+        case 0: *row0 = 0; *row1 = c.q_rows + 2 * c.kv_rows; return;
+        case 1: *row0 = 0; *row1 = c.hidden; return;
+        case 3: units = c.hidden; break;
         case 2: units = 2 * c.ffn / 64; unit = 64; break;
         default: units = c.vocab; break;
     }

@@ -1,7 +1,8 @@
 """Tensor-parallel decode: host-side logic on CPU.
 
-Row shards (lalb_tp_rows and its Python statement), the reassembly of
-sharded row-major weights, and the gathering of every rank's exchange-buffer
+Row shards (lalb_tp_rows and its Python statement: qkv and o whole on every
+rank, gate/up, down and the LM head split), the reassembly of sharded
+row-major weights, and the gathering of every rank's exchange-buffer
 handle over a 2-rank gloo process group.  The device path is covered by the
 gpu-marked tests in test_gpu_tp.py."""
 import ctypes
@@ -31,12 +32,15 @@ def lib_rows(cfg, n, r, m):
 
 @pytest.mark.parametrize("cfg", [QWEN, SMALL])
 @pytest.mark.parametrize("n", [1, 2, 3, 4, 8])
-def test_shards_partition_every_matrix(cfg, n):
+def test_shards_partition_the_split_matrices(cfg, n):
     totals = [cfg["q_rows"] + 2 * cfg["kv_rows"], cfg["hidden"], 2 * cfg["ffn"], cfg["hidden"],
               cfg["vocab"]]
     for m, total in enumerate(totals):
         bounds = [lb.tp_range(cfg, m, n, r) for r in range(n)]
         assert bounds == [lib_rows(cfg, n, r, m) for r in range(n)]
+        if m in (0, 1):   # qkv and o: every rank holds every row
+            assert bounds == [(0, total)] * n
+            continue
         assert bounds[0][0] == 0 and bounds[-1][1] == total
         for (a0, a1), (b0, b1) in zip(bounds, bounds[1:]):
             assert a1 == b0 and a0 <= a1
@@ -57,7 +61,7 @@ def test_row_shards_reassemble_q4k_bytes():
     w = np.random.default_rng(3).integers(0, 256, size=(rows, K // 256 * 144), dtype=np.uint8)
     t = torch.from_numpy(w)
     cfg = dict(SMALL, hidden=rows)
-    parts = [lb.shard_rows(t, *lb.tp_range(cfg, 1, 3, r)) for r in range(3)]
+    parts = [lb.shard_rows(t, *lb.tp_range(cfg, 3, 3, r)) for r in range(3)]
     assert all(p.is_contiguous() for p in parts)
     assert torch.equal(torch.cat(parts), t)
 
