@@ -288,7 +288,9 @@ def run_ste_case(args):
             "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
                          "tensor_work": round(2 * tflops, 2), "peak": tf32_peak,
                          "peak_kind": kind, "unit": "TFLOP/s",
-                         "frac": round(2 * tflops / tf32_peak, 4)},
+                         "frac": round(2 * tflops / tf32_peak, 4),
+                         "traffic_head_launch": profile_traffic("tc_gemm_ste_head_ncu.md",
+                                                                "traffic_bytes_per_launch")},
             "cpu_baseline": cpu}
     print(json.dumps(line), flush=True)
     for L in layers:
@@ -607,8 +609,9 @@ def run_gpu(args, rank, world, local_rank):
         roofline = {"kernel": "q4k_gemv (the %d Q4_K matvec launches of a token)" % q4k_launches,
                     "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                    "traffic": profile_traffic("q4k_gemv_decode7b_ncu.md",
-                                               "traffic_bytes_per_launch"),
+                    # measured DRAM/algorithmic ratio of the GEMV (ncu) x this average launch
+                    "traffic": (lambda r: r and round(r * q4k_bytes_tok / q4k_launches))(
+                        profile_traffic("q4k_gemv_decode7b_ncu.md", "traffic_ratio")),
                     "bytes_per_launch_avg": q4k_bytes_tok / q4k_launches,
                     "us_per_launch_avg": round(q4k_us / q4k_launches, 3)}
     roofline["step_gbs"] = round(rank_bytes / (ms_per_step * 1e-3) / 1e9, 1)
