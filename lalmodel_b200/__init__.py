@@ -216,6 +216,9 @@ class Decoder:
         self.ctx = ctx
         self.cfg = DecoderCfg(n_layer, hidden, q_rows, kv_rows, ffn, vocab)
         self.n_rank, self.rank = n_rank, rank
+        # the library keeps only device pointers: hold the weight tensors (a
+        # shard built on the fly would otherwise be freed while still in use)
+        self._keep = {}
         h = ctypes.c_void_p()
         ctx._call("lalb_decoder_create_tp", ctx.h, ctypes.byref(self.cfg), n_rank, rank,
                   ctypes.byref(h))
@@ -236,9 +239,11 @@ class Decoder:
     def set_layer_shard(self, rank, layer, wqkv, wo, wgu, wdown):
         lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())
         self.ctx._call("lalb_decoder_set_layer_shard", self.h, rank, layer, ctypes.byref(lw))
+        self._keep[("layer", rank, layer)] = (wqkv, wo, wgu, wdown)
 
     def set_lm_head_shard(self, rank, w, sw):
         self.ctx._call("lalb_decoder_set_lm_head_shard", self.h, rank, _p(w), _p(sw))
+        self._keep[("head", rank)] = (w, sw)
 
     def ipc_handle(self):
         """This rank's exchange-buffer handle (bytes) for the other ranks."""
@@ -256,9 +261,11 @@ class Decoder:
     def set_layer(self, layer, wqkv, wo, wgu, wdown):
         lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())
         self.ctx._call("lalb_decoder_set_layer", self.h, layer, ctypes.byref(lw))
+        self._keep[("layer", 0, layer)] = (wqkv, wo, wgu, wdown)
 
     def set_lm_head(self, w, sw):
         self.ctx._call("lalb_decoder_set_lm_head", self.h, _p(w), _p(sw))
+        self._keep[("head", 0)] = (w, sw)
 
     def step(self, h_in, h_out=None, logits=None, argmax=None):
         self.ctx._call("lalb_decoder_step", self.h, _p(h_in), _p(h_out), _p(logits),

@@ -286,3 +286,26 @@ def test_decoder_persistent_rejects_unfit_shapes(ctx):
         dec.set_path(7)
     assert e.value.status == -1
     dec.close()
+
+
+def test_decoder_keeps_weights_passed_as_temporaries(ctx):
+    """The library holds device pointers only; the Python decoder must keep
+    the tensors alive, so weights built on the fly still decode correctly
+    after their names are gone and the allocator has reused freed memory."""
+    cfg = dict(n_layer=2, hidden=512, q_rows=512, kv_rows=128, ffn=1024, vocab=3000)
+    layers, dl, lq, ls = make_decoder_weights(cfg, seed=4242, n_vocab=cfg["vocab"])
+    dec = lb.Decoder(ctx, **cfg)
+    for l, w in enumerate(dl):
+        dec.set_layer(l, w["wqkv"].clone(), w["wo"].clone(), w["wgu"].clone(), w["wdown"].clone())
+    dec.set_lm_head(dev(lq), dev(ls))
+    del dl
+    junk = [torch.full((1 << 20,), 255, dtype=torch.uint8, device="cuda") for _ in range(8)]
+    h_in = O.normal(cfg["hidden"], seed=5)
+    ref_h, ref_logits, ref_am = O.decode_chain(layers, lq, ls, h_in, cfg)
+    h_out = torch.empty(cfg["hidden"], dtype=torch.float32, device="cuda")
+    am = torch.empty(1, dtype=torch.int32, device="cuda")
+    dec.step(dev(h_in), h_out, None, am)
+    assert_fp32_parity(host(h_out), ref_h)
+    assert int(host(am)[0]) == ref_am
+    del junk
+    dec.close()
