@@ -34,6 +34,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <initializer_list>
 #include <mutex>
 
 #include "lalb_internal.cuh"
@@ -166,6 +167,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // programmatic dependent launch: the setup above overlapped the previous
+    // kernel's tail; its outputs (A) are read only after it completes
+    pdl_wait();
+    pdl_launch_dependents();
 
     const uint32_t stage_tx = (uint32_t)(a.a_parts * kATile + a.b_parts * kBTile);
     if (warp == 0) {
@@ -318,12 +323,35 @@ int make_map(lalb_ctx *ctx, CUtensorMap *m, const float *base, int rows, int K, 
     return LALB_OK;
 }
 
+// Launch with programmatic dependent launch allowed (the kernels call
+// pdl_wait before reading what the previous kernel wrote).
+int launch_pdl(lalb_ctx *ctx, const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+               std::initializer_list<void *> args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *params[8];
+    int i = 0;
+    for (void *p : args) params[i++] = p;
+    LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, fn, params));
+    return LALB_OK;
+}
+
 }  // namespace
 
 // fp32 -> (hi, lo) tf32 parts: hi = tf32(x) (round to nearest, ties away),
 // lo = tf32(x - hi).
 __global__ void split_tf32_kernel(const float *__restrict__ x, float *__restrict__ hi,
                                   float *__restrict__ lo, size_t n) {
+    pdl_wait();   // x may be the previous kernel's output
+    pdl_launch_dependents();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
         const float v = x[i];
@@ -339,8 +367,9 @@ __global__ void split_tf32_kernel(const float *__restrict__ x, float *__restrict
 int lalb_split_tf32(lalb_ctx *ctx, const float *x, float *hi, float *lo, size_t n, cudaStream_t s) {
     if (n == 0) return LALB_OK;
     const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
-    split_tf32_kernel<<<blocks, 256, 0, s>>>(x, hi, lo, n);
-    LALB_LAUNCH_CHECK(ctx, "split_tf32_kernel");
+    if (int st = launch_pdl(ctx, (const void *)split_tf32_kernel, dim3(blocks), dim3(256), 0, s,
+                            {(void *)&x, (void *)&hi, (void *)&lo, (void *)&n}))
+        return st;
     return LALB_OK;
 }
 
@@ -373,7 +402,6 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     a.bias = p.bias;
     a.status = &ctx->scratch->status;
     const int grid = std::min(a.tiles, ctx->sm_count);
-    tc_gemm_tf32_kernel<<<grid, kTcThreads, kTcSmem, s>>>(mA0, mA1, mB0, mB1, a);
-    LALB_LAUNCH_CHECK(ctx, "tc_gemm_tf32_kernel");
-    return LALB_OK;
+    return launch_pdl(ctx, (const void *)tc_gemm_tf32_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, s,
+                      {(void *)&mA0, (void *)&mA1, (void *)&mB0, (void *)&mB1, (void *)&a});
 }
