@@ -5,6 +5,8 @@
 // controls, int8 dot helpers and the Q4_K scale unpacking.
 #pragma once
 
+#include <initializer_list>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -160,6 +162,27 @@ __device__ __forceinline__ void pdl_wait() {
 // allow the next kernel in the stream to be scheduled early.
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with programmatic dependent launch allowed (the kernels call
+// pdl_wait before reading what the previous kernel wrote).
+inline int launch_pdl(lalb_ctx *ctx, const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+               std::initializer_list<void *> args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *params[8];
+    int i = 0;
+    for (void *p : args) params[i++] = p;
+    LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, fn, params));
+    return LALB_OK;
 }
 
 // ---- misc ------------------------------------------------------------------

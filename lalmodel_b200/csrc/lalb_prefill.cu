@@ -173,6 +173,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mbar_init(&sempty[s], kEpiWarps);
         }
         fence_barrier_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mBh)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mBl)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mAx)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mBx)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mRS)) : "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -185,6 +191,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // programmatic dependent launch: the setup above overlapped the previous
+    // kernel's tail; the token parts it wrote are read only after it completes
+    pdl_wait();
+    pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -364,6 +374,10 @@ __global__ void prefill_act_kernel(const float *__restrict__ X, int T, int K, __
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
     const int nb = K / 32;
     const float *x = X + (size_t)t * K;
+    // X may be the previous kernel's output, and the previous matmul reads the
+    // workspace written here: wait for it before any global access
+    pdl_wait();
+    pdl_launch_dependents();
     // pass 1: the token's largest |x| (rows are 16-byte aligned: K % 256 == 0)
     float m = 0.0f;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
@@ -522,10 +536,12 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, cons
     __nv_bfloat16 *Bx = reinterpret_cast<__nv_bfloat16 *>(w + 2 * act_b_bytes(T, K));
     float *inv = reinterpret_cast<float *>(w + 2 * act_b_bytes(T, K) + act_bx_bytes(T, K));
     const int Tp = tokens_padded(T);
-    prefill_act_kernel<<<T, kActThreads, 0, s>>>(X, T, K, Bh, Bl, Bx, inv);
+    int st;
+    if ((st = launch_pdl(ctx, (const void *)prefill_act_kernel, dim3(T), dim3(kActThreads), 0, s,
+                         {&X, &T, &K, &Bh, &Bl, &Bx, &inv})))
+        return st;
     LALB_LAUNCH_CHECK(ctx, "prefill_act_kernel");
     CUtensorMap mA, mBh, mBl, mAx, mBx, mRS;
-    int st;
     if ((st = map2d(ctx, &mA, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, rows, PK, PM,
                     CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
@@ -553,7 +569,9 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, cons
     a.Y = Y;
     a.status = &ctx->scratch->status;
     const dim3 grid(Tp / PN, (rows + PM - 1) / PM);
-    prefill_tc_kernel<<<grid, kPThreads, kPSmem, s>>>(mA, mBh, mBl, mAx, mBx, mRS, a);
+    if ((st = launch_pdl(ctx, (const void *)prefill_tc_kernel, grid, dim3(kPThreads), kPSmem, s,
+                         {&mA, &mBh, &mBl, &mAx, &mBx, &mRS, &a})))
+        return st;
     LALB_LAUNCH_CHECK(ctx, "prefill_tc_kernel");
     return LALB_OK;
 }

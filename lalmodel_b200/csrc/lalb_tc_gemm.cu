@@ -34,7 +34,6 @@
 #include <cuda.h>
 
 #include <algorithm>
-#include <initializer_list>
 #include <mutex>
 
 #include "lalb_internal.cuh"
@@ -320,27 +319,6 @@ int make_map(lalb_ctx *ctx, CUtensorMap *m, const float *base, int rows, int K, 
                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return lalb_fail(ctx, LALB_ERR_CUDA, "tc_gemm: tensor map encode (%d)", (int)r);
-    return LALB_OK;
-}
-
-// Launch with programmatic dependent launch allowed (the kernels call
-// pdl_wait before reading what the previous kernel wrote).
-int launch_pdl(lalb_ctx *ctx, const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-               std::initializer_list<void *> args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    void *params[8];
-    int i = 0;
-    for (void *p : args) params[i++] = p;
-    LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, fn, params));
     return LALB_OK;
 }
 
