@@ -114,6 +114,8 @@ struct TcArgs {
     int a_parts, b_parts;       // 1 or 2 each
     int tiles_n, tiles;         // output tiles along N, in all
     int nacc, ngroups;          // accumulators per tile, accumulator groups in TMEM
+    int splits;                 // split-K kernel: CTAs of a cluster sharing a tile
+    int y_vec4;                 // Y rows 16-byte aligned (N % 4 == 0, Y aligned)
     float *Y;                   // [M][N]
     const float *rowscale;      // [M] or null (1)
     const float *colscale;      // [N] or null (1)
@@ -287,6 +289,194 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Split-K over a thread-block cluster, for outputs with few tiles (the seed
+// model's o and down projections: 32 tiles of 128 x 128 on 148 SMs).  The
+// S = a.splits CTAs of a cluster share one output tile: CTA r (its rank in
+// the cluster) accumulates K-blocks [r nk / S, (r+1) nk / S) in TMEM, writes
+// its fp32 partial tile into its own shared memory (the operand ring, idle by
+// then), and after a cluster barrier sums rows [r BM / S, (r+1) BM / S) of
+// all S partials through distributed shared memory, in rank order, applying
+// the scales and bias.  A second cluster barrier keeps every partial alive
+// until all readers are done.  Same warp roles as tc_gemm_tf32_kernel.
+constexpr int kSplitAcc = 2;   // accumulators per split (K-blocks round-robin)
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_tf32_splitk_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
+                               const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1,
+                               const TcArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    uint8_t *stages = smem;
+    float *part = reinterpret_cast<float *>(smem);   // [BM][BN] partial, reuses stage 0
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStagesTc * kStageBytes + kEpiBytes);
+    uint64_t *empty = full + kStagesTc;
+    uint64_t *acc_full = empty + kStagesTc;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = a.splits;
+    uint32_t rank;
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const int t = blockIdx.x / S;
+    const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * BN;
+    const int nk = a.K / BK;
+    const int kb0 = (int)rank * nk / S, kb1 = ((int)rank + 1) * nk / S;
+
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA1)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB1)) : "memory");
+        for (int st = 0; st < kStagesTc; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], 1);
+        }
+        mbar_init(&acc_full[0], 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const uint32_t stage_tx = (uint32_t)(a.a_parts * kATile + a.b_parts * kBTile);
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = kb0; kb < kb1; ++kb) {
+                const uint32_t it = (uint32_t)(kb - kb0);
+                const int st = it % kStagesTc;
+                const uint32_t use = it / kStagesTc;
+                if (use > 0 && !mbar_wait_bounded(&empty[st], (use - 1) & 1u, a.status)) break;
+                uint8_t *sp = stages + (size_t)st * kStageBytes;
+                mbar_arrive_expect_tx(&full[st], stage_tx);
+                tma_load_2d(sp, &mA0, kb * BK, m0, &full[st]);
+                if (a.a_parts > 1) tma_load_2d(sp + kATile, &mA1, kb * BK, m0, &full[st]);
+                tma_load_2d(sp + 2 * kATile, &mB0, kb * BK, n0, &full[st]);
+                if (a.b_parts > 1) tma_load_2d(sp + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[st]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int kb = kb0; kb < kb1; ++kb) {
+                const uint32_t it = (uint32_t)(kb - kb0);
+                const int st = it % kStagesTc;
+                if (!mbar_wait_bounded(&full[st], (it / kStagesTc) & 1u, a.status)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t sp = smem_u32(stages + (size_t)st * kStageBytes);
+                const uint32_t a0 = sp, a1 = sp + kATile, b0 = sp + 2 * kATile, b1 = b0 + kBTile;
+                const uint32_t td = tmem + (uint32_t)((it % kSplitAcc) * BN);
+                uint32_t acc = it >= (uint32_t)kSplitAcc;   // the first block of an accumulator overwrites it
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {
+                    const uint32_t ko = k * 32;
+                    mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), acc);
+                    acc = 1;
+                    if (a.a_parts > 1) mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), 1);
+                    if (a.b_parts > 1) mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), 1);
+                }
+                mma_commit(&empty[st]);
+            }
+            mma_commit(&acc_full[0]);   // every MMA above (and the stage reads) completed
+        }
+        __syncwarp();
+    } else {
+        // ---- the partial tile into shared memory: row R = q*32 + lane, its
+        // 16-byte chunk c (of 32) at chunk c ^ (R & 31) ----
+        const int q = warp & 3, R = q * 32 + lane;
+        const int nacc = kb1 - kb0 < kSplitAcc ? kb1 - kb0 : kSplitAcc;
+        // warp-uniform, so that the tcgen05.ld below stay converged
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[0], 0, a.status));
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            float sum[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+            for (int ai = 0; ai < nacc && ok; ++ai) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ai * BN + c0), r);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+            }
+            float4 *row = reinterpret_cast<float4 *>(part + (size_t)R * BN);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                row[((c0 >> 2) + i) ^ (R & 31)] =
+                    make_float4(sum[4 * i], sum[4 * i + 1], sum[4 * i + 2], sum[4 * i + 3]);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+    cluster_sync_all();   // every CTA's partial is in its shared memory
+
+    if (warp >= 2) {
+        // ---- rows [rank BM/S, (rank+1) BM/S): sum the S partials, rank order ----
+        const int rows = BM / S, e = warp - 2;
+        const int c = lane;   // 16-byte chunk: columns 4c .. 4c+3
+        const int n = n0 + 4 * c;
+        float cs[4], bs[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const bool in = n + i < a.N;
+            cs[i] = in && a.colscale ? a.colscale[n + i] : 1.0f;
+            bs[i] = in && a.bias ? a.bias[n + i] : 0.0f;
+        }
+        for (int rr = e; rr < rows; rr += kEpiWarpsTc) {
+            const int R = (int)rank * rows + rr, m = m0 + R;
+            const uint32_t off = smem_u32(part) + (uint32_t)(R * BN * 4 + 16 * (c ^ (R & 31)));
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int j = 0; j < S; ++j) {
+                uint32_t raddr;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(off), "r"(j));
+                float4 p;
+                asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                             : "=f"(p.x), "=f"(p.y), "=f"(p.z), "=f"(p.w)
+                             : "r"(raddr)
+                             : "memory");
+                v[0] = __fadd_rn(v[0], p.x);
+                v[1] = __fadd_rn(v[1], p.y);
+                v[2] = __fadd_rn(v[2], p.z);
+                v[3] = __fadd_rn(v[3], p.w);
+            }
+            if (m < a.M) {
+                const float rs = a.rowscale ? a.rowscale[m] : 1.0f;
+                float o[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = __fadd_rn(__fmul_rn(__fmul_rn(v[i], rs), cs[i]), bs[i]);
+                float *yp = a.Y + (size_t)m * a.N + n;
+                if (a.y_vec4 && n + 3 < a.N) {
+                    *reinterpret_cast<float4 *>(yp) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (n + i < a.N) yp[i] = o[i];
+                }
+            }
+        }
+    }
+    cluster_sync_all();   // no CTA leaves while the others still read its partial
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 // ---- tensor maps ----------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
@@ -351,6 +541,66 @@ int lalb_split_tf32(lalb_ctx *ctx, const float *x, float *hi, float *lo, size_t 
     return LALB_OK;
 }
 
+namespace {
+
+// Launch with a cluster of `cluster` CTAs along x and programmatic dependent
+// launch allowed.
+int launch_cluster_pdl(lalb_ctx *ctx, const void *fn, dim3 grid, dim3 block, size_t smem, int cluster,
+                       cudaStream_t s, std::initializer_list<void *> args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    void *params[8];
+    int i = 0;
+    for (void *p : args) params[i++] = p;
+    LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, fn, params));
+    return LALB_OK;
+}
+
+// Clusters of S split-K CTAs that can be resident at once on this device
+// (0 when the query fails), cached per device and S.
+int splitk_clusters_fit(lalb_ctx *ctx, int S) {
+    static std::mutex mu;
+    static int cache[64][5];
+    static bool have[64][5];
+    std::lock_guard<std::mutex> lock(mu);
+    const int dev = ctx->device & 63;
+    if (!have[dev][S]) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(S * 64));
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = kTcSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)S;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (const void *)tc_gemm_tf32_splitk_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        cache[dev][S] = n;
+        have[dev][S] = true;
+    }
+    return cache[dev][S];
+}
+
+}  // namespace
+
 int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.K % BK || !p.a_hi || !p.b_hi || !p.Y)
         return lalb_fail(ctx, LALB_ERR_INVALID, "tc_gemm: M, N > 0, K a multiple of %d", BK);
@@ -379,6 +629,18 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     a.colscale = p.colscale;
     a.bias = p.bias;
     a.status = &ctx->scratch->status;
+    a.splits = 1;
+    a.y_vec4 = (p.N % 4 == 0) && ((uintptr_t)p.Y & 15u) == 0;
+    // few output tiles: split K over clusters of S CTAs so that most SMs work
+    for (int S = 4; S >= 2; S /= 2) {
+        if (a.tiles * S > ctx->sm_count || p.K / BK < 2 * S) continue;
+        if ((st = lalb_set_smem_attr(ctx, (const void *)tc_gemm_tf32_splitk_kernel, (int)kTcSmem))) return st;
+        if (splitk_clusters_fit(ctx, S) < a.tiles) continue;   // one wave of clusters or nothing
+        a.splits = S;
+        return launch_cluster_pdl(ctx, (const void *)tc_gemm_tf32_splitk_kernel, dim3(a.tiles * S),
+                                  dim3(kTcThreads), kTcSmem, S, s,
+                                  {(void *)&mA0, (void *)&mA1, (void *)&mB0, (void *)&mB1, (void *)&a});
+    }
     const int grid = std::min(a.tiles, ctx->sm_count);
     return launch_pdl(ctx, (const void *)tc_gemm_tf32_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, s,
                       {(void *)&mA0, (void *)&mA1, (void *)&mB0, (void *)&mB1, (void *)&a});

@@ -79,6 +79,27 @@ def test_logic_codes_pack_and_forward_match_oracle(ctx, rows, K, M):
     L.close()
 
 
+# outputs with few 128 x 128 tiles take the split-K kernel (clusters of 4 or 2
+# CTAs summing their partial tiles through distributed shared memory): 4-way
+# (448 rows), 2-way (640 rows: 40 tiles), a ragged last tile with rows not a
+# multiple of 4 (scalar stores), and token counts that end inside a tile
+@pytest.mark.parametrize("rows,K,M", [(448, 448, 1024), (640, 448, 1024), (450, 448, 256),
+                                      (448, 1792, 100), (90, 256, 33)])
+def test_logic_layer_split_k_shapes_match_oracle(ctx, rows, K, M):
+    W = O.normal(rows * K, seed=rows * 3 + K, sigma=0.02).reshape(rows, K)
+    st = O.logic_state(rows * 17 + K, rows * K, 0.10, 0.50).reshape(rows, K)
+    codes, srow = O.logic_pack(W, st)
+    bias = O.normal(rows, seed=7, sigma=0.01)
+    X = O.normal(M * K, seed=M + 11).reshape(M, K)
+    ref = O.logic_forward(codes, srow, bias, X)
+    L = lb.LogicLayer(ctx, dev(codes), dev(srow), dev(bias), max_rows=M)
+    Y = host(L.forward(dev(X)))
+    assert O.normwise_rel_err(Y, ref) < TOL
+    Y2 = host(L.forward(dev(X)))
+    assert np.array_equal(Y, Y2)   # fixed summation order: repeatable
+    L.close()
+
+
 def test_logic_layer_rejects_too_many_rows(ctx):
     codes = torch.zeros((64, 64), dtype=torch.int8, device="cuda")
     srow = torch.ones(64, dtype=torch.float32, device="cuda")
