@@ -232,8 +232,6 @@ extern "C" int lalb_binlayer_forward(lalb_binlayer *b, const float *X, int M, fl
         return lalb_fail(ctx, LALB_ERR_INVALID, "binlayer_forward: bad arguments (M <= %d, mode 0/1)",
                          b->max_rows);
     cudaStream_t s = (cudaStream_t)stream;
-    int st;
-    if ((st = lalb_split_tf32(ctx, X, b->x_hi, b->x_lo, (size_t)M * b->in, s))) return st;
     if (mode == 0) {
         knorm_kernel<<<M, 128, 0, s>>>(X, b->in, b->knorm);
         LALB_LAUNCH_CHECK(ctx, "knorm_kernel");
@@ -242,8 +240,8 @@ extern "C" int lalb_binlayer_forward(lalb_binlayer *b, const float *X, int M, fl
     p.M = M;
     p.N = b->out;
     p.K = b->in;
-    p.a_hi = b->x_hi;
-    p.a_lo = b->x_lo;
+    p.a_hi = X;   // the GEMM splits X into tf32 parts in shared memory
+    p.split_a = 1;
     p.b_hi = mode == 0 ? b->b0_hi : b->b1_hi;
     p.b_lo = mode == 0 ? b->b0_lo : b->b1_lo;
     p.Y = Y;
@@ -323,14 +321,12 @@ extern "C" int lalb_logic_layer_forward(lalb_logic_layer *L, const float *X, int
         return lalb_fail(ctx, LALB_ERR_INVALID, "logic_layer_forward: bad arguments (M <= %d)",
                          L->max_rows);
     cudaStream_t s = (cudaStream_t)stream;
-    int st;
-    if ((st = lalb_split_tf32(ctx, X, L->x_hi, L->x_lo, (size_t)M * L->K, s))) return st;
     TcGemmParts p = {};
     p.M = M;
     p.N = L->rows;
     p.K = L->K;
-    p.a_hi = L->x_hi;
-    p.a_lo = L->x_lo;
+    p.a_hi = X;   // the GEMM splits X into tf32 parts in shared memory
+    p.split_a = 1;
     p.b_hi = L->b;
     p.b_lo = nullptr;
     p.Y = Y;

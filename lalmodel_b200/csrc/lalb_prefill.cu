@@ -561,7 +561,7 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, cons
                     CU_TENSOR_MAP_SWIZZLE_NONE)))
         return st;
     if ((st = lalb_set_smem_attr(ctx, (const void *)prefill_tc_kernel, (int)kPSmem))) return st;
-    PfArgs a;
+    PfArgs a = {};
     a.rows = rows;
     a.K = K;
     a.T = T;

@@ -44,17 +44,20 @@ using namespace lalb;
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 32;     // BK fp32 = 128 B: one 128-byte swizzle row
-constexpr int kStagesTc = 3;
+constexpr int kMaxStages = 4;                   // ring slots: 4 x 48 KB (one B part) or 3 x 64 KB
 constexpr int kTmemCols = 512;                  // the whole TMEM of the SM: 4 accumulators of BN
 constexpr int kLongK = 16;                      // K-blocks above which one group of 4 accumulators is used
 constexpr int kEpiWarpsTc = 4;
-constexpr int kTcThreads = 32 * (2 + kEpiWarpsTc);
+constexpr int kConvWarps = 4;                   // A given as raw fp32: its lo part formed in shared memory
+constexpr int kConvWarp0 = 2 + kEpiWarpsTc;
+constexpr int kTcThreads = 32 * (2 + kEpiWarpsTc + kConvWarps);
 constexpr uint32_t kATile = BM * BK * 4;       // 16 KB
 constexpr uint32_t kBTile = BN * BK * 4;       // 16 KB
 // stage: A hi | A lo | B hi | B lo
 constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
+constexpr uint32_t kRingBytes = 3 * kStageBytes;
 constexpr uint32_t kEpiBytes = 4 * 32 * 33 * 4;             // per-warp 32x32 transpose
-constexpr uint32_t kTcSmem = 1024 /* alignment slack */ + kStagesTc * kStageBytes + kEpiBytes + 256;
+constexpr uint32_t kTcSmem = 1024 /* alignment slack */ + kRingBytes + kEpiBytes + 256;
 
 // K-major operand tile with 128-byte swizzle (the TMA layout): rows of
 // 128 bytes, 8-row groups 1024 bytes apart.  Descriptor fields: start
@@ -109,9 +112,39 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
+// The low part of x below its tf32 truncation: x - (x with the low 13
+// mantissa bits cleared), exact in fp32.  The tensor core reads the raw fp32
+// x as its truncation (the low 13 bits are not used), so hi + lo = x up to
+// the tf32 rounding of lo (2^-21 |x| at most).
+__device__ __forceinline__ float tf32_trunc_lo(float x) {
+    return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+}
+
+// One stage's A tile (raw fp32, 128 x 32) -> its lo part in the next 16 KB,
+// same swizzled layout (element for element); 128 converter threads.  Then
+// the writes are made visible to the tensor core (async proxy) and the warp
+// arrives on conv.
+__device__ __forceinline__ void convert_a_stage(uint8_t *stage, int ct, int lane, uint64_t *conv) {
+    const float4 *src = reinterpret_cast<const float4 *>(stage);
+    float4 *dst = reinterpret_cast<float4 *>(stage + BM * BK * 4);
+#pragma unroll
+    for (int i = 0; i < (BM * BK / 4) / (32 * kConvWarps); ++i) {
+        const float4 x = src[ct + 32 * kConvWarps * i];
+        dst[ct + 32 * kConvWarps * i] =
+            make_float4(tf32_trunc_lo(x.x), tf32_trunc_lo(x.y), tf32_trunc_lo(x.z), tf32_trunc_lo(x.w));
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(conv);
+}
+
 struct TcArgs {
     int M, N, K;
-    int a_parts, b_parts;       // 1 or 2 each
+    int a_parts, b_parts;       // parts multiplied: 1 or 2 each
+    int a_loads;                // A parts loaded by TMA (1 when the kernel forms lo itself)
+    int conv_a;                 // A is raw fp32: hi = its tf32 truncation, lo = A - hi
+    int nstages;                // ring slots in use
+    uint32_t stage_bytes;       // A hi | A lo | B hi (| B lo)
     int tiles_n, tiles;         // output tiles along N, in all
     int nacc, ngroups;          // accumulators per tile, accumulator groups in TMEM
     int splits;                 // split-K kernel: CTAs of a cluster sharing a tile
@@ -131,12 +164,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // 1024-byte alignment for the swizzled tiles
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint8_t *stages = smem;
-    float *epi = reinterpret_cast<float *>(smem + kStagesTc * kStageBytes);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStagesTc * kStageBytes + kEpiBytes);
-    uint64_t *empty = full + kStagesTc;         // the stage's MMAs completed
-    uint64_t *acc_full = empty + kStagesTc;     // [2] a tile's accumulators are complete
+    float *epi = reinterpret_cast<float *>(smem + kRingBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kRingBytes + kEpiBytes);
+    uint64_t *empty = full + kMaxStages;         // the stage's MMAs completed
+    uint64_t *acc_full = empty + kMaxStages;     // [2] a tile's accumulators are complete
     uint64_t *acc_empty = acc_full + 2;         // [2] the epilogue has read them
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint64_t *conv = acc_empty + 2;             // [stages] the stage's A lo part is formed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(conv + kMaxStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = a.K / BK;
@@ -147,7 +181,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA1)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB0)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB1)) : "memory");
-        for (int s = 0; s < kStagesTc; ++s) {
+        for (int s = 0; s < kMaxStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -155,6 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&acc_full[g], 1);
             mbar_init(&acc_empty[g], kEpiWarpsTc);
         }
+        for (int st = 0; st < kMaxStages; ++st) mbar_init(&conv[st], kConvWarps);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -173,7 +208,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();
     pdl_launch_dependents();
 
-    const uint32_t stage_tx = (uint32_t)(a.a_parts * kATile + a.b_parts * kBTile);
+    const uint32_t stage_tx = (uint32_t)(a.a_loads * kATile + a.b_parts * kBTile);
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer ----
@@ -182,18 +217,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
                 const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * BN;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % kStagesTc;
-                    const uint32_t use = it / kStagesTc;
+                    const int s = it % a.nstages;
+                    const uint32_t use = it / a.nstages;
                     if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u, a.status)) {
                         ok = false;
                         break;
                     }
-                    uint8_t *st = stages + (size_t)s * kStageBytes;
+                    uint8_t *st = stages + (size_t)s * a.stage_bytes;
                     mbar_arrive_expect_tx(&full[s], stage_tx);
                     tma_load_2d(st, &mA0, kb * BK, m0, &full[s]);
-                    if (a.a_parts > 1) tma_load_2d(st + kATile, &mA1, kb * BK, m0, &full[s]);
+                    if (a.a_loads > 1) tma_load_2d(st + kATile, &mA1, kb * BK, m0, &full[s]);
                     tma_load_2d(st + 2 * kATile, &mB0, kb * BK, n0, &full[s]);
                     if (a.b_parts > 1) tma_load_2d(st + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[s]);
+                }
+            }
+        }
+    } else if (warp >= kConvWarp0) {
+        // ---- A lo parts (raw fp32 A only) ----
+        if (a.conv_a) {
+            const int ct = threadIdx.x - 32 * kConvWarp0;
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % a.nstages;
+                    ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (it / a.nstages) & 1u, a.status));
+                    if (!ok) break;
+                    convert_a_stage(stages + (size_t)s * a.stage_bytes, ct, lane, &conv[s]);
                 }
             }
         }
@@ -208,13 +258,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (gu > 0 && !mbar_wait_bounded(&acc_empty[g], (gu - 1) & 1u, a.status)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % kStagesTc;
-                    if (!mbar_wait_bounded(&full[s], (it / kStagesTc) & 1u, a.status)) {
+                    const int s = it % a.nstages;
+                    // raw fp32 A: the converters' arrival implies the stage's TMA data too
+                    if (!mbar_wait_bounded(a.conv_a ? &conv[s] : &full[s], (it / a.nstages) & 1u, a.status)) {
                         ok = false;
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t st = smem_u32(stages + (size_t)s * kStageBytes);
+                    const uint32_t st = smem_u32(stages + (size_t)s * a.stage_bytes);
                     const uint32_t a0 = st, a1 = st + kATile, b0 = st + 2 * kATile, b1 = b0 + kBTile;
                     const uint32_t td = tmem + (uint32_t)((g * a.nacc + kb % a.nacc) * BN);
                     uint32_t acc = kb >= a.nacc;   // the first block of an accumulator overwrites it
@@ -313,10 +364,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint8_t *stages = smem;
     float *part = reinterpret_cast<float *>(smem);   // [BM][BN] partial, reuses stage 0
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStagesTc * kStageBytes + kEpiBytes);
-    uint64_t *empty = full + kStagesTc;
-    uint64_t *acc_full = empty + kStagesTc;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 2);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kRingBytes + kEpiBytes);
+    uint64_t *empty = full + kMaxStages;
+    uint64_t *acc_full = empty + kMaxStages;
+    uint64_t *conv = acc_full + 2;              // [stages] the stage's A lo part is formed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(conv + kMaxStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.splits;
@@ -332,11 +384,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA1)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB0)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mB1)) : "memory");
-        for (int st = 0; st < kStagesTc; ++st) {
+        for (int st = 0; st < kMaxStages; ++st) {
             mbar_init(&full[st], 1);
             mbar_init(&empty[st], 1);
         }
         mbar_init(&acc_full[0], 1);
+        for (int st = 0; st < kMaxStages; ++st) mbar_init(&conv[st], kConvWarps);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -353,31 +406,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();
     pdl_launch_dependents();
 
-    const uint32_t stage_tx = (uint32_t)(a.a_parts * kATile + a.b_parts * kBTile);
+    const uint32_t stage_tx = (uint32_t)(a.a_loads * kATile + a.b_parts * kBTile);
     if (warp == 0) {
         if (lane == 0) {
             for (int kb = kb0; kb < kb1; ++kb) {
                 const uint32_t it = (uint32_t)(kb - kb0);
-                const int st = it % kStagesTc;
-                const uint32_t use = it / kStagesTc;
+                const int st = it % a.nstages;
+                const uint32_t use = it / a.nstages;
                 if (use > 0 && !mbar_wait_bounded(&empty[st], (use - 1) & 1u, a.status)) break;
-                uint8_t *sp = stages + (size_t)st * kStageBytes;
+                uint8_t *sp = stages + (size_t)st * a.stage_bytes;
                 mbar_arrive_expect_tx(&full[st], stage_tx);
                 tma_load_2d(sp, &mA0, kb * BK, m0, &full[st]);
-                if (a.a_parts > 1) tma_load_2d(sp + kATile, &mA1, kb * BK, m0, &full[st]);
+                if (a.a_loads > 1) tma_load_2d(sp + kATile, &mA1, kb * BK, m0, &full[st]);
                 tma_load_2d(sp + 2 * kATile, &mB0, kb * BK, n0, &full[st]);
                 if (a.b_parts > 1) tma_load_2d(sp + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[st]);
             }
         }
         __syncwarp();
+    } else if (warp >= kConvWarp0) {
+        if (a.conv_a) {
+            const int ct = threadIdx.x - 32 * kConvWarp0;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                const uint32_t it = (uint32_t)(kb - kb0);
+                const int st = it % a.nstages;
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[st], (it / a.nstages) & 1u, a.status)))
+                    break;
+                convert_a_stage(stages + (size_t)st * a.stage_bytes, ct, lane, &conv[st]);
+            }
+        }
     } else if (warp == 1) {
         if (lane == 0) {
             for (int kb = kb0; kb < kb1; ++kb) {
                 const uint32_t it = (uint32_t)(kb - kb0);
-                const int st = it % kStagesTc;
-                if (!mbar_wait_bounded(&full[st], (it / kStagesTc) & 1u, a.status)) break;
+                const int st = it % a.nstages;
+                if (!mbar_wait_bounded(a.conv_a ? &conv[st] : &full[st], (it / a.nstages) & 1u, a.status))
+                    break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t sp = smem_u32(stages + (size_t)st * kStageBytes);
+                const uint32_t sp = smem_u32(stages + (size_t)st * a.stage_bytes);
                 const uint32_t a0 = sp, a1 = sp + kATile, b0 = sp + 2 * kATile, b1 = b0 + kBTile;
                 const uint32_t td = tmem + (uint32_t)((it % kSplitAcc) * BN);
                 uint32_t acc = it >= (uint32_t)kSplitAcc;   // the first block of an accumulator overwrites it
@@ -422,7 +487,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     cluster_sync_all();   // every CTA's partial is in its shared memory
 
-    if (warp >= 2) {
+    if (warp >= 2 && warp < kConvWarp0) {
         // ---- rows [rank BM/S, (rank+1) BM/S): sum the S partials, rank order ----
         const int rows = BM / S, e = warp - 2;
         const int c = lane;   // 16-byte chunk: columns 4c .. 4c+3
@@ -613,12 +678,19 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     if ((st = make_map(ctx, &mB0, p.b_hi, p.N, p.K, BN))) return st;
     if ((st = make_map(ctx, &mB1, p.b_lo ? p.b_lo : p.b_hi, p.N, p.K, BN))) return st;
     if ((st = lalb_set_smem_attr(ctx, (const void *)tc_gemm_tf32_kernel, (int)kTcSmem))) return st;
-    TcArgs a;
+    TcArgs a = {};
     a.M = p.M;
     a.N = p.N;
     a.K = p.K;
-    a.a_parts = p.a_lo ? 2 : 1;
+    a.conv_a = p.split_a && !p.a_lo;
+    a.a_parts = (p.a_lo || a.conv_a) ? 2 : 1;
+    a.a_loads = p.a_lo ? 2 : 1;
     a.b_parts = p.b_lo ? 2 : 1;
+    // ring slot: A hi | A lo | B hi (| B lo), each 16 KB and 1024-byte aligned
+    a.stage_bytes = 2 * kATile + (uint32_t)a.b_parts * kBTile;
+    a.nstages = (int)std::min<uint32_t>(kMaxStages, kRingBytes / a.stage_bytes);
+    if (a.nstages < 2 || (size_t)a.nstages * a.stage_bytes > kRingBytes)
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "tc_gemm: ring layout");
     a.tiles_n = (p.N + BN - 1) / BN;
     a.tiles = a.tiles_n * ((p.M + BM - 1) / BM);
     const bool long_k = p.K / BK > kLongK;

@@ -8,7 +8,7 @@
 
 // Y[m][n] = rowscale[m] * colscale[n] * sum_k A[m][k] B[n][k] + bias[n];
 // A = a_hi (+ a_lo), B = b_hi (+ b_lo), every part exactly representable in
-// tf32 (lalb_split_tf32).  Row-major, K a multiple of 32, 16-byte aligned.
+// tf32 (lalb_split_tf32), or A raw fp32 with split_a set.  Row-major, K a multiple of 32, 16-byte aligned.
 struct TcGemmParts {
     int M, N, K;
     const float *a_hi, *a_lo;   // [M][K]; a_lo nullable
@@ -17,6 +17,8 @@ struct TcGemmParts {
     const float *rowscale;      // [M], nullable
     const float *colscale;      // [N], nullable
     const float *bias;          // [N], nullable
+    int split_a;                // a_lo null: a_hi is raw fp32 and the kernel forms
+                                // hi (its tf32 truncation) and lo = A - hi itself
 };
 
 int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s);
