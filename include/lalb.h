@@ -301,7 +301,8 @@ LALB_API int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *packed, int row
  * (runtime/lal_runtime.c:1567-1676) from W [out][in] fp32 (row-major),
  * bias [out] (nullable) and mask [out], all device buffers; alpha_repack = 1
  * recomputes alpha as bin_layer_repack (:1703-1766) does.  max_rows bounds
- * the M of a forward (the layer owns its workspace).  in_dim % 32 == 0. */
+ * the M of a forward (the layer owns its per-row scale buffer).
+ * in_dim % 32 == 0. */
 typedef struct lalb_binlayer lalb_binlayer;
 LALB_API int lalb_binlayer_create(lalb_ctx *ctx, const float *W, const float *bias,
                                   const uint8_t *mask, int in_dim, int out_dim,
@@ -309,8 +310,9 @@ LALB_API int lalb_binlayer_create(lalb_ctx *ctx, const float *W, const float *bi
                                   lalb_binlayer **out);
 /* Y [M][out] = the layer over the M rows of X [M][in]: mode 0 bin_forward
  * (:1852-1938, logic-mask path), mode 1 bin_forward_pure_float (:543-582).
- * fp32 operands as sums of tf32 parts on tcgen05; within 1e-5 of the exact
- * products. */
+ * fp32 operands as sums of tf32 parts on tcgen05 (X is read once, its parts
+ * formed on chip); within 1e-5 of the exact products.  X 16-byte
+ * aligned (LALB_ERR_INVALID otherwise). */
 LALB_API int lalb_binlayer_forward(lalb_binlayer *bl, const float *X, int M, float *Y,
                                    int mode, lalb_stream stream);
 LALB_API int lalb_binlayer_alpha(lalb_binlayer *bl, float *alpha, lalb_stream stream);
@@ -322,7 +324,7 @@ LALB_API int lalb_binlayer_destroy(lalb_binlayer *bl);
 LALB_API int lalb_logic_pack(lalb_ctx *ctx, const float *W, const uint8_t *state, int rows,
                              int K, int8_t *codes, float *srow, lalb_stream stream);
 /* Y [M][rows] = srow * (X . codes^T) + bias; bias nullable; the layer keeps
- * pointers to srow and bias. */
+ * pointers to srow and bias.  X 16-byte aligned, K % 32 == 0. */
 typedef struct lalb_logic_layer lalb_logic_layer;
 LALB_API int lalb_logic_layer_create(lalb_ctx *ctx, const int8_t *codes, const float *srow,
                                      const float *bias, int rows, int K, int max_rows,

@@ -36,7 +36,6 @@ struct lalb_binlayer {
     float *cs0, *bias0;     // [out]
     float *cs1, *bias1;
     float *alpha;           // [out]
-    float *x_hi, *x_lo;     // [max_rows][in] workspace
     float *knorm;           // [max_rows]
 };
 
@@ -45,7 +44,6 @@ struct lalb_logic_layer {
     int rows, K, max_rows;
     float *b;               // codes as fp32 [rows][K] (exact in tf32)
     const float *srow, *bias;
-    float *x_hi, *x_lo;
 };
 
 namespace {
@@ -169,15 +167,13 @@ __global__ void codes_to_f32_kernel(const int8_t *__restrict__ c, float *__restr
 
 void free_binlayer(lalb_binlayer *b) {
     for (float *p : {b->b0_hi, b->b0_lo, b->b1_hi, b->b1_lo, b->cs0, b->bias0, b->cs1, b->bias1,
-                     b->alpha, b->x_hi, b->x_lo, b->knorm})
+                     b->alpha, b->knorm})
         cudaFree(p);
     delete b;
 }
 
 void free_logic(lalb_logic_layer *L) {
     cudaFree(L->b);
-    cudaFree(L->x_hi);
-    cudaFree(L->x_lo);
     delete L;
 }
 
@@ -199,15 +195,14 @@ extern "C" int lalb_binlayer_create(lalb_ctx *ctx, const float *W, const float *
     b->in = in_dim;
     b->out = out_dim;
     b->max_rows = max_rows;
-    const size_t wn = (size_t)in_dim * out_dim, xn = (size_t)max_rows * in_dim;
+    const size_t wn = (size_t)in_dim * out_dim;
     bool ok = cudaMalloc(&b->b0_hi, 4 * wn) == cudaSuccess && cudaMalloc(&b->b0_lo, 4 * wn) == cudaSuccess &&
               cudaMalloc(&b->b1_hi, 4 * wn) == cudaSuccess && cudaMalloc(&b->b1_lo, 4 * wn) == cudaSuccess &&
               cudaMalloc(&b->cs0, 4 * out_dim) == cudaSuccess &&
               cudaMalloc(&b->bias0, 4 * out_dim) == cudaSuccess &&
               cudaMalloc(&b->cs1, 4 * out_dim) == cudaSuccess &&
               cudaMalloc(&b->bias1, 4 * out_dim) == cudaSuccess &&
-              cudaMalloc(&b->alpha, 4 * out_dim) == cudaSuccess && cudaMalloc(&b->x_hi, 4 * xn) == cudaSuccess &&
-              cudaMalloc(&b->x_lo, 4 * xn) == cudaSuccess && cudaMalloc(&b->knorm, 4 * max_rows) == cudaSuccess;
+              cudaMalloc(&b->alpha, 4 * out_dim) == cudaSuccess && cudaMalloc(&b->knorm, 4 * max_rows) == cudaSuccess;
     if (!ok) {
         cudaGetLastError();
         free_binlayer(b);
@@ -294,9 +289,8 @@ extern "C" int lalb_logic_layer_create(lalb_ctx *ctx, const int8_t *codes, const
     L->max_rows = max_rows;
     L->srow = srow;
     L->bias = bias;
-    const size_t wn = (size_t)rows * K, xn = (size_t)max_rows * K;
-    if (cudaMalloc(&L->b, 4 * wn) != cudaSuccess || cudaMalloc(&L->x_hi, 4 * xn) != cudaSuccess ||
-        cudaMalloc(&L->x_lo, 4 * xn) != cudaSuccess) {
+    const size_t wn = (size_t)rows * K;
+    if (cudaMalloc(&L->b, 4 * wn) != cudaSuccess) {
         cudaGetLastError();
         free_logic(L);
         return lalb_fail(ctx, LALB_ERR_NOMEM, "logic_layer_create: device buffers");

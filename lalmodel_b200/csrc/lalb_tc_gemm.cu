@@ -579,33 +579,6 @@ int make_map(lalb_ctx *ctx, CUtensorMap *m, const float *base, int rows, int K, 
 
 }  // namespace
 
-// fp32 -> (hi, lo) tf32 parts: hi = tf32(x) (round to nearest, ties away),
-// lo = tf32(x - hi).
-__global__ void split_tf32_kernel(const float *__restrict__ x, float *__restrict__ hi,
-                                  float *__restrict__ lo, size_t n) {
-    pdl_wait();   // x may be the previous kernel's output
-    pdl_launch_dependents();
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-         i += (size_t)gridDim.x * blockDim.x) {
-        const float v = x[i];
-        uint32_t h, l;
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
-        const float r = __fsub_rn(v, __uint_as_float(h));
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
-        hi[i] = __uint_as_float(h);
-        if (lo) lo[i] = __uint_as_float(l);
-    }
-}
-
-int lalb_split_tf32(lalb_ctx *ctx, const float *x, float *hi, float *lo, size_t n, cudaStream_t s) {
-    if (n == 0) return LALB_OK;
-    const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
-    if (int st = launch_pdl(ctx, (const void *)split_tf32_kernel, dim3(blocks), dim3(256), 0, s,
-                            {(void *)&x, (void *)&hi, (void *)&lo, (void *)&n}))
-        return st;
-    return LALB_OK;
-}
-
 namespace {
 
 // Launch with a cluster of `cluster` CTAs along x and programmatic dependent

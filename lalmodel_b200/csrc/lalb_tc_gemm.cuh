@@ -8,7 +8,7 @@
 
 // Y[m][n] = rowscale[m] * colscale[n] * sum_k A[m][k] B[n][k] + bias[n];
 // A = a_hi (+ a_lo), B = b_hi (+ b_lo), every part exactly representable in
-// tf32 (lalb_split_tf32), or A raw fp32 with split_a set.  Row-major, K a multiple of 32, 16-byte aligned.
+// tf32, or A raw fp32 with split_a set.  Row-major, K a multiple of 32, 16-byte aligned.
 struct TcGemmParts {
     int M, N, K;
     const float *a_hi, *a_lo;   // [M][K]; a_lo nullable
@@ -22,5 +22,3 @@ struct TcGemmParts {
 };
 
 int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s);
-// hi = tf32(x), lo = tf32(x - hi) (lo nullable).
-int lalb_split_tf32(lalb_ctx *ctx, const float *x, float *hi, float *lo, size_t n, cudaStream_t s);
