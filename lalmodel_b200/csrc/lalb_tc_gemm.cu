@@ -44,8 +44,9 @@ using namespace lalb;
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 32;     // BK fp32 = 128 B: one 128-byte swizzle row
+constexpr int kBNWide = 256;                    // wide tiles: A read once for 256 output columns
 constexpr int kMaxStages = 4;                   // ring slots: 4 x 48 KB (one B part) or 3 x 64 KB
-constexpr int kTmemCols = 512;                  // the whole TMEM of the SM: 4 accumulators of BN
+constexpr int kTmemCols = 512;                  // the whole TMEM of the SM: 4 accumulators of 128 columns
 constexpr int kLongK = 16;                      // K-blocks above which one group of 4 accumulators is used
 constexpr int kEpiWarpsTc = 4;
 constexpr int kConvWarps = 4;                   // A given as raw fp32: its lo part formed in shared memory
@@ -69,9 +70,10 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
 }
 
 // kind::tf32 instruction descriptor: fp32 accumulator, tf32 A and B, both
-// K-major, M = 128, N = BN.
-constexpr uint32_t kIdescTf32 = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                                ((uint32_t)(BM >> 4) << 24);
+// K-major, M = 128, N = bn (128 or 256).
+__host__ __device__ constexpr uint32_t idesc_tf32(int bn) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
@@ -82,12 +84,12 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdescTf32), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -145,6 +147,9 @@ struct TcArgs {
     int conv_a;                 // A is raw fp32: hi = its tf32 truncation, lo = A - hi
     int nstages;                // ring slots in use
     uint32_t stage_bytes;       // A hi | A lo | B hi (| B lo)
+    int bn;                     // output tile width: 128 or 256
+    uint32_t b_tile;            // bytes of one B part's tile: bn x BK fp32
+    uint32_t idesc;             // MMA instruction descriptor for bn
     int tiles_n, tiles;         // output tiles along N, in all
     int nacc, ngroups;          // accumulators per tile, accumulator groups in TMEM
     int splits;                 // split-K kernel: CTAs of a cluster sharing a tile
@@ -208,14 +213,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();
     pdl_launch_dependents();
 
-    const uint32_t stage_tx = (uint32_t)(a.a_loads * kATile + a.b_parts * kBTile);
+    const uint32_t stage_tx = (uint32_t)(a.a_loads * kATile + a.b_parts * a.b_tile);
     if (warp == 0) {
         if (lane == 0) {
             // ---- TMA producer ----
             uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
-                const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * BN;
+                const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * a.bn;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % a.nstages;
                     const uint32_t use = it / a.nstages;
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tma_load_2d(st, &mA0, kb * BK, m0, &full[s]);
                     if (a.a_loads > 1) tma_load_2d(st + kATile, &mA1, kb * BK, m0, &full[s]);
                     tma_load_2d(st + 2 * kATile, &mB0, kb * BK, n0, &full[s]);
-                    if (a.b_parts > 1) tma_load_2d(st + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[s]);
+                    if (a.b_parts > 1) tma_load_2d(st + 2 * kATile + a.b_tile, &mB1, kb * BK, n0, &full[s]);
                 }
             }
         }
@@ -266,18 +271,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t st = smem_u32(stages + (size_t)s * a.stage_bytes);
-                    const uint32_t a0 = st, a1 = st + kATile, b0 = st + 2 * kATile, b1 = b0 + kBTile;
-                    const uint32_t td = tmem + (uint32_t)((g * a.nacc + kb % a.nacc) * BN);
+                    const uint32_t a0 = st, a1 = st + kATile, b0 = st + 2 * kATile, b1 = b0 + a.b_tile;
+                    const uint32_t td = tmem + (uint32_t)((g * a.nacc + kb % a.nacc) * a.bn);
                     uint32_t acc = kb >= a.nacc;   // the first block of an accumulator overwrites it
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {   // 8 tf32 = 32 bytes per instruction
                         const uint32_t ko = k * 32;
-                        mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), acc);
+                        mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), a.idesc, acc);
                         acc = 1;
                         if (a.a_parts > 1)
-                            mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), 1);
+                            mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), a.idesc, 1);
                         if (a.b_parts > 1)
-                            mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), 1);
+                            mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), a.idesc, 1);
                     }
                     mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
                 }
@@ -291,21 +296,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int nacc = nk < a.nacc ? nk : a.nacc;
         uint32_t ti = 0;
         for (int t = blockIdx.x; t < a.tiles; t += gridDim.x, ++ti) {
-            const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * BN;
+            const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * a.bn;
             const int g = ti % a.ngroups;
             if (!mbar_wait_bounded(&acc_full[g], (ti / a.ngroups) & 1u, a.status)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = 0; c0 < a.bn; c0 += 32) {
                 float sum[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
                 for (int ai = 0; ai < nacc; ++ai) {
                     uint32_t r[32];
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((g * a.nacc + ai) * BN + c0), r);
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((g * a.nacc + ai) * a.bn + c0), r);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
                 }
-                if (c0 == BN - 32) {   // the group's last columns are in registers: free it
+                if (c0 == a.bn - 32) {   // the group's last columns are in registers: free it
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[g]);
@@ -318,12 +323,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const bool ncol = n < a.N;
                 const float cs = ncol && a.colscale ? a.colscale[n] : 1.0f;
                 const float b = ncol && a.bias ? a.bias[n] : 0.0f;
+                // lane's row scale, broadcast per row below; rows unrolled so
+                // that the loads and stores of several rows are in flight
+                const int mrow = m0 + q * 32 + lane;
+                const float rs_lane = a.rowscale && mrow < a.M ? a.rowscale[mrow] : 1.0f;
+                float *yc = a.Y + (size_t)(m0 + q * 32) * a.N + n;
+#pragma unroll 8
                 for (int j = 0; j < 32; ++j) {
-                    const int m = m0 + q * 32 + j;
-                    if (m < a.M && ncol) {
-                        const float rs = a.rowscale ? a.rowscale[m] : 1.0f;
-                        a.Y[(size_t)m * a.N + n] = __fadd_rn(__fmul_rn(__fmul_rn(st[j * 33 + lane], rs), cs), b);
-                    }
+                    const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+                    if (m0 + q * 32 + j < a.M && ncol)
+                        yc[(size_t)j * a.N] = __fadd_rn(__fmul_rn(__fmul_rn(st[j * 33 + lane], rs), cs), b);
                 }
                 __syncwarp();
             }
@@ -363,7 +372,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint8_t *stages = smem;
-    float *part = reinterpret_cast<float *>(smem);   // [BM][BN] partial, reuses stage 0
+    float *part = reinterpret_cast<float *>(smem);   // [BM][bn] partial, reuses the ring
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kRingBytes + kEpiBytes);
     uint64_t *empty = full + kMaxStages;
     uint64_t *acc_full = empty + kMaxStages;
@@ -375,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t rank;
     asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
     const int t = blockIdx.x / S;
-    const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * BN;
+    const int m0 = (t / a.tiles_n) * BM, n0 = (t % a.tiles_n) * a.bn;
     const int nk = a.K / BK;
     const int kb0 = (int)rank * nk / S, kb1 = ((int)rank + 1) * nk / S;
 
@@ -406,7 +415,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();
     pdl_launch_dependents();
 
-    const uint32_t stage_tx = (uint32_t)(a.a_loads * kATile + a.b_parts * kBTile);
+    const uint32_t stage_tx = (uint32_t)(a.a_loads * kATile + a.b_parts * a.b_tile);
     if (warp == 0) {
         if (lane == 0) {
             for (int kb = kb0; kb < kb1; ++kb) {
@@ -419,7 +428,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tma_load_2d(sp, &mA0, kb * BK, m0, &full[st]);
                 if (a.a_loads > 1) tma_load_2d(sp + kATile, &mA1, kb * BK, m0, &full[st]);
                 tma_load_2d(sp + 2 * kATile, &mB0, kb * BK, n0, &full[st]);
-                if (a.b_parts > 1) tma_load_2d(sp + 2 * kATile + kBTile, &mB1, kb * BK, n0, &full[st]);
+                if (a.b_parts > 1) tma_load_2d(sp + 2 * kATile + a.b_tile, &mB1, kb * BK, n0, &full[st]);
             }
         }
         __syncwarp();
@@ -443,16 +452,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t sp = smem_u32(stages + (size_t)st * a.stage_bytes);
-                const uint32_t a0 = sp, a1 = sp + kATile, b0 = sp + 2 * kATile, b1 = b0 + kBTile;
-                const uint32_t td = tmem + (uint32_t)((it % kSplitAcc) * BN);
+                const uint32_t a0 = sp, a1 = sp + kATile, b0 = sp + 2 * kATile, b1 = b0 + a.b_tile;
+                const uint32_t td = tmem + (uint32_t)((it % kSplitAcc) * a.bn);
                 uint32_t acc = it >= (uint32_t)kSplitAcc;   // the first block of an accumulator overwrites it
 #pragma unroll
                 for (int k = 0; k < BK / 8; ++k) {
                     const uint32_t ko = k * 32;
-                    mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), acc);
+                    mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), a.idesc, acc);
                     acc = 1;
-                    if (a.a_parts > 1) mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), 1);
-                    if (a.b_parts > 1) mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), 1);
+                    if (a.a_parts > 1) mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), a.idesc, 1);
+                    if (a.b_parts > 1) mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b1 + ko), a.idesc, 1);
                 }
                 mma_commit(&empty[st]);
             }
@@ -467,17 +476,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // warp-uniform, so that the tcgen05.ld below stay converged
         const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[0], 0, a.status));
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 0; c0 < a.bn; c0 += 32) {
             float sum[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
             for (int ai = 0; ai < nacc && ok; ++ai) {
                 uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ai * BN + c0), r);
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ai * a.bn + c0), r);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
             }
-            float4 *row = reinterpret_cast<float4 *>(part + (size_t)R * BN);
+            float4 *row = reinterpret_cast<float4 *>(part + (size_t)R * a.bn);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
                 row[((c0 >> 2) + i) ^ (R & 31)] =
@@ -489,45 +498,54 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp >= 2 && warp < kConvWarp0) {
         // ---- rows [rank BM/S, (rank+1) BM/S): sum the S partials, rank order ----
-        const int rows = BM / S, e = warp - 2;
-        const int c = lane;   // 16-byte chunk: columns 4c .. 4c+3
-        const int n = n0 + 4 * c;
-        float cs[4], bs[4];
+        const int r0 = (int)rank * BM / S, r1 = ((int)rank + 1) * BM / S, e = warp - 2;
+        for (int c = lane; c < a.bn / 4; c += 32) {   // 16-byte chunk: columns 4c .. 4c+3
+            const int n = n0 + 4 * c;
+            float cs[4], bs[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const bool in = n + i < a.N;
-            cs[i] = in && a.colscale ? a.colscale[n + i] : 1.0f;
-            bs[i] = in && a.bias ? a.bias[n + i] : 0.0f;
-        }
-        for (int rr = e; rr < rows; rr += kEpiWarpsTc) {
-            const int R = (int)rank * rows + rr, m = m0 + R;
-            const uint32_t off = smem_u32(part) + (uint32_t)(R * BN * 4 + 16 * (c ^ (R & 31)));
-            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            for (int j = 0; j < S; ++j) {
-                uint32_t raddr;
-                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(off), "r"(j));
-                float4 p;
-                asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                             : "=f"(p.x), "=f"(p.y), "=f"(p.z), "=f"(p.w)
-                             : "r"(raddr)
-                             : "memory");
-                v[0] = __fadd_rn(v[0], p.x);
-                v[1] = __fadd_rn(v[1], p.y);
-                v[2] = __fadd_rn(v[2], p.z);
-                v[3] = __fadd_rn(v[3], p.w);
+            for (int i = 0; i < 4; ++i) {
+                const bool in = n + i < a.N;
+                cs[i] = in && a.colscale ? a.colscale[n + i] : 1.0f;
+                bs[i] = in && a.bias ? a.bias[n + i] : 0.0f;
             }
-            if (m < a.M) {
-                const float rs = a.rowscale ? a.rowscale[m] : 1.0f;
-                float o[4];
+            for (int R = r0 + e; R < r1; R += kEpiWarpsTc) {
+                const int m = m0 + R;
+                const uint32_t off = smem_u32(part) + (uint32_t)((R * a.bn + 4 * (c ^ (R & 31))) * 4);
+                // every partial's chunk in flight at once, then added in rank order
+                float4 pj[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] = __fadd_rn(__fmul_rn(__fmul_rn(v[i], rs), cs[i]), bs[i]);
-                float *yp = a.Y + (size_t)m * a.N + n;
-                if (a.y_vec4 && n + 3 < a.N) {
-                    *reinterpret_cast<float4 *>(yp) = make_float4(o[0], o[1], o[2], o[3]);
-                } else {
+                for (int j = 0; j < 4; ++j) {
+                    if (j < S) {
+                        uint32_t raddr;
+                        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(off), "r"(j));
+                        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                     : "=f"(pj[j].x), "=f"(pj[j].y), "=f"(pj[j].z), "=f"(pj[j].w)
+                                     : "r"(raddr));
+                    }
+                }
+                float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        if (n + i < a.N) yp[i] = o[i];
+                for (int j = 0; j < 4; ++j) {
+                    if (j < S) {
+                        v[0] = __fadd_rn(v[0], pj[j].x);
+                        v[1] = __fadd_rn(v[1], pj[j].y);
+                        v[2] = __fadd_rn(v[2], pj[j].z);
+                        v[3] = __fadd_rn(v[3], pj[j].w);
+                    }
+                }
+                if (m < a.M) {
+                    const float rs = a.rowscale ? a.rowscale[m] : 1.0f;
+                    float o[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o[i] = __fadd_rn(__fmul_rn(__fmul_rn(v[i], rs), cs[i]), bs[i]);
+                    float *yp = a.Y + (size_t)m * a.N + n;
+                    if (a.y_vec4 && n + 3 < a.N) {
+                        *reinterpret_cast<float4 *>(yp) = make_float4(o[0], o[1], o[2], o[3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            if (n + i < a.N) yp[i] = o[i];
+                    }
                 }
             }
         }
@@ -644,13 +662,6 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
         return lalb_fail(ctx, LALB_ERR_INVALID, "tc_gemm: M, N > 0, K a multiple of %d", BK);
     if (((uintptr_t)p.a_hi | (uintptr_t)p.a_lo | (uintptr_t)p.b_hi | (uintptr_t)p.b_lo) & 15u)
         return lalb_fail(ctx, LALB_ERR_INVALID, "tc_gemm: operands must be 16-byte aligned");
-    CUtensorMap mA0, mA1, mB0, mB1;
-    int st;
-    if ((st = make_map(ctx, &mA0, p.a_hi, p.M, p.K, BM))) return st;
-    if ((st = make_map(ctx, &mA1, p.a_lo ? p.a_lo : p.a_hi, p.M, p.K, BM))) return st;
-    if ((st = make_map(ctx, &mB0, p.b_hi, p.N, p.K, BN))) return st;
-    if ((st = make_map(ctx, &mB1, p.b_lo ? p.b_lo : p.b_hi, p.N, p.K, BN))) return st;
-    if ((st = lalb_set_smem_attr(ctx, (const void *)tc_gemm_tf32_kernel, (int)kTcSmem))) return st;
     TcArgs a = {};
     a.M = p.M;
     a.N = p.N;
@@ -659,33 +670,79 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     a.a_parts = (p.a_lo || a.conv_a) ? 2 : 1;
     a.a_loads = p.a_lo ? 2 : 1;
     a.b_parts = p.b_lo ? 2 : 1;
-    // ring slot: A hi | A lo | B hi (| B lo), each 16 KB and 1024-byte aligned
-    a.stage_bytes = 2 * kATile + (uint32_t)a.b_parts * kBTile;
-    a.nstages = (int)std::min<uint32_t>(kMaxStages, kRingBytes / a.stage_bytes);
-    if (a.nstages < 2 || (size_t)a.nstages * a.stage_bytes > kRingBytes)
-        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "tc_gemm: ring layout");
-    a.tiles_n = (p.N + BN - 1) / BN;
-    a.tiles = a.tiles_n * ((p.M + BM - 1) / BM);
-    const bool long_k = p.K / BK > kLongK;
-    a.nacc = long_k ? 4 : 2;
-    a.ngroups = long_k ? 1 : 2;
     a.Y = p.Y;
     a.rowscale = p.rowscale;
     a.colscale = p.colscale;
     a.bias = p.bias;
     a.status = &ctx->scratch->status;
-    a.splits = 1;
     a.y_vec4 = (p.N % 4 == 0) && ((uintptr_t)p.Y & 15u) == 0;
-    // few output tiles: split K over clusters of S CTAs so that most SMs work
-    for (int S = 4; S >= 2; S /= 2) {
-        if (a.tiles * S > ctx->sm_count || p.K / BK < 2 * S) continue;
-        if ((st = lalb_set_smem_attr(ctx, (const void *)tc_gemm_tf32_splitk_kernel, (int)kTcSmem))) return st;
-        if (splitk_clusters_fit(ctx, S) < a.tiles) continue;   // one wave of clusters or nothing
-        a.splits = S;
-        return launch_cluster_pdl(ctx, (const void *)tc_gemm_tf32_splitk_kernel, dim3(a.tiles * S),
-                                  dim3(kTcThreads), kTcSmem, S, s,
-                                  {(void *)&mA0, (void *)&mA1, (void *)&mB0, (void *)&mB1, (void *)&a});
+    int st;
+    if ((st = lalb_set_smem_attr(ctx, (const void *)tc_gemm_tf32_kernel, (int)kTcSmem))) return st;
+    if ((st = lalb_set_smem_attr(ctx, (const void *)tc_gemm_tf32_splitk_kernel, (int)kTcSmem))) return st;
+
+    // Plan: tile width bn (256 only with one B part, its ring slot then 64 KB,
+    // and only for many tiles) and split S (a cluster of S CTAs per tile when
+    // one wave of them fits).  The K-loop is bound by the shared memory each SM
+    // moves per K-block: TMA writes, the converters' reads and writes, and the
+    // MMAs' operand reads; the plan with the fewest such bytes on the busiest
+    // SM wins.
+    const int nk = p.K / BK, tiles_m = (p.M + BM - 1) / BM;
+    const int mmas_per_k8 = a.a_parts + (a.b_parts - 1);
+    int best_bn = BN, best_s = 1;
+    double best_cost = 1e300;
+    for (int bn : {BN, kBNWide}) {
+        // 256-wide tiles only for the persistent kernel over many tiles: in one
+        // wave (and with split-K) they measured slower than 128-wide ones
+        if (bn == kBNWide && (a.b_parts > 1 || ((p.N + BN - 1) / BN) * tiles_m <= 2 * ctx->sm_count))
+            continue;
+        const int tiles = ((p.N + bn - 1) / bn) * tiles_m;
+        const double kb_bytes = (double)a.a_loads * kATile + (double)a.b_parts * bn * BK * 4 +
+                                (a.conv_a ? 2.0 * kATile : 0.0) +
+                                (double)(BK / 8) * mmas_per_k8 * (BM * 8 * 4 + bn * 8 * 4);
+        for (int S = 1; S <= (bn == BN ? 4 : 1); ++S) {
+            double cost;
+            if (S == 1) {
+                const double waves = tiles <= ctx->sm_count ? 1.0 : (double)tiles / ctx->sm_count;
+                cost = waves * nk * kb_bytes;
+            } else {
+                if (tiles * S > ctx->sm_count || nk < 2 * S) continue;
+                if (splitk_clusters_fit(ctx, S) < tiles) continue;   // one wave of clusters or nothing
+                cost = (double)nk / S * kb_bytes + 2.0 * BM * bn * 4;   // + the partial's write and reads
+            }
+            if (cost < best_cost * 0.97) {   // ties go to the simpler plan
+                best_cost = cost;
+                best_bn = bn;
+                best_s = S;
+            }
+        }
     }
+    a.bn = best_bn;
+    a.b_tile = (uint32_t)a.bn * BK * 4;
+    a.idesc = idesc_tf32(a.bn);
+    // ring slot: A hi | A lo | B hi (| B lo), each 1024-byte aligned
+    a.stage_bytes = 2 * kATile + (uint32_t)a.b_parts * a.b_tile;
+    a.nstages = (int)std::min<uint32_t>(kMaxStages, kRingBytes / a.stage_bytes);
+    if (a.nstages < 2 || (size_t)a.nstages * a.stage_bytes > kRingBytes)
+        return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "tc_gemm: ring layout");
+    a.tiles_n = (p.N + a.bn - 1) / a.bn;
+    a.tiles = a.tiles_n * tiles_m;
+    // accumulators: 512 TMEM columns hold nacc x ngroups tiles of bn columns;
+    // short K: two groups (the epilogue of one tile overlaps the next tile's
+    // MMAs), long K: one group of more accumulators (shorter fp32 chains)
+    const bool long_k = nk > kLongK;
+    a.nacc = (long_k ? 4 : 2) * BN / a.bn;
+    a.ngroups = long_k ? 1 : 2;
+    a.splits = best_s;
+
+    CUtensorMap mA0, mA1, mB0, mB1;
+    if ((st = make_map(ctx, &mA0, p.a_hi, p.M, p.K, BM))) return st;
+    if ((st = make_map(ctx, &mA1, p.a_lo ? p.a_lo : p.a_hi, p.M, p.K, BM))) return st;
+    if ((st = make_map(ctx, &mB0, p.b_hi, p.N, p.K, a.bn))) return st;
+    if ((st = make_map(ctx, &mB1, p.b_lo ? p.b_lo : p.b_hi, p.N, p.K, a.bn))) return st;
+    if (a.splits > 1)
+        return launch_cluster_pdl(ctx, (const void *)tc_gemm_tf32_splitk_kernel, dim3(a.tiles * a.splits),
+                                  dim3(kTcThreads), kTcSmem, a.splits, s,
+                                  {(void *)&mA0, (void *)&mA1, (void *)&mB0, (void *)&mB1, (void *)&a});
     const int grid = std::min(a.tiles, ctx->sm_count);
     return launch_pdl(ctx, (const void *)tc_gemm_tf32_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, s,
                       {(void *)&mA0, (void *)&mA1, (void *)&mB0, (void *)&mB1, (void *)&a});

@@ -79,12 +79,17 @@ def test_logic_codes_pack_and_forward_match_oracle(ctx, rows, K, M):
     L.close()
 
 
-# outputs with few 128 x 128 tiles take the split-K kernel (clusters of 4 or 2
-# CTAs summing their partial tiles through distributed shared memory): 4-way
-# (448 rows), 2-way (640 rows: 40 tiles), a ragged last tile with rows not a
-# multiple of 4 (scalar stores), and token counts that end inside a tile
+# outputs with few tiles take the split-K kernel (clusters of 2 to 4 CTAs
+# summing their partial tiles through distributed shared memory), outputs with
+# many tiles the persistent kernel with 256-column tiles: 4-way (448 rows),
+# 3-way (640 rows: 40 tiles), one wave of 128-wide tiles (1344, 1300, 1790,
+# 1792 rows: ragged last tiles), a ragged last tile with rows not a multiple of
+# 4 (scalar stores), token counts that end inside a tile, and the 256-wide
+# persistent kernel (32768 rows; 16384 rows over 1024 tokens)
 @pytest.mark.parametrize("rows,K,M", [(448, 448, 1024), (640, 448, 1024), (450, 448, 256),
-                                      (448, 1792, 100), (90, 256, 33)])
+                                      (1344, 448, 1024), (1300, 448, 1024), (1790, 448, 1024),
+                                      (1792, 448, 1024), (448, 1792, 100), (90, 256, 33),
+                                      (32768, 448, 200), (16384, 448, 1024)])
 def test_logic_layer_split_k_shapes_match_oracle(ctx, rows, K, M):
     W = O.normal(rows * K, seed=rows * 3 + K, sigma=0.02).reshape(rows, K)
     st = O.logic_state(rows * 17 + K, rows * K, 0.10, 0.50).reshape(rows, K)

@@ -100,6 +100,29 @@ def test_q4k_gemv_parity(ctx, rows, K):
     assert np.array_equal(host(y2), host(y))
 
 
+def test_q4k_gemv_sees_weights_written_by_the_previous_kernel(ctx):
+    """The standalone matvec overlaps the preceding kernel in the stream
+    (programmatic dependent launch) but must see what that kernel wrote: W
+    re-quantized into the same buffer by the GPU quantizer right before each
+    call, alternating between two matrices, with no host synchronisation."""
+    rows, K = 4096, 3584
+    wa = O.normal(rows * K, seed=91, sigma=0.02).reshape(rows, K)
+    wb = O.normal(rows * K, seed=92, sigma=0.02).reshape(rows, K)
+    x = O.normal(K, seed=93)
+    xq, sx, sq = O.quantize_act(x)
+    refs = [O.q4k_matmul(O.q4k_quantize(w), rows, K, xq, sx, sq)[0][0] for w in (wa, wb)]
+    wd = [dev(wa), dev(wb)]
+    xd = dev(x)
+    Wd = ctx.q4k_quantize(wd[0])
+    ys = []
+    for i in range(6):
+        ctx.q4k_quantize(wd[i % 2], out=Wd)   # the kernel right before the matvec writes W
+        ys.append(ctx.matmul_q4_k(Wd, xd, rows, K))
+    torch.cuda.synchronize()
+    for i, y in enumerate(ys):
+        assert_fp32_parity(host(y), refs[i % 2])
+
+
 def test_q4k_gemv_rejects_bad_arguments(ctx):
     W = torch.zeros(4 * 144 * 2 + 16, dtype=torch.uint8, device="cuda")
     x = torch.zeros(512, dtype=torch.float32, device="cuda")
