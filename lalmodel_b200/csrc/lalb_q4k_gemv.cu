@@ -145,27 +145,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
     }
     __syncthreads();
     const uint64_t policy = l2_evict_first_policy();
-    if (a.w_l2_first) {
-        // The weights may be the preceding kernel's output: before the
-        // dependency wait this CTA's rows are only prefetched into L2 (L2 is
-        // where that kernel's writes land, so nothing stale is kept), and the
-        // shared-memory stream starts after it.
-        if (warp == 0) {
-            const uint8_t *w0 = a.W + (size_t)r0 * row_bytes;
-            const size_t bytes = (size_t)(r1 - r0) * row_bytes;   // a multiple of 16
-            for (size_t off = (size_t)lane * 32768; off < bytes; off += 32 * 32768)
-                bulk_prefetch_l2(w0 + off, (uint32_t)(bytes - off < 32768 ? bytes - off : 32768));
-        }
-        pdl_wait();
-        if (kw == 0 && lane == 0)
-            for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
-    } else {
-        // The weights are never written by the preceding kernel, so their
-        // stream starts before the dependency wait; activations come after it.
-        if (kw == 0 && lane == 0)
-            for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
-        pdl_wait();
-    }
+    if (kw == 0 && lane == 0)
+        for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
+
+    // The weights are never written by the preceding kernel, so their
+    // stream starts before the dependency wait; activations come after it.
+    pdl_wait();
 
     // ---- activation prologue -------------------------------------------------
     if (IN == kInQ8) {
@@ -385,9 +370,7 @@ void *select_kernel(int in, int epi) {
 }  // namespace
 
 // Launches one Q4_K matvec.  `unit` = row granularity of the CTA split (64
-// for the SwiGLU epilogue).  ctas_per_sm: 1 or 2 (clamped to what fits), or 0:
-// one CTA per SM sized so that the next launch's CTA fits beside it (with
-// programmatic dependent launch the two overlap).
+// for the SwiGLU epilogue).  ctas_per_sm: 1 or 2 (clamped to what fits).
 int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int epi,
                          cudaStream_t stream, bool pdl, int ctas_per_sm) {
     Q4kGemvArgs a = args_in;
@@ -411,7 +394,7 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int 
     a.act_bulk = in == kInQ8 ? (al16(a.xq) && al16(a.sx) && al16(a.sumq)) : al16(a.x);
 
     // teams: as many as fit the thread, register and shared-memory budget
-    const size_t budget = ctas_per_sm != 1 ? 110 * 1024 : ctx->smem_optin - 1024;
+    const size_t budget = ctas_per_sm >= 2 ? 110 * 1024 : ctx->smem_optin - 1024;
     int teams = std::max(1, std::min(12 / wr, kMaxThreads / (32 * wr)));
     while (teams > 1 && make_layout(a.K, wr, teams).total > budget) --teams;
     Layout L = make_layout(a.K, wr, teams);
@@ -432,7 +415,7 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &args_in, int in, int 
     if (resident < 1) return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "q4k gemv: CTA does not fit");
     if (ctas_per_sm > resident) ctas_per_sm = resident;
     const int nunits = a.rows / a.unit;
-    int grid = ctx->sm_count * std::max(ctas_per_sm, 1);
+    int grid = ctx->sm_count * ctas_per_sm;
     if (grid > nunits) grid = nunits;
 
     cudaLaunchConfig_t cfg = {};
@@ -461,8 +444,7 @@ extern "C" int lalb_matmul_q4_k(lalb_ctx *ctx, const void *W, int rows, int K, c
     a.x = x;
     a.y = y;
     a.unit = 1;
-    a.w_l2_first = 1;   // W may be the output of the preceding kernel in the stream
-    return lalb_launch_q4k_gemv(ctx, a, kInF32, kEpiStore, (cudaStream_t)stream, true, 0);
+    return lalb_launch_q4k_gemv(ctx, a, kInF32, kEpiStore, (cudaStream_t)stream, false, 1);
 }
 
 extern "C" int lalb_matmul_q4_k_q8(lalb_ctx *ctx, const void *W, int rows, int K,
@@ -481,6 +463,5 @@ extern "C" int lalb_matmul_q4_k_q8(lalb_ctx *ctx, const void *W, int rows, int K
     a.y = y;
     a.isum = isum;
     a.unit = 1;
-    a.w_l2_first = 1;
-    return lalb_launch_q4k_gemv(ctx, a, kInQ8, kEpiStore, (cudaStream_t)stream, true, 0);
+    return lalb_launch_q4k_gemv(ctx, a, kInQ8, kEpiStore, (cudaStream_t)stream, false, 1);
 }
