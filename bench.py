@@ -201,7 +201,8 @@ def run_ste_case(args):
     """The seed STE model's forward matmuls (8 layers, d=448, FFN 1792, vocab
     32768) on X 1024 x 448 fp32: per-element CORE/BINARY/PRUNE weights drawn
     10/50/40, packed as int8 codes with a per-row scale; every matmul on the
-    tcgen05 tf32-part GEMM.  Prints its own JSON line (not the decode line)."""
+    tcgen05 tf32-part GEMM.  Two weight sets (larger than L2 together) are
+    used on alternate steps.  Prints its own JSON line (not the decode line)."""
     import torch
 
     import lalmodel_b200 as lb
@@ -212,45 +213,82 @@ def run_ste_case(args):
     gen.manual_seed(55)
     M, d, f = c["rows"], c["d"], c["ffn"]
     shapes = [(3 * d, d), (d, d), (f, d), (d, f)] * c["n_layer"] + [(c["vocab"], d)]
-    layers = []
-    for i, (rows, K) in enumerate(shapes):
-        W = torch.empty((rows, K), dtype=torch.float32, device="cuda")
-        ctx.fill_normal(W, seed=900 + i, sigma=0.02)
-        u = torch.rand((rows, K), generator=gen, device="cuda")
-        state = torch.where(u < 0.10, 0, torch.where(u < 0.60, 1, 2)).to(torch.uint8)
-        codes, srow = lb.LogicLayer.pack(ctx, W, state)
-        bias = torch.zeros(rows, dtype=torch.float32, device="cuda")
-        layers.append(lb.LogicLayer(ctx, codes, srow, bias, max_rows=M))
-        del W, u, state
+    nsets = 2
+    sets = []
+    for ws in range(nsets):
+        layers = []
+        for i, (rows, K) in enumerate(shapes):
+            W = torch.empty((rows, K), dtype=torch.float32, device="cuda")
+            ctx.fill_normal(W, seed=900 + 97 * ws + i, sigma=0.02)
+            u = torch.rand((rows, K), generator=gen, device="cuda")
+            state = torch.where(u < 0.10, 0, torch.where(u < 0.60, 1, 2)).to(torch.uint8)
+            codes, srow = lb.LogicLayer.pack(ctx, W, state)
+            bias = torch.zeros(rows, dtype=torch.float32, device="cuda")
+            layers.append(lb.LogicLayer(ctx, codes, srow, bias, max_rows=M))
+            del W, u, state
+        sets.append(layers)
     X = torch.empty((M, d), dtype=torch.float32, device="cuda")
     X2 = torch.empty((M, f), dtype=torch.float32, device="cuda")
     ctx.fill_normal(X, seed=7, sigma=1.0)
     ctx.fill_normal(X2, seed=8, sigma=1.0)
     outs = [torch.empty((M, rows), dtype=torch.float32, device="cuda") for rows, _ in shapes]
     flops = sum(2.0 * M * rows * K for rows, K in shapes)
+    weight_bytes = sum(rows * K * 4 + rows * 8 for rows, K in shapes)   # codes as fp32 + scale, bias
     stream = torch.cuda.Stream()
 
-    def step():
+    def step(layers):
         for L, (rows, K), Y in zip(layers, shapes, outs):
             L.forward(X if K == d else X2, Y)
 
     with torch.cuda.stream(stream):
-        step()   # first calls set kernel attributes outside the capture
+        for layers in sets:
+            step(layers)   # first calls set kernel attributes outside the capture
     torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        step()
+    graphs = []
+    for layers in sets:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(layers)
+        graphs.append(g)
+    props = torch.cuda.get_device_properties(0)
+    sampler = ClockSampler("%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id,
+                                                 props.pci_device_id))
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            g.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(args.warmup):
+            graphs[i % nsets].replay()
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
         e0.record(stream)
-        for _ in range(args.steps):
-            g.replay()
+        for i in range(args.steps):
+            graphs[i % nsets].replay()
         e1.record(stream)
     torch.cuda.synchronize()
+    clocks = sampler.stop()
     ms = e0.elapsed_time(e1) / args.steps
     tflops = flops / (ms * 1e-3) / 1e12
+
+    # end to end through the public entry point: the step's activations copied
+    # in from pinned host memory, the first row of the LM-head output copied back
+    hx, hx2 = X.cpu().pin_memory(), X2.cpu().pin_memory()
+    hy = torch.empty(c["vocab"], dtype=torch.float32).pin_memory()
+    n_e2e = max(5, min(args.steps, 50))
+    with torch.cuda.stream(stream):
+        for i in range(2):
+            graphs[i % nsets].replay()
+        stream.synchronize()
+        t0 = time.perf_counter()
+        for i in range(n_e2e):
+            X.copy_(hx, non_blocking=True)
+            X2.copy_(hx2, non_blocking=True)
+            graphs[i % nsets].replay()
+            hy.copy_(outs[-1][0], non_blocking=True)
+            stream.synchronize()
+        e2e_s = (time.perf_counter() - t0) / n_e2e
+    e2e = {"value": round(flops / e2e_s / 1e12, 2), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": int(hx.numel() * 4 + hx2.numel() * 4),
+           "d2h_bytes_per_step": int(hy.numel() * 4)}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
             bf16 = float(json.load(fh)["bf16_tflops"])
@@ -264,7 +302,7 @@ def run_ste_case(args):
     cpu = None
     if not args.no_cpu:
         O = _cpu_lib()
-        codes, srow, bias = (t.cpu().numpy() for t in layers[0]._keep)
+        codes, srow, bias = (t.cpu().numpy() for t in sets[0][0]._keep)
         xs = X[:64].cpu().numpy()
         rows, K = shapes[0]
         n, t0 = 0, time.perf_counter()
@@ -280,21 +318,26 @@ def run_ste_case(args):
     line = {"case": "seed-ste-forward", "metric": "seed STE forward matmuls TFLOPS",
             "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
             "dtype": "fp32 as tf32 parts (hi+lo activations x int8 codes), fp32 accumulate",
             "data": "synthetic: seeded N(0,0.02) weights, per-element states 10/50/40, X N(0,1)",
             "config": {"workload": "seed STE forward: 8 x (qkv 1344x448, o 448x448, fc 1792x448, "
                                    "down 448x1792) + LM head 32768x448 on X 1024x448",
-                       "flops_per_step": flops, "gemm_launches_per_step": len(shapes)},
+                       "flops_per_step": flops, "gemm_launches_per_step": len(shapes),
+                       "l2": "inputs larger than L2: two weight sets of %.0f MB on alternate steps"
+                             % (weight_bytes / 1e6)},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
                          "tensor_work": round(2 * tflops, 2), "peak": tf32_peak,
                          "peak_kind": kind, "unit": "TFLOP/s",
                          "frac": round(2 * tflops / tf32_peak, 4),
                          "traffic_head_launch": profile_traffic("tc_gemm_ste_head_ncu.md",
                                                                 "traffic_bytes_per_launch")},
-            "cpu_baseline": cpu}
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": len(shapes) * args.steps,
+            "clocks": clocks}
     print(json.dumps(line), flush=True)
-    for L in layers:
-        L.close()
+    for layers in sets:
+        for L in layers:
+            L.close()
     ctx.close()
 
 
