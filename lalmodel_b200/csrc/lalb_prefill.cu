@@ -78,7 +78,10 @@ constexpr int kSbSlots = 2;
 constexpr uint32_t kPSmem = 1024 + kPStages * kPStage + kSbSlots * kSbBytes + 512;
 static_assert(kPStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 static_assert(kPSmem <= 232448, "fits the 227 KB opt-in shared memory");
-constexpr int kActThreads = 1024, kActUnroll = 2;   // token preparation: 32 warps x 2 x 4 blocks in flight
+constexpr int kActThreads = 128;   // token preparation: 4 warps per token, 4 tokens per SM at once
+constexpr int kActCache = 20;      // 128-element groups a warp keeps in registers between the passes
+                                   // (K <= 4 x 20 x 128 = 10240 reads X once, longer rows
+                                   // re-read the rest)
 
 // kind::f16: f32 accumulator, fp16 A and B, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
@@ -365,7 +368,7 @@ __global__ void prefill_pack_kernel(const uint8_t *__restrict__ W, int rows, int
 // of two e (largest block amax * 2^e in [2^14, 2^15)), and
 //   Bhi + Blo = xq * sx * 2^e (fp16 parts),  Bx = the parts of sx * sumq * 2^e,
 //   inv[t] = 2^-e.
-__global__ void prefill_act_kernel(const float *__restrict__ X, int T, int K, __half *__restrict__ Bh,
+__global__ void __launch_bounds__(kActThreads, 4) prefill_act_kernel(const float *__restrict__ X, int T, int K, __half *__restrict__ Bh,
                                    __half *__restrict__ Bl, __nv_bfloat16 *__restrict__ Bx,
                                    float *__restrict__ inv) {
     __shared__ float s_amax[32];
@@ -378,11 +381,23 @@ __global__ void prefill_act_kernel(const float *__restrict__ X, int T, int K, __
     // workspace written here: wait for it before any global access
     pdl_wait();
     pdl_launch_dependents();
-    // pass 1: the token's largest |x| (rows are 16-byte aligned: K % 256 == 0)
+    // pass 1: the token's largest |x| (rows are 16-byte aligned: K % 256 == 0).
+    // A warp takes the 128-element groups g = warp + i nwarp, a lane 4
+    // consecutive elements of each; the first kActCache stay in registers
+    // for pass 2.
+    const int ngrp = nb / 4;                 // K % 256 == 0: whole groups
     float m = 0.0f;
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
-    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
-        const float4 v = x4[i];
+    float4 cache[kActCache];
+#pragma unroll
+    for (int i = 0; i < kActCache; ++i) {
+        const int g = warp + i * nwarp;
+        cache[i] = g < ngrp ? x4[g * 32 + lane] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float4 v = cache[i];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    for (int g = warp + kActCache * nwarp; g < ngrp; g += nwarp) {
+        const float4 v = x4[g * 32 + lane];
         m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
     m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
@@ -403,54 +418,52 @@ __global__ void prefill_act_kernel(const float *__restrict__ X, int T, int K, __
     __syncthreads();
     const float sc2 = s_scale;
     __nv_bfloat16 *bx = Bx + (size_t)t * (K / 4);
-    // pass 2: a warp takes 4 consecutive 32-blocks (128 elements), a lane 4
-    // consecutive elements, so a block is 8 lanes; kActUnroll groups per round
-    const int ngrp = nb / 4;                 // K % 256 == 0: whole groups
+    // pass 2: a block is 8 lanes of a group
     const int sub = lane & 7;                // lane within its block
-    for (int g0 = warp; g0 < ngrp; g0 += nwarp * kActUnroll) {
+    auto group = [&](int g, const float4 v) {
+        const int j = g * 4 + (lane >> 3);   // this lane's block
+        float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-        for (int u = 0; u < kActUnroll; ++u) {
-            const int g = g0 + u * nwarp;
-            if (g >= ngrp) break;
-            const int j = g * 4 + (lane >> 3);   // this lane's block
-            const float4 v = x4[g * 32 + lane];
-            float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        for (int o = 1; o < 8; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        const float d = __fdiv_rn(a, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+        int qv[4], sq = 0;
 #pragma unroll
-            for (int o = 1; o < 8; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-            const float d = __fdiv_rn(a, 127.0f);
-            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-            const float vv[4] = {v.x, v.y, v.z, v.w};
-            int qv[4], sq = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float tq = roundf(__fmul_rn(vv[e], id));
-                qv[e] = tq > 127.0f ? 127 : (tq < -127.0f ? -127 : (int)tq);
-                sq += qv[e];
-            }
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-            __align__(8) __half hh[4], hl[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float b = __fmul_rn(__fmul_rn((float)qv[e], d), sc2);
-                hh[e] = __float2half_rn(b);
-                hl[e] = __float2half_rn(b - __half2float(hh[e]));
-            }
-            const size_t off = (size_t)t * K + (size_t)g * 128 + lane * 4;
-            *reinterpret_cast<uint2 *>(Bh + off) = *reinterpret_cast<const uint2 *>(hh);
-            *reinterpret_cast<uint2 *>(Bl + off) = *reinterpret_cast<const uint2 *>(hl);
-            // the block's min-term parts: 16 values per pair of blocks
-            __nv_bfloat16 *o = bx + (j >> 1) * 16;
-            if (sub == 0) {
-                __nv_bfloat16 a0, a1, a2;
-                split3_bf16(__fmul_rn(__fmul_rn(d, (float)sq), sc2), a0, a1, a2);
-                __nv_bfloat16 *p = o + (j & 1) * 6;
-                p[0] = a0; p[1] = a1; p[2] = a0; p[3] = a2; p[4] = a1; p[5] = a0;
-            } else if ((j & 1) == 0 && sub < 5) {
-                o[12 + sub - 1] = __float2bfloat16_rn(0.0f);
-            }
+        for (int e = 0; e < 4; ++e) {
+            const float tq = roundf(__fmul_rn(vv[e], id));
+            qv[e] = tq > 127.0f ? 127 : (tq < -127.0f ? -127 : (int)tq);
+            sq += qv[e];
         }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        __align__(8) __half hh[4], hl[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float b = __fmul_rn(__fmul_rn((float)qv[e], d), sc2);
+            hh[e] = __float2half_rn(b);
+            hl[e] = __float2half_rn(b - __half2float(hh[e]));
+        }
+        const size_t off = (size_t)t * K + (size_t)g * 128 + lane * 4;
+        *reinterpret_cast<uint2 *>(Bh + off) = *reinterpret_cast<const uint2 *>(hh);
+        *reinterpret_cast<uint2 *>(Bl + off) = *reinterpret_cast<const uint2 *>(hl);
+        // the block's min-term parts: 16 values per pair of blocks
+        __nv_bfloat16 *o = bx + (j >> 1) * 16;
+        if (sub == 0) {
+            __nv_bfloat16 a0, a1, a2;
+            split3_bf16(__fmul_rn(__fmul_rn(d, (float)sq), sc2), a0, a1, a2);
+            __nv_bfloat16 *p = o + (j & 1) * 6;
+            p[0] = a0; p[1] = a1; p[2] = a0; p[3] = a2; p[4] = a1; p[5] = a0;
+        } else if ((j & 1) == 0 && sub < 5) {
+            o[12 + sub - 1] = __float2bfloat16_rn(0.0f);
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < kActCache; ++i) {
+        const int g = warp + i * nwarp;
+        if (g < ngrp) group(g, cache[i]);
     }
+    for (int g = warp + kActCache * nwarp; g < ngrp; g += nwarp) group(g, x4[g * 32 + lane]);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
