@@ -38,6 +38,8 @@ struct Q4kGemvArgs {
     float *act_out;        //   nullable: the fp32 product [rows/2]
     int unit;              // CTA row split granularity (64 for kEpiSwiglu)
     int act_bulk;          // set by the launcher: activations arrive by bulk copy
+    int w_l2_first;        // the weights may come from the preceding kernel: before the
+                           //   dependency wait they are only prefetched into L2
     int wr, teams;         // set by the launcher: warps per row, teams per CTA
     int nstages;           // set by the launcher
     unsigned int *status;  // set by the launcher

@@ -145,12 +145,27 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
     }
     __syncthreads();
     const uint64_t policy = l2_evict_first_policy();
-    if (kw == 0 && lane == 0)
-        for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
-
-    // The weights are never written by the preceding kernel, so their
-    // stream starts before the dependency wait; activations come after it.
-    pdl_wait();
+    if (a.w_l2_first) {
+        // The weights may be the preceding kernel's output: before the
+        // dependency wait this CTA's rows are only prefetched into L2 (where
+        // that kernel's writes land, so nothing stale is kept), and the
+        // shared-memory stream starts after it.
+        if (warp == 0) {
+            const uint8_t *w0 = a.W + (size_t)r0 * row_bytes;
+            const size_t bytes = (size_t)(r1 - r0) * row_bytes;   // a multiple of 16
+            for (size_t off = (size_t)lane * 32768; off < bytes; off += 32 * 32768)
+                bulk_prefetch_l2(w0 + off, (uint32_t)(bytes - off < 32768 ? bytes - off : 32768));
+        }
+        pdl_wait();
+        if (kw == 0 && lane == 0)
+            for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
+    } else {
+        // The weights are never written by the preceding kernel, so their
+        // stream starts before the dependency wait; activations come after it.
+        if (kw == 0 && lane == 0)
+            for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
+        pdl_wait();
+    }
 
     // ---- activation prologue -------------------------------------------------
     if (IN == kInQ8) {
@@ -444,7 +459,8 @@ extern "C" int lalb_matmul_q4_k(lalb_ctx *ctx, const void *W, int rows, int K, c
     a.x = x;
     a.y = y;
     a.unit = 1;
-    return lalb_launch_q4k_gemv(ctx, a, kInF32, kEpiStore, (cudaStream_t)stream, false, 1);
+    a.w_l2_first = 1;   // W may be the output of the preceding kernel in the stream
+    return lalb_launch_q4k_gemv(ctx, a, kInF32, kEpiStore, (cudaStream_t)stream, true, 1);
 }
 
 extern "C" int lalb_matmul_q4_k_q8(lalb_ctx *ctx, const void *W, int rows, int K,
@@ -463,5 +479,6 @@ extern "C" int lalb_matmul_q4_k_q8(lalb_ctx *ctx, const void *W, int rows, int K
     a.y = y;
     a.isum = isum;
     a.unit = 1;
-    return lalb_launch_q4k_gemv(ctx, a, kInQ8, kEpiStore, (cudaStream_t)stream, false, 1);
+    a.w_l2_first = 1;
+    return lalb_launch_q4k_gemv(ctx, a, kInQ8, kEpiStore, (cudaStream_t)stream, true, 1);
 }
