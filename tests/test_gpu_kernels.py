@@ -224,6 +224,9 @@ def make_decoder_weights(cfg, seed, n_vocab):
     dict(n_layer=1, hidden=3584, q_rows=3584, kv_rows=512, ffn=18944, vocab=20000),
     dict(n_layer=3, hidden=1024, q_rows=1024, kv_rows=256, ffn=4096, vocab=5000),
     dict(n_layer=0, hidden=768, q_rows=256, kv_rows=0, ffn=256, vocab=777),
+    # down rows of 9216 bytes (one per chunk) and 3-4 of them per CTA: every
+    # row goes through the persistent kernel's K-split of a CTA's last rows
+    dict(n_layer=2, hidden=512, q_rows=512, kv_rows=128, ffn=16384, vocab=3000),
 ])
 def test_decoder_step_matches_oracle_chain(ctx, cfg, path):
     layers, dl, lq, ls = make_decoder_weights(cfg, seed=1000 + cfg["hidden"], n_vocab=cfg["vocab"])
