@@ -780,13 +780,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 ss = warp_sum_d(ss);
                 if (lane == 0) red_s[ci] = ss;
                 cons_bar();
-                if (ct == 0) {
-                    double t = 0.0;
-                    for (int cw = 0; cw < kNC; ++cw) t += red_s[cw];
-                    red_s[kNC] = (double)(float)(1.0 / sqrt(t / (double)d.K + 1e-6));
-                }
-                cons_bar();
-                const float scale = (float)red_s[kNC];
+                // every thread adds the warps' partial sums in the same order:
+                // the same scale everywhere, with one barrier fewer
+                double t = 0.0;
+#pragma unroll
+                for (int cw = 0; cw < kNC; ++cw) t += red_s[cw];
+                const float scale = (float)(1.0 / sqrt(t / (double)d.K + 1e-6));
 #pragma unroll
                 for (int ps = 0; ps < kPrepPasses; ++ps)
 #pragma unroll
