@@ -4,31 +4,37 @@
 //   Y[m][n] = rowscale[m] * colscale[n] * sum_k A[m][k] * B[n][k] + bias[n]
 //
 // A (activations, [M][K]) and B (weights, [N][K]) are row-major fp32 in HBM,
-// both K-major.  Each is given as one or two tf32 parts (x = hi + lo, each
-// part exactly representable in tf32, so |x - hi - lo| <= 2^-22 |x|); the
-// kernel accumulates hi*hi + lo*hi (+ hi*lo when B has two parts) in fp32 in
-// TMEM.  This is the seed STE model's
-// forward (BinLayer) on tensor cores: the reference computes it in fp32 on
-// the CPU (runtime/lal_runtime.c bin_forward :1852-1938,
-// bin_forward_pure_float :543-582).
+// both K-major.  B is given as one or two tf32 parts (x = hi + lo, each part
+// exactly representable in tf32); A either the same way or raw (split_a),
+// in which case the kernel forms its parts on chip: hi is the raw fp32 read
+// by the tensor core as its tf32 truncation, lo = x - hi is written next to
+// it by converter warps.  The kernel accumulates hi*hi + lo*hi (+ hi*lo when
+// B has two parts) in fp32 in TMEM.  This is the seed STE model's forward
+// (BinLayer) on tensor cores: the reference computes it in fp32 on the CPU
+// (runtime/lal_runtime.c bin_forward :1852-1938, bin_forward_pure_float
+// :543-582).
 //
-// Persistent: one CTA per SM walks the 128 x 128 output tiles (tile t,
-// t + grid, ...), 6 warps:
+// tc_gemm_tf32_kernel, persistent: one CTA per SM walks the output tiles of
+// 128 x bn (bn = 128, or 256 over many tiles; tile t, t + grid, ...), 10 warps:
 //   warp 0     TMA producer: per 32-wide K-block, 2-D tiled copies
-//              (128-byte swizzle) of every part's A and B tiles into a
-//              3-stage ring (full mbarrier per stage);
+//              (128-byte swizzle) of the A and B parts into a ring of 4 slots
+//              (3 when B has two parts), full mbarrier per slot;
 //   warp 1     allocates all 512 TMEM columns and issues tcgen05.mma
-//              (kind::tf32, M=128, N=128, K=8 per instruction) from one lane.
+//              (kind::tf32, M=128, N=bn, K=8 per instruction) from one lane.
 //              K-block kb of a tile goes to accumulator kb % nacc of the
-//              tile's accumulator group; with short K there are two groups
-//              of two accumulators, so the next tile's MMAs run while the
-//              epilogue drains the previous tile; long K uses one group of
-//              four (shorter fp32 accumulation chains in the tensor core);
+//              tile's accumulator group; with short K there are two groups,
+//              so the next tile's MMAs run while the epilogue drains the
+//              previous tile; long K uses one group of more accumulators
+//              (shorter fp32 accumulation chains in the tensor core);
 //   warps 2-5  epilogue: wait for the group (commit), read each warp's 32
 //              TMEM lanes (= rows) 32 columns at a time from every
 //              accumulator (tcgen05.ld 32x32b.x32), add them, free the group,
 //              transpose through shared memory and write 128-byte row
-//              segments with the scales and bias.
+//              segments with the scales and bias;
+//   warps 6-9  converters (raw A only): A's lo part per slot.
+// tc_gemm_tf32_splitk_kernel: outputs with few tiles; a cluster of S CTAs
+// shares a tile along K and sums the partial tiles through distributed
+// shared memory (its comment below).  The host picks the tile width and S.
 // Every wait is bounded; on expiry the kernel raises the status word and
 // still drains and frees its TMEM.
 #include <cuda.h>
