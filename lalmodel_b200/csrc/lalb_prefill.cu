@@ -63,8 +63,9 @@ namespace {
 
 constexpr int PM = 128, PN = 128, PK = 64;   // PK fp16 = 128 B: one swizzle row
 constexpr int kPStages = 4;
-constexpr int kSlotsT = 4;                   // TMEM super-block slots (PN columns each)
-constexpr int kTmemCols = kSlotsT * PN;
+constexpr int kSlotsT = 2;                   // TMEM super-block slots
+constexpr int kSlotW = 2 * PN;               // a slot: B_hi products (PN columns), then B_lo's
+constexpr int kTmemCols = kSlotsT * kSlotW;
 constexpr int kEpiWarps = 16;
 constexpr int kPThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kPA = PM * PK * 2;        // 16 KB
@@ -83,10 +84,14 @@ constexpr int kActCache = 20;      // 128-element groups a warp keeps in registe
                                    // (K <= 4 x 20 x 128 = 10240 reads X once, longer rows
                                    // re-read the rest)
 
-// kind::f16: f32 accumulator, fp16 A and B, both K-major, M = 128, N = 128.
-constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
-// the same with bf16 A and B (the min-term MMA)
-constexpr uint32_t kIdescBF16 = kIdescF16 | (1u << 7) | (1u << 10);
+// kind::f16: f32 accumulator, fp16 A and B, both K-major, M = 128, N = 256:
+// B is B_hi's 128 token rows followed by B_lo's (adjacent in the stage), so
+// one MMA reads A once for both parts.
+constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(kSlotW >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
+// bf16 A and B, N = 128 (the min-term MMA, into the B_hi half)
+constexpr uint32_t kIdescBF16 =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
+static_assert(kOffBl == kOffBh + PN * 128, "B_lo's rows follow B_hi's in the stage");
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
@@ -233,12 +238,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 if (!mbar_wait_bounded(&full[s], (uint32_t)(kb / kPStages) & 1u, a.status)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t st = smem_u32(smem + (size_t)s * kPStage);
-                const uint32_t d = tmem + slot * PN;
+                const uint32_t d = tmem + slot * kSlotW;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {   // 16 weights per step, B_hi then B_lo
-                    const uint64_t ad = sw128_desc(st + kk * 32);
-                    mma_f16(d, ad, sw128_desc(st + kOffBh + kk * 32), kIdescF16, ((kb & 3) | kk) != 0 ? 1u : 0u);
-                    mma_f16(d, ad, sw128_desc(st + kOffBl + kk * 32), kIdescF16, 1u);
+                for (int kk = 0; kk < 4; ++kk) {   // 16 weights per step, B_hi and B_lo at once
+                    mma_f16(d, sw128_desc(st + kk * 32), sw128_desc(st + kOffBh + kk * 32), kIdescF16,
+                            ((kb & 3) | kk) != 0 ? 1u : 0u);
                 }
                 // the two sub-blocks' min terms
                 mma_f16(d, sw32_desc(st + kOffAx), sw32_desc(st + kOffBx), kIdescBF16, 1u);
@@ -268,10 +272,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const float D = sbring[sslot * PM + row];
             const float2 D2 = make_float2(D, D);
-            float S[32];
-            tmem_ld16(tbase + slot * PN, *reinterpret_cast<float(*)[16]>(S));
-            tmem_ld16(tbase + slot * PN + 16, *reinterpret_cast<float(*)[16]>(S + 16));
+            float S[32], L[32];
+            tmem_ld16(tbase + slot * kSlotW, *reinterpret_cast<float(*)[16]>(S));
+            tmem_ld16(tbase + slot * kSlotW + 16, *reinterpret_cast<float(*)[16]>(S + 16));
+            tmem_ld16(tbase + slot * kSlotW + PN, *reinterpret_cast<float(*)[16]>(L));
+            tmem_ld16(tbase + slot * kSlotW + PN + 16, *reinterpret_cast<float(*)[16]>(L + 16));
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+#pragma unroll
+            for (int i = 0; i < 32; ++i) S[i] = __fadd_rn(S[i], L[i]);   // B_hi + B_lo products
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&sempty[slot]);
