@@ -154,6 +154,11 @@ struct TcArgs {
     int nstages;                // ring slots in use
     uint32_t stage_bytes;       // A hi | A lo | B hi (| B lo)
     int bn;                     // output tile width: 128 or 256
+    int swap;                   // rows-as-M: B's tile is the MMA's M side, A's hi and lo
+                                //   parts (adjacent in the slot) its N = 256 side, so one
+                                //   MMA reads B once for both parts; TMEM lane = output
+                                //   column, TMEM column = output row (hi, then lo at +128)
+    int acc_cols;               // TMEM columns per accumulator
     uint32_t b_tile;            // bytes of one B part's tile: bn x BK fp32
     uint32_t idesc;             // MMA instruction descriptor for bn
     int tiles_n, tiles;         // output tiles along N, in all
@@ -278,11 +283,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t st = smem_u32(stages + (size_t)s * a.stage_bytes);
                     const uint32_t a0 = st, a1 = st + kATile, b0 = st + 2 * kATile, b1 = b0 + a.b_tile;
-                    const uint32_t td = tmem + (uint32_t)((g * a.nacc + kb % a.nacc) * a.bn);
+                    const uint32_t td = tmem + (uint32_t)((g * a.nacc + kb % a.nacc) * a.acc_cols);
                     uint32_t acc = kb >= a.nacc;   // the first block of an accumulator overwrites it
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {   // 8 tf32 = 32 bytes per instruction
                         const uint32_t ko = k * 32;
+                        if (a.swap) {   // B rows x (A hi rows ; A lo rows)
+                            mma_tf32(td, sw128_kmajor_desc(b0 + ko), sw128_kmajor_desc(a0 + ko), a.idesc, acc);
+                            acc = 1;
+                            continue;
+                        }
                         mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), a.idesc, acc);
                         acc = 1;
                         if (a.a_parts > 1)
@@ -306,6 +316,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int g = ti % a.ngroups;
             if (!mbar_wait_bounded(&acc_full[g], (ti / a.ngroups) & 1u, a.status)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (a.swap) {
+                // lane = output column n, TMEM columns = output rows: hi products
+                // at c, lo products at c + 128; row stores are 128 bytes per warp
+                const int n = n0 + q * 32 + lane;
+                const bool ncol = n < a.N;
+                const float cs = ncol && a.colscale ? a.colscale[n] : 1.0f;
+                const float b = ncol && a.bias ? a.bias[n] : 0.0f;
+                for (int c0 = 0; c0 < BM; c0 += 32) {
+                    float sum[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+                    for (int ai = 0; ai < nacc; ++ai) {
+                        uint32_t r[32];
+                        const uint32_t col = (uint32_t)((g * a.nacc + ai) * a.acc_cols + c0);
+                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col, r);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col + BM, r);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+                    }
+                    if (c0 == BM - 32) {   // the group's last columns are in registers: free it
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[g]);
+                    }
+                    const int mrow = m0 + c0 + lane;
+                    const float rs_lane = a.rowscale && mrow < a.M ? a.rowscale[mrow] : 1.0f;
+                    float *yc = a.Y + (size_t)(m0 + c0) * a.N + n;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+                        if (m0 + c0 + j < a.M && ncol)
+                            yc[(size_t)j * a.N] = __fadd_rn(__fmul_rn(__fmul_rn(sum[j], rs), cs), b);
+                    }
+                }
+                continue;
+            }
             for (int c0 = 0; c0 < a.bn; c0 += 32) {
                 float sum[32];
 #pragma unroll
@@ -459,11 +507,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t sp = smem_u32(stages + (size_t)st * a.stage_bytes);
                 const uint32_t a0 = sp, a1 = sp + kATile, b0 = sp + 2 * kATile, b1 = b0 + a.b_tile;
-                const uint32_t td = tmem + (uint32_t)((it % kSplitAcc) * a.bn);
+                const uint32_t td = tmem + (uint32_t)((it % kSplitAcc) * a.acc_cols);
                 uint32_t acc = it >= (uint32_t)kSplitAcc;   // the first block of an accumulator overwrites it
 #pragma unroll
                 for (int k = 0; k < BK / 8; ++k) {
                     const uint32_t ko = k * 32;
+                    if (a.swap) {   // B rows x (A hi rows ; A lo rows)
+                        mma_tf32(td, sw128_kmajor_desc(b0 + ko), sw128_kmajor_desc(a0 + ko), a.idesc, acc);
+                        acc = 1;
+                        continue;
+                    }
                     mma_tf32(td, sw128_kmajor_desc(a0 + ko), sw128_kmajor_desc(b0 + ko), a.idesc, acc);
                     acc = 1;
                     if (a.a_parts > 1) mma_tf32(td, sw128_kmajor_desc(a1 + ko), sw128_kmajor_desc(b0 + ko), a.idesc, 1);
@@ -482,13 +535,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // warp-uniform, so that the tcgen05.ld below stay converged
         const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[0], 0, a.status));
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        for (int c0 = 0; c0 < a.bn; c0 += 32) {
+        if (a.swap) {
+            // lane = output column R (of bn = 128), TMEM columns = output rows
+            // (hi at c, lo at c + 128): element (row t, column R) goes to the
+            // same swizzled place as above, t * bn + 4 ((R >> 2) ^ (t & 31)) + (R & 3)
+            for (int c0 = 0; c0 < BM; c0 += 32) {
+                float sum[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
+                for (int ai = 0; ai < nacc && ok; ++ai) {
+                    uint32_t r[32];
+                    const uint32_t col = (uint32_t)(ai * a.acc_cols + c0);
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col, r);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col + BM, r);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = c0 + j;
+                    part[(size_t)t * a.bn + 4 * ((R >> 2) ^ (t & 31)) + (R & 3)] = sum[j];
+                }
+            }
+        }
+        for (int c0 = 0; c0 < a.bn && !a.swap; c0 += 32) {
             float sum[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) sum[j] = 0.0f;
             for (int ai = 0; ai < nacc && ok; ++ai) {
                 uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ai * a.bn + c0), r);
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ai * a.acc_cols + c0), r);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
             }
@@ -694,6 +772,9 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     // SM wins.
     const int nk = p.K / BK, tiles_m = (p.M + BM - 1) / BM;
     const int mmas_per_k8 = a.a_parts + (a.b_parts - 1);
+    // rows-as-M (one MMA per step over A's adjacent hi and lo tiles) when A
+    // has two parts and B one, with 128-wide tiles
+    const bool can_swap = a.a_parts == 2 && a.b_parts == 1;
     int best_bn = BN, best_s = 1;
     double best_cost = 1e300;
     for (int bn : {BN, kBNWide}) {
@@ -702,9 +783,11 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
         if (bn == kBNWide && (a.b_parts > 1 || ((p.N + BN - 1) / BN) * tiles_m <= 2 * ctx->sm_count))
             continue;
         const int tiles = ((p.N + bn - 1) / bn) * tiles_m;
+        const double mma_bytes = (bn == BN && can_swap)
+                                     ? (double)(BK / 8) * (bn * 8 * 4 + 2 * BM * 8 * 4)
+                                     : (double)(BK / 8) * mmas_per_k8 * (BM * 8 * 4 + bn * 8 * 4);
         const double kb_bytes = (double)a.a_loads * kATile + (double)a.b_parts * bn * BK * 4 +
-                                (a.conv_a ? 2.0 * kATile : 0.0) +
-                                (double)(BK / 8) * mmas_per_k8 * (BM * 8 * 4 + bn * 8 * 4);
+                                (a.conv_a ? 2.0 * kATile : 0.0) + mma_bytes;
         for (int S = 1; S <= (bn == BN ? 4 : 1); ++S) {
             double cost;
             if (S == 1) {
@@ -724,7 +807,9 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     }
     a.bn = best_bn;
     a.b_tile = (uint32_t)a.bn * BK * 4;
-    a.idesc = idesc_tf32(a.bn);
+    a.swap = can_swap && a.bn == BN;
+    a.acc_cols = a.swap ? 2 * BM : a.bn;   // swap: N = 256 (A hi rows, then A lo rows)
+    a.idesc = idesc_tf32(a.swap ? 2 * BM : a.bn);
     // ring slot: A hi | A lo | B hi (| B lo), each 1024-byte aligned
     a.stage_bytes = 2 * kATile + (uint32_t)a.b_parts * a.b_tile;
     a.nstages = (int)std::min<uint32_t>(kMaxStages, kRingBytes / a.stage_bytes);
@@ -736,7 +821,7 @@ int lalb_tc_gemm_tf32(lalb_ctx *ctx, const TcGemmParts &p, cudaStream_t s) {
     // short K: two groups (the epilogue of one tile overlaps the next tile's
     // MMAs), long K: one group of more accumulators (shorter fp32 chains)
     const bool long_k = nk > kLongK;
-    a.nacc = (long_k ? 4 : 2) * BN / a.bn;
+    a.nacc = (long_k ? 4 : 2) * BN / a.acc_cols;
     a.ngroups = long_k ? 1 : 2;
     a.splits = best_s;
 
