@@ -32,6 +32,10 @@
 //              transpose through shared memory and write 128-byte row
 //              segments with the scales and bias;
 //   warps 6-9  converters (raw A only): A's lo part per slot.
+// Rows-as-M (swap, 128-wide tiles with two A parts and one B part): the MMA
+// takes B's 128 rows as M and A's hi and lo tiles, adjacent in the slot, as
+// one N = 256 operand, so B is read once per step instead of twice; TMEM
+// lanes are then output columns and the epilogue stores rows from registers.
 // tc_gemm_tf32_splitk_kernel: outputs with few tiles; a cluster of S CTAs
 // shares a tile along K and sums the partial tiles through distributed
 // shared memory (its comment below).  The host picks the tile width and S.
