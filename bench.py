@@ -11,10 +11,15 @@ Weights are seeded N(0, 0.02) drawn and quantized on the GPU by the library;
 the hidden state is seeded N(0, 1).  Attention is outside the measured path
 (the q projection stands in for the attention output).
 
-One JSON line on rank 0.  Under torchrun (N > 1) every rank runs an
-independent replica of the decode on its own GPU (weak scaling).
+One JSON line on rank 0.  Under torchrun (N > 1) the ranks decode the SAME
+token tensor-parallel (strong scaling): every rank holds a row shard of the
+gate/up, down and LM-head matrices (qkv and o whole), and the persistent
+kernels exchange rows over NVLink.  After the timed region the sharded token
+is checked against a one-GPU decoder built on rank 0 from the same seeds
+(`tp_check`); a mismatch fails the run.
 `--impl reference` times the CPU kernels (AVX2 + OpenMP port of the
-reference's absent lal_q4k_kernel.h / lal_q8_kernel.h) on the host cores.
+reference's absent lal_q4k_kernel.h / lal_q8_kernel.h) on the host cores,
+with the OpenMP team set to the host's core count.
 """
 import argparse
 import datetime
@@ -311,7 +316,7 @@ def run_ste_case(args):
             n += 1
         dt = (time.perf_counter() - t0) / n
         cpu_tflops = 2.0 * 64 * rows * K / dt / 1e12
-        cpu = {"value": round(cpu_tflops, 4), "unit": "TFLOP/s", "cores": os.cpu_count(),
+        cpu = {"value": round(cpu_tflops, 4), "unit": "TFLOP/s", "cores": O.lib().lalb_cpu_threads(),
                "kind": "port",
                "sample": "%d x layer-0 qkv (%dx%d codes) over 64 rows, %.2f ms each; step time "
                          "at this rate %.1f ms" % (n, rows, K, dt * 1e3, flops / (cpu_tflops * 1e12) * 1e3)}
@@ -676,6 +681,9 @@ def run_gpu(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = n_e2e / (float(t.item()) / 1000.0)
 
+    tp_check = check_tp_against_one_gpu(ctx, lb, torch, dist, dec, c, rank, world, stream) \
+        if tp else None
+
     gemv = gemv_standalone(ctx, torch, stream) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -685,7 +693,7 @@ def run_gpu(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8 (q4 x i8 dp4a -> int32 per 32-block, fp32 terms, f64 row sum)",
             "data": "synthetic: seeded N(0,0.02) weights quantized on the GPU (Q4_K min-max, "
                     "int8 per-row LM head); seeded N(0,1) hidden state",
@@ -706,6 +714,8 @@ def run_gpu(args, rank, world, local_rank):
             "gpu_launches": args.steps * launches,
             "clocks": clocks,
         }
+        if tp_check is not None:
+            line["tp_check"] = tp_check
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()   # no rank unmaps its exchange buffer while a peer may still use it
@@ -713,16 +723,90 @@ def run_gpu(args, rank, world, local_rank):
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+    if tp_check is not None and not tp_check["ok"]:
+        sys.exit(3)
+
+
+TP_CHECK_TOL = 1e-4   # normwise, after the rows of every shard are joined
+
+
+def check_tp_against_one_gpu(ctx, lb, torch, dist, dec, c, rank, world, stream, tokens=3):
+    """Runs `tokens` tokens through the tensor-parallel decoder (every rank)
+    and through a one-GPU decoder that rank 0 builds from the same seeds, and
+    compares the final residual stream, the joined logits and the argmax
+    (first maximum over the whole vocabulary).  Every rank takes the same
+    collective steps."""
+    r0, r1 = lb.tp_range(c, 4, world, rank)
+    shard = max(lb.tp_range(c, 4, world, j)[1] - lb.tp_range(c, 4, world, j)[0]
+                for j in range(world))
+    h_out = torch.empty(c["hidden"], dtype=torch.float32, device="cuda")
+    logits = torch.zeros(c["vocab"], dtype=torch.float32, device="cuda")
+    am = torch.empty(1, dtype=torch.int32, device="cuda")
+    h_in = torch.empty(c["hidden"], dtype=torch.float32, device="cuda")
+    outs = []
+    for t in range(tokens):
+        ctx.fill_normal(h_in, seed=4100 + t, sigma=1.0)
+        with torch.cuda.stream(stream):
+            dec.step(h_in, h_out, logits, am)
+        stream.synchronize()
+        part = torch.zeros(shard, dtype=torch.float32, device="cuda")
+        part[: r1 - r0] = logits[r0:r1]
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        outs.append((h_out.clone(), parts, int(am.item())))
+    dist.barrier()
+    result = None
+    if rank == 0:
+        one, _, _ = build_decoder(ctx, lb, torch, c, seed=1234, n_rank=1, rank=0)
+        ref_h = torch.empty_like(h_out)
+        ref_l = torch.empty_like(logits)
+        ref_am = torch.empty_like(am)
+        err_h, err_l, same_am, exact = 0.0, 0.0, True, []
+        for t, (h_tp, parts, am_tp) in enumerate(outs):
+            ctx.fill_normal(h_in, seed=4100 + t, sigma=1.0)
+            with torch.cuda.stream(stream):
+                one.step(h_in, ref_h, ref_l, ref_am)
+            stream.synchronize()
+            joined = torch.cat([p[: lb.tp_range(c, 4, world, j)[1] - lb.tp_range(c, 4, world, j)[0]]
+                                for j, p in enumerate(parts)])
+
+            def nerr(a, b):
+                return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+            err_h = max(err_h, nerr(h_tp, ref_h))
+            err_l = max(err_l, nerr(joined, ref_l))
+            same_am = same_am and am_tp == int(ref_am.item())
+            exact.append(float((joined == ref_l).float().mean()))
+        one.close()
+        result = {"tokens": tokens, "max_rel_err_h": err_h, "max_rel_err_logits": err_l,
+                  "argmax_equal": same_am, "logits_bit_identical_frac": min(exact),
+                  "tol": TP_CHECK_TOL, "against": "one-GPU decoder, same seeds, on rank 0",
+                  "ok": bool(same_am and err_h <= TP_CHECK_TOL and err_l <= TP_CHECK_TOL)}
+    flag = torch.tensor([0 if rank != 0 else (1 if result["ok"] else 2)], device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        result = {"ok": int(flag.item()) == 1}
+    return result
 
 
 # --------------------------------------------------------------------------
 # CPU: the oracle's AVX2 + OpenMP kernels (port of the reference's absent
 # CPU kernels) timed on the host cores
 # --------------------------------------------------------------------------
+def host_cores():
+    """Host cores this process may run on (torchrun's OMP_NUM_THREADS=1 is
+    not a statement about the machine)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def _cpu_lib():
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import _oracle as O  # builds oracle/liblalb_oracle.so if needed
 
+    O.lib().lalb_cpu_set_threads(host_cores())
     return O
 
 

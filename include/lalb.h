@@ -154,13 +154,18 @@ LALB_API int lalb_lm_head_int8_q8(lalb_ctx *ctx, const int8_t *W, const float *s
  * so the sizes it rejects are the kernel's own: K > 4096 returns
  * LALB_ERR_UNSUPPORTED; K not a multiple of 32, an inverted range, a null or
  * misaligned pointer return LALB_ERR_INVALID.  Errors are reported only
- * through the returned status (there is no context to hold a message).
+ * through the returned status (there is no context to hold a message),
+ * except one that happens on the GPU after the call has returned: if a
+ * bounded wait inside the kernel expires, the logits of the range are
+ * incomplete and *argmax is set to -1 (pass argmax to be able to tell).
  * The first call on a device sets it up (looks up the array's device
- * address, reads the SM count, raises the kernel's shared-memory limit);
- * make that first call before any stream capture.  Every call shares the
- * array and clears the 16 bytes it uses on the caller's stream before the
- * kernel runs; calls that overlap on the GPU (another stream, another host
- * thread on the same device) race on it. */
+ * address and reads the SM count); make that first call before any stream
+ * capture.  Every call makes sure the kernel's shared-memory limit covers
+ * its size, through the same never-lowering registry as the context-based
+ * calls, so the two kinds of call can be mixed in any order.  Every call
+ * shares the array and clears the 16 bytes it uses on the caller's stream
+ * before the kernel runs; calls that overlap on the GPU (another stream,
+ * another host thread on the same device) race on it. */
 LALB_API int lalb_lm_head_int8_range_noalloc(const int8_t *W, const float *sw, int K,
                                              int row_begin, int row_end, const float *x,
                                              float *logits, int32_t *argmax,
@@ -260,6 +265,27 @@ LALB_API int lalb_decoder_set_lm_head_shard(lalb_decoder *dec, int rank, const i
  * before the first step. */
 LALB_API int lalb_decoder_ipc_handle(lalb_decoder *dec, void *handle);
 LALB_API int lalb_decoder_connect(lalb_decoder *dec, const void *handles);
+/* The same connection when every rank lives in one process (one host thread
+ * per GPU, peer access enabled between the GPUs by the caller with
+ * cudaDeviceEnablePeerAccess; or several ranks' decoders on one GPU, whose
+ * steps must then never run at the same time): exchange_buffer gives this
+ * rank's buffer (device address, 128-byte aligned), connect_local takes
+ * every rank's, in rank order. */
+LALB_API int lalb_decoder_exchange_buffer(lalb_decoder *dec, void **buf);
+LALB_API int lalb_decoder_connect_local(lalb_decoder *dec, void *const *bufs);
+/* Bound on every grid-wide and cross-GPU wait of the persistent kernel, in
+ * seconds (default 10; accepted range [1e-4, 600]).  A wait that expires
+ * raises the context's status word (lalb_device_status returns
+ * LALB_STATUS_WAIT_TIMEOUT = 1), the rest of the token runs on whatever
+ * data it has, and its argmax is -1.  Waits for the kernel's own copies are
+ * bounded by four times this limit. */
+LALB_API int lalb_decoder_set_wait_limit(lalb_decoder *dec, double seconds);
+/* After a failed step: clears this rank's exchange buffer (phase counters,
+ * token count, argmax keys).  Every rank resets, with a host barrier between
+ * the ranks before (no step in flight anywhere) and after (no rank steps
+ * before all have reset); then reset the context's status word with
+ * lalb_device_status(ctx, 1). */
+LALB_API int lalb_decoder_reset(lalb_decoder *dec, lalb_stream stream);
 
 /* Execution path of lalb_decoder_step.  AUTO takes the persistent path
  * (the whole token in one cooperative kernel, one CTA per SM) when the
@@ -280,14 +306,18 @@ LALB_API int lalb_decoder_path(const lalb_decoder *dec);
 LALB_API int lalb_decoder_launches_per_step(const lalb_decoder *dec);
 LALB_API int lalb_decoder_destroy(lalb_decoder *dec);
 
-/* ---- prefill: the Q4_K x Q8 matmul for T tokens at once (tcgen05 int8) -----
+/* ---- prefill: the Q4_K x Q8 matmul for T tokens at once (tcgen05) --------
  * Y [T][rows] fp32 = lal_matmul_q4_k (README.md:130,210) applied to each of
- * the T rows of X [T][K] fp32: per-32 activation quantizer, exact int32 sums
- * per 32-weight sub-block (one tcgen05.mma kind::i8 instruction each), the
- * sub-block scale and min corrections applied in fp32 (within 1e-5).  The
- * weights are first unpacked once into `packed` (weight_bytes: int8 quants
- * + per-sub-block scales); `ws` holds the quantized tokens (ws_bytes).
- * K % 256 == 0; packed and ws 256-byte aligned. */
+ * the T rows of X [T][K] fp32, with the same per-32 activation quantizer.
+ * On the tensor cores (tcgen05.mma kind::f16, fp32 accumulators in TMEM):
+ * A = sc*q per weight as fp16 (exact), B = xq*sx per token as two fp16
+ * parts under a per-token power of two, the min terms as bf16 parts; each
+ * 256-weight super-block is scaled by d in the epilogue.  Every output is
+ * within 1e-5 of the exact value relative to the sum of its term
+ * magnitudes.  The weights are first unpacked once into `packed`
+ * (weight_bytes: fp16 sc*q, bf16 min parts and d per super-block); `ws`
+ * holds the prepared tokens (ws_bytes).  K % 256 == 0; packed and ws
+ * 256-byte aligned. */
 LALB_API int lalb_prefill_sizes(int rows, int K, int T, size_t *weight_bytes, size_t *ws_bytes);
 LALB_API int lalb_q4k_prefill_pack(lalb_ctx *ctx, const void *W, int rows, int K, void *packed,
                                    lalb_stream stream);

@@ -258,6 +258,24 @@ class Decoder:
         buf = (ctypes.c_ubyte * len(blob)).from_buffer_copy(blob)
         self.ctx._call("lalb_decoder_connect", self.h, buf)
 
+    def exchange_buffer(self):
+        """Device address of this rank's exchange buffer (int)."""
+        out = ctypes.c_void_p()
+        self.ctx._call("lalb_decoder_exchange_buffer", self.h, ctypes.byref(out))
+        return out.value
+
+    def connect_local(self, bufs):
+        """bufs: every rank's exchange_buffer() address, in rank order (all
+        ranks in this process)."""
+        arr = (ctypes.c_void_p * len(bufs))(*bufs)
+        self.ctx._call("lalb_decoder_connect_local", self.h, arr)
+
+    def set_wait_limit(self, seconds):
+        self.ctx._call("lalb_decoder_set_wait_limit", self.h, ctypes.c_double(seconds))
+
+    def reset(self):
+        self.ctx._call("lalb_decoder_reset", self.h, _stream())
+
     def set_layer(self, layer, wqkv, wo, wgu, wdown):
         lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())
         self.ctx._call("lalb_decoder_set_layer", self.h, layer, ctypes.byref(lw))

@@ -58,6 +58,10 @@ SIGNATURES = {
     "lalb_decoder_set_lm_head_shard": (c_int, [P, c_int, P, P]),
     "lalb_decoder_ipc_handle": (c_int, [P, P]),
     "lalb_decoder_connect": (c_int, [P, P]),
+    "lalb_decoder_exchange_buffer": (c_int, [P, ctypes.POINTER(P)]),
+    "lalb_decoder_connect_local": (c_int, [P, P]),
+    "lalb_decoder_set_wait_limit": (c_int, [P, ctypes.c_double]),
+    "lalb_decoder_reset": (c_int, [P, P]),
     "lalb_decoder_set_path": (c_int, [P, c_int]),
     "lalb_prefill_sizes": (c_int, [c_int, c_int, c_int, ctypes.POINTER(ctypes.c_size_t),
                                    ctypes.POINTER(ctypes.c_size_t)]),

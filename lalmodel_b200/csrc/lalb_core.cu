@@ -35,18 +35,26 @@ int lalb_cuda_fail(lalb_ctx *ctx, cudaError_t e, const char *what) {
                      cudaGetErrorName(e));
 }
 
-// Raises a kernel's dynamic shared-memory limit once per (device, kernel);
-// later launches (including those recorded during stream capture) skip the
-// attribute call.
-int lalb_set_smem_attr(lalb_ctx *ctx, const void *fn, int bytes) {
+// Raises a kernel's dynamic shared-memory limit, per (device, kernel), to the
+// largest size any caller has asked for; it is never lowered, so a launch
+// sized for an earlier, larger request stays valid.  Every path that sets
+// the attribute goes through this registry (the context-based launchers and
+// the allocation-free LM head alike).  Later launches with a size already
+// covered (including those recorded during stream capture) skip the call.
+cudaError_t lalb_raise_smem_attr(int device, const void *fn, int bytes) {
     static std::mutex mu;
     static std::map<std::pair<int, const void *>, int> done;
     std::lock_guard<std::mutex> lock(mu);
-    auto key = std::make_pair(ctx->device, fn);
+    auto key = std::make_pair(device, fn);
     auto it = done.find(key);
-    if (it != done.end() && it->second >= bytes) return LALB_OK;
-    LALB_CUDA_TRY(ctx, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    done[key] = bytes;
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done[key] = bytes;
+    return e;
+}
+
+int lalb_set_smem_attr(lalb_ctx *ctx, const void *fn, int bytes) {
+    LALB_CUDA_TRY(ctx, lalb_raise_smem_attr(ctx->device, fn, bytes));
     return LALB_OK;
 }
 

@@ -41,6 +41,7 @@ struct lalb_decoder {
     bool xb_opened[kPersistMaxRanks] = {};     // mapped through CUDA IPC
     bool connected = false;
     bool layers_dirty = true;
+    unsigned long long wait_ns = 10ull * 1000 * 1000 * 1000;   // bound on a grid / cross-GPU wait
     bool persist_fits = false;
     int path = LALB_DECODE_AUTO;
     bool use_graph = true;
@@ -182,6 +183,7 @@ int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, fl
     a.logits = logits;
     a.argmax = argmax;
     a.status = &ctx->scratch->status;
+    a.wait_ns = d->wait_ns;
     a.trace = trace;
     if (int st = lalb_launch_persist(ctx, a, s)) return st;
     if (h_out) {
@@ -384,6 +386,51 @@ extern "C" int lalb_decoder_connect(lalb_decoder *d, const void *handles) {
     }
     d->connected = true;
     drop_graphs(d);
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_exchange_buffer(lalb_decoder *d, void **buf) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!buf || d->ranks_here != 1)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_exchange_buffer: one rank per decoder");
+    *buf = d->xb_own;
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_connect_local(lalb_decoder *d, void *const *bufs) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!bufs || d->ranks_here != 1)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_connect_local: one rank per decoder");
+    if (d->connected) return LALB_OK;
+    for (int j = 0; j < d->n_rank; ++j) {
+        if (!bufs[j] || ((uintptr_t)bufs[j] & 127u))
+            return lalb_fail(d->ctx, LALB_ERR_INVALID,
+                             "decoder_connect_local: exchange buffer %d null or misaligned", j);
+        if (j == d->rank0 && bufs[j] != d->xb_own)
+            return lalb_fail(d->ctx, LALB_ERR_INVALID,
+                             "decoder_connect_local: entry %d is not this rank's buffer", j);
+    }
+    for (int j = 0; j < d->n_rank; ++j) d->xb[j] = static_cast<unsigned char *>(bufs[j]);
+    d->connected = true;
+    drop_graphs(d);
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_set_wait_limit(lalb_decoder *d, double seconds) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!(seconds >= 1e-4 && seconds <= 600.0))
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_wait_limit: %g s outside [1e-4, 600]",
+                         seconds);
+    d->wait_ns = (unsigned long long)(seconds * 1e9);
+    drop_graphs(d);   // the limit is a kernel argument baked into captured graphs
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_reset(lalb_decoder *d, lalb_stream stream) {
+    if (!d) return LALB_ERR_INVALID;
+    LALB_CUDA_TRY(d->ctx, cudaSetDevice(d->ctx->device));
+    LALB_CUDA_TRY(d->ctx, cudaMemsetAsync(d->xb_own, 0, d->xb_bytes * d->ranks_here,
+                                          (cudaStream_t)stream));
     return LALB_OK;
 }
 

@@ -64,7 +64,6 @@ constexpr int kSlots = LALB_PERSIST_SLOTS;
 constexpr uint32_t kSlotBytes = LALB_PERSIST_SLOT_BYTES;
 constexpr int kMaxTiles = 8;                 // gate/up 64-row tiles per CTA
 constexpr int kMaxNS = kPersistMaxFfn / 32;
-constexpr unsigned long long kWaitLimitNs = 10ull * 1000 * 1000 * 1000;   // 10 s
 constexpr uint32_t kWaitIterCap = 1u << 28;   // safety net beside the time limit
 constexpr int kTraceFields = 8;
 constexpr int kPrefetchChunks = LALB_PERSIST_PREFETCH;   // L2 prefetch distance beyond the ring
@@ -226,10 +225,10 @@ __device__ __forceinline__ void cons_bar() {
 // their stores into the other ranks' buffers.  A CTA then waits until its
 // rank's lbar[ph] has all local CTAs and rbar[ph] all other ranks.  Both
 // counters grow across tokens (targets from the token count `seq`; the
-// comparisons survive wrap-around).  Gives up after kWaitLimitNs, or as soon
-// as this rank's status word is raised (then every later wait of the token
-// is skipped: a failed token ends in seconds, not one time-out per wait).
-// Returns false on failure.
+// comparisons survive wrap-around).  Gives up after a.wait_ns, or as soon
+// as this rank's status word is raised (then every later grid wait of the
+// token gives up at once: a failed token ends after one time-out, not one
+// per wait).  Returns false on failure.
 // Phases whose outputs go to other ranks (gate/up, down): their barrier waits
 // for every rank; after qkv and o (computed whole on every rank) a rank only
 // waits for its own CTAs.
@@ -290,7 +289,7 @@ __device__ __forceinline__ bool grid_wait(const PersistArgs &a, const XView &own
         if ((k & 255) == 255) {
             const unsigned long long t = global_ns();
             if (t0 == 0) t0 = t;
-            else if (t - t0 > kWaitLimitNs) k = kWaitIterCap;
+            else if (t - t0 > a.wait_ns) k = kWaitIterCap;
         }
         if (k >= kWaitIterCap) {
             atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
@@ -328,7 +327,7 @@ __device__ __forceinline__ bool keys_arrive_wait(const PersistArgs &a, const XVi
         if ((k & 255) == 255) {
             const unsigned long long t = global_ns();
             if (t0 == 0) t0 = t;
-            else if (t - t0 > kWaitLimitNs) k = kWaitIterCap;
+            else if (t - t0 > a.wait_ns) k = kWaitIterCap;
         }
         if (k >= kWaitIterCap) {
             atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
@@ -338,15 +337,19 @@ __device__ __forceinline__ bool keys_arrive_wait(const PersistArgs &a, const XVi
     }
 }
 
-// Bounded mbarrier wait that is skipped once this thread has seen a failure.
-// Adds the number of polls to `polls`.
-// The limit is time-based (kWaitLimitNs on the global timer, with an
-// iteration cap as well): every wait of this kernel may depend, through the
-// grid barriers, on other GPUs whose launches can lag by a good fraction of
-// a second.
-__device__ __forceinline__ void pwait(uint64_t *bar, uint32_t parity, unsigned int *status,
+// Bounded mbarrier wait that is skipped once this thread has seen an
+// mbarrier wait expire.  Adds the number of polls to `polls`.
+// The limit is time-based (4 x a.wait_ns on the global timer, with an
+// iteration cap as well): a producer waiting for a free slot legitimately
+// waits as long as its consumers wait at a grid barrier (up to a.wait_ns,
+// on other GPUs whose launches can lag), so its own limit is longer.  A
+// grid barrier that gave up does NOT make the CTA skip mbarrier waits: the
+// producers keep issuing and the consumers keep waiting for every copy, so
+// no copy is ever in flight when a slot is refilled or the CTA exits.
+__device__ __forceinline__ void pwait(const PersistArgs &a, uint64_t *bar, uint32_t parity,
                                       bool &dead, unsigned long long &polls) {
     if (dead) return;
+    const unsigned long long limit = 4ull * a.wait_ns;
     unsigned long long t0 = 0;
     for (uint32_t i = 0; i < kWaitIterCap; ++i) {
         ++polls;
@@ -354,10 +357,10 @@ __device__ __forceinline__ void pwait(uint64_t *bar, uint32_t parity, unsigned i
         if ((i & 63) == 63) {
             const unsigned long long t = global_ns();
             if (t0 == 0) t0 = t;
-            else if (t - t0 > kWaitLimitNs) break;
+            else if (t - t0 > limit) break;
         }
     }
-    if (status) atomicOr(status, LALB_STATUS_WAIT_TIMEOUT);
+    atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
     dead = true;
 }
 
@@ -447,8 +450,8 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
         const int slot = g % kSlots;
         const uint32_t use = g / kSlots;
         const unsigned long long tw0 = cs.tracing ? global_ns() : 0;
-        if (use > 0) pwait(&cs.empty[slot], (use - 1) & 1u, a.status, cs.dead, cs.polls);
-        pwait(&cs.full[slot], use & 1u, a.status, cs.dead, cs.polls);
+        if (use > 0) pwait(a, &cs.empty[slot], (use - 1) & 1u, cs.dead, cs.polls);
+        pwait(a, &cs.full[slot], use & 1u, cs.dead, cs.polls);
         const unsigned long long tw1 = cs.tracing ? global_ns() : 0;
         cs.wait_ns += tw1 - tw0;
         const uint8_t *sp = cs.slot_s + (size_t)slot * kSlotBytes;
@@ -666,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     if (g % kNP != (uint32_t)warp) continue;
                     const int slot = g % kSlots;
                     const uint32_t use = g / kSlots;
-                    if (use > 0) pwait(&empty[slot], (use - 1) & 1u, a.status, dead, polls);
+                    if (use > 0) pwait(a, &empty[slot], (use - 1) & 1u, dead, polls);
                     if (dead) break;   // stop issuing: consumers time out once and skip
                     const int rs = d.r0 + j * d.R;
                     const int nr = min(d.R, d.r1 - rs);
@@ -690,7 +693,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     const int ci = warp - kNP;        // consumer index 0..kNC-1
     const int ct = tid - 32 * kNP;    // consumer thread 0..kConsThreads-1
     uint32_t g_base = 0;
-    int *abort_s = tcnt_s + kMaxTiles;   // CTA-wide: a grid barrier failed
     Cons cs;
     cs.full = full;
     cs.empty = empty;
@@ -729,13 +731,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 }
                 grid_arrive(a, own, w.rank, p - 1, seq);
                 d = phase_desc(a, p, w);   // while the arrivals propagate
-                *abort_s = !grid_wait(a, own, p - 1, seq);
+                // a grid barrier that gives up leaves the rest of the token
+                // to run on whatever data it has: later grid waits give up
+                // at once (the status word is raised), mbarrier waits stay
+                grid_wait(a, own, p - 1, seq);
                 if (tr) tr[1] = global_ns();
             } else {
                 d = phase_desc(a, p, w);
             }
             cons_bar();
-            if (*abort_s) cs.dead = true;
         } else {
             d = phase_desc(a, p, w);
         }

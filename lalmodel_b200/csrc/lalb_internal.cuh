@@ -35,7 +35,10 @@ struct lalb_ctx {
 
 // Records an error message on the context and returns the status code.
 int lalb_fail(lalb_ctx *ctx, int status, const char *fmt, ...);
-// Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (device, kernel).
+// Raises cudaFuncAttributeMaxDynamicSharedMemorySize of a kernel on `device`
+// (the current device) to at least `bytes`; never lowers it.
+cudaError_t lalb_raise_smem_attr(int device, const void *fn, int bytes);
+// The same for the context's device, with the error recorded on the context.
 int lalb_set_smem_attr(lalb_ctx *ctx, const void *fn, int bytes);
 // Converts a CUDA error into LALB_ERR_CUDA with the call site recorded.
 int lalb_cuda_fail(lalb_ctx *ctx, cudaError_t e, const char *what);

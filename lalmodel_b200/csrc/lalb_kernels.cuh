@@ -60,6 +60,7 @@ struct Q8HeadArgs {
     unsigned int *ticket;      // CTA ticket counter (4 bytes)
     int nstages;
     unsigned int *status;
+    int fail_argmax;           // nonzero: publish argmax = -1 when the status word is raised
 };
 
 int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &a, int in, int epi,
@@ -94,6 +95,7 @@ struct PersistArgs {
     float *logits;                      // nullable: [vocab] (each rank writes its rows)
     int32_t *argmax;                    // nullable
     unsigned int *status;
+    unsigned long long wait_ns;         // bound on a grid or cross-GPU wait (global timer)
     // nullable: per CTA and phase, timeline and counters (lalb_decoder_trace_step)
     unsigned long long *trace;
 };

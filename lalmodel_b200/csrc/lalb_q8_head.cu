@@ -230,7 +230,14 @@ __global__ void __launch_bounds__(kThreads, 1) q8_head_kernel(const Q8HeadArgs a
         const unsigned int t = atomicAdd(a.ticket, 1u);
         if (t == gridDim.x - 1) {
             const unsigned long long key = atomicExch(a.best, 0ull);
-            *a.argmax = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+            int32_t row = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+            if (a.fail_argmax) {
+                // every CTA raised the status word (if it failed) before its
+                // ticket: a row over a partial range is never published
+                __threadfence();
+                if (*(volatile unsigned int *)a.status) row = -1;
+            }
+            *a.argmax = row;
             atomicExch(a.ticket, 0u);
         }
     }
@@ -363,7 +370,7 @@ std::mutex g_noalloc_mu;
 
 // Once per device, with that device current: the array's device address (the
 // host-side name g_noalloc_scratch is only a stand-in and must never reach a
-// kernel), the SM count, and the kernel's shared-memory limit.
+// kernel), the SM count and the shared-memory budget of one CTA.
 int noalloc_setup(int dev, NoAllocDevice **out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     NoAllocDevice &d = g_noalloc_dev[dev];
@@ -381,11 +388,6 @@ int noalloc_setup(int dev, NoAllocDevice **out) {
             return LALB_ERR_CUDA;
         }
         const int budget = optin - 1024;
-        if (cudaFuncSetAttribute((const void *)q8_head_kernel<kInF32>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, budget) != cudaSuccess) {
-            cudaGetLastError();
-            return LALB_ERR_CUDA;
-        }
         d.scratch = static_cast<unsigned char *>(ptr);
         d.sm_count = sm;
         d.smem_budget = budget;
@@ -425,6 +427,14 @@ extern "C" int lalb_lm_head_int8_range_noalloc(const int8_t *W, const float *sw,
     if (nst > 8) nst = 8;
     if (nst < 2) return LALB_ERR_UNSUPPORTED;
     const Layout L = make_layout(K, nst);
+    // The kernel's shared-memory limit goes through the same raise-only
+    // registry as the context-based launches, so a later regular call with a
+    // smaller K cannot lower it below what this launch needs.
+    if (lalb_raise_smem_attr(dev, (const void *)q8_head_kernel<kInF32>, (int)L.total) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return LALB_ERR_CUDA;
+    }
 
     // the array keeps the previous call's contents: clear the key, ticket and
     // status word that this call's reduction starts from
@@ -443,10 +453,19 @@ extern "C" int lalb_lm_head_int8_range_noalloc(const int8_t *W, const float *sw,
     a.best = reinterpret_cast<unsigned long long *>(nd->scratch);
     a.ticket = reinterpret_cast<unsigned int *>(nd->scratch + 8);
     a.status = reinterpret_cast<unsigned int *>(nd->scratch + 12);
+    a.fail_argmax = 1;   // a bounded wait that expired publishes argmax = -1
     int grid = nd->sm_count;
     const int units = (nrows + kRps - 1) / kRps;
     if (grid > units) grid = units;
-    q8_head_kernel<kInF32><<<grid, kThreads, L.total, s>>>(a);
-    if (cudaGetLastError() != cudaSuccess) return LALB_ERR_CUDA;
+    // the launch's own result (cudaGetLastError would also report, and
+    // clear, an earlier error of unrelated code)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = s;
+    void *params[] = {&a};
+    if (cudaLaunchKernelExC(&cfg, (const void *)q8_head_kernel<kInF32>, params) != cudaSuccess)
+        return LALB_ERR_CUDA;
     return LALB_OK;
 }

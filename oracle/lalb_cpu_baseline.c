@@ -20,6 +20,13 @@
 
 int lalb_cpu_threads(void) { return omp_get_max_threads(); }
 
+/* The OpenMP team size of the baseline's parallel loops.  A launcher such as
+ * torchrun exports OMP_NUM_THREADS=1 to every rank; the timed CPU baseline
+ * sets its thread count explicitly instead of inheriting that. */
+void lalb_cpu_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+
 void lalb_cpu_quantize_act(const float *x, int M, int K, int8_t *xq, float *sx,
                            int32_t *sumq) {
     const int nblk = K / 32;

@@ -124,6 +124,7 @@ void lalb_o_binlayer_forward(const float *W, const float *bias,
 
 /* --- AVX2 + OpenMP CPU baseline (same integer results as the scalar code) - */
 int  lalb_cpu_threads(void);
+void lalb_cpu_set_threads(int n);
 void lalb_cpu_quantize_act(const float *x, int M, int K, int8_t *xq, float *sx,
                            int32_t *sumq);
 void lalb_cpu_q4k_gemv(const uint8_t *W, int rows, int K, const int8_t *xq,

@@ -35,6 +35,7 @@ _SIG = {
     "lalb_o_binlayer_forward": (None, [P, P, P, c_int, c_int, P, c_int, P, c_int, c_int,
                                        c_float, P]),
     "lalb_cpu_threads": (c_int, []),
+    "lalb_cpu_set_threads": (None, [c_int]),
     "lalb_cpu_quantize_act": (None, [P, c_int, c_int, P, P, P]),
     "lalb_cpu_q4k_gemv": (None, [P, c_int, c_int, P, P, P, P]),
     "lalb_cpu_q8_lmhead": (c_int, [P, P, c_int, c_int, P, P, P]),

@@ -67,6 +67,60 @@ def test_tp_all_ranks_on_one_gpu_match_oracle(ctx, n_rank, ci):
     dec.close()
 
 
+def test_tp_wait_runs_out_when_a_peer_never_steps(ctx):
+    """A bounded cross-GPU wait made to run out on purpose, with no fault:
+    rank 0 of a two-rank decoder steps alone (rank 1's decoder exists on the
+    same GPU, its exchange buffer connected, but it never launches), with a
+    50 ms wait limit.  The token must end by itself within seconds, report
+    the expired wait through the status word and an argmax of -1, and leave
+    the context usable."""
+    import time
+
+    cfg = CFGS[0]
+    layers, dl, lq, ls = make_decoder_weights(cfg, seed=2100, n_vocab=cfg["vocab"])
+    lqd, lsd = dev(lq), dev(ls)
+    a = lb.Decoder(ctx, **cfg, n_rank=2, rank=0)
+    b = lb.Decoder(ctx, **cfg, n_rank=2, rank=1)   # connected, never steps
+    load_shards(a, 0, cfg, dl, lqd, lsd)
+    a.connect_local([a.exchange_buffer(), b.exchange_buffer()])
+    a.set_wait_limit(0.05)
+    h_in = dev(O.normal(cfg["hidden"], seed=2101))
+    am = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    assert ctx.device_status() == 0
+    t0 = time.perf_counter()
+    with torch.cuda.stream(s):
+        a.step(h_in, None, None, am)
+    s.synchronize()
+    dt = time.perf_counter() - t0
+    assert dt < 10.0, dt
+    assert ctx.device_status() == 1          # LALB_STATUS_WAIT_TIMEOUT
+    assert int(am.item()) == -1
+    assert ctx.device_status(reset=True) == 1
+    assert ctx.device_status() == 0
+    with torch.cuda.stream(s):
+        a.reset()
+        b.reset()
+    s.synchronize()
+    a.close()
+    b.close()
+    # the context still computes: a one-GPU decoder on the same weights
+    one = lb.Decoder(ctx, **cfg)
+    for l, w in enumerate(dl):
+        one.set_layer(l, w["wqkv"], w["wo"], w["wgu"], w["wdown"])
+    one.set_lm_head(lqd, lsd)
+    h = O.normal(cfg["hidden"], seed=2102)
+    _, ref_logits, ref_am = O.decode_chain(layers, lq, ls, h, cfg)
+    logits = torch.empty(cfg["vocab"], dtype=torch.float32, device="cuda")
+    with torch.cuda.stream(s):
+        one.step(dev(h), None, logits, am)
+    s.synchronize()
+    assert int(am.item()) == ref_am
+    assert O.normwise_rel_err(host(logits), ref_logits) < 1e-5
+    assert ctx.device_status() == 0
+    one.close()
+
+
 def test_tp_rejects_chain_path_and_unheld_ranks(ctx):
     cfg = CFGS[0]
     dec = lb.Decoder(ctx, **cfg, n_rank=2, rank=1)

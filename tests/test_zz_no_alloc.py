@@ -55,6 +55,42 @@ def test_noalloc_lm_head_matches_regular_entry_point_twice(ctx):
         assert int(am.item()) == oracle_am
 
 
+def test_noalloc_and_regular_calls_mix_in_any_order(ctx):
+    """Allocation-free call at a large K, then a regular call at a small K,
+    then the allocation-free call again: the regular call must not shrink the
+    kernel's shared-memory limit under the next allocation-free launch.  (In
+    a fresh process the regular call below is the kernel's first regular
+    launch, the order in which that could happen.)"""
+    rows, K, Ks = 5000, 3584, 512
+    q, s = O.q8_quantize_rows(O.normal(rows * K, seed=911, sigma=0.02).reshape(rows, K))
+    qs, ss = O.q8_quantize_rows(O.normal(rows * Ks, seed=912, sigma=0.02).reshape(rows, Ks))
+    qd, sd, qsd, ssd = dev(q), dev(s), dev(qs), dev(ss)
+    x, xs = O.normal(K, seed=913), O.normal(Ks, seed=914)
+    xd, xsd = dev(x), dev(xs)
+    xq, sx, _ = O.quantize_act(x)
+    oracle_logits, _, oracle_am = O.q8_lmhead(q, s, xq, sx, 0, rows)
+    xqs, sxs, _ = O.quantize_act(xs)
+    _, _, oracle_small = O.q8_lmhead(qs, ss, xqs, sxs, 0, rows)
+    got = []
+    for _ in range(2):
+        logits = torch.empty(rows, dtype=torch.float32, device="cuda")
+        am = torch.full((1,), -2, dtype=torch.int32, device="cuda")
+        assert noalloc(qd, sd, K, 0, rows, xd, logits, am) == 0
+        torch.cuda.synchronize()
+        assert O.normwise_rel_err(logits.cpu().numpy(), oracle_logits) < TOL
+        assert int(am.item()) == oracle_am
+        got.append(logits.cpu().numpy())
+        # the regular entry point at a small K in between
+        _, small_am = ctx.lm_head_int8_range(qsd, ssd, xsd, 0, rows)
+        torch.cuda.synchronize()
+        assert int(small_am.item()) == oracle_small
+    ref_logits, ref_am = ctx.lm_head_int8_range(qd, sd, xd, 0, rows)
+    torch.cuda.synchronize()
+    for g in got:
+        assert np.array_equal(g.view(np.uint32), ref_logits.cpu().numpy().view(np.uint32))
+    assert int(ref_am.item()) == oracle_am
+
+
 def test_noalloc_lm_head_rejects_what_the_kernel_cannot_do(ctx):
     q = torch.zeros((4, 4128), dtype=torch.int8, device="cuda")
     s = torch.ones(4, dtype=torch.float32, device="cuda")
