@@ -45,7 +45,7 @@ extern "C" {
 #define LALB_API
 #endif
 
-#define LALB_ABI_VERSION 1
+#define LALB_ABI_VERSION 2
 #define LALB_QK_K 256
 #define LALB_QB 32
 #define LALB_Q4K_BLOCK_BYTES 144
@@ -173,17 +173,19 @@ LALB_API int lalb_lm_head_int8_range_noalloc(const int8_t *W, const float *sw, i
 
 /* ---- Qwen2.5-shape decode matmul set (one token) -----------------------
  * Per layer, with h the fp32 residual stream [hidden]:
- *   qkv  = Wqkv . Q8(rmsnorm(h))              rows q_rows + 2*kv_rows
+ *   qkv  = Wqkv . Q8(rmsnorm(h, attn_norm))    rows q_rows + 2*kv_rows
  *   h    = h + Wo . Q8(qkv[0:q_rows])          (the attention output is
- *                                              out of scope; q stands in)
- *   a    = silu(gate) * up, gate/up = Wgu . Q8(rmsnorm(h))
+ *                                              out of scope: q stands in)
+ *   a    = silu(gate) * up, gate/up = Wgu . Q8(rmsnorm(h, ffn_norm))
  *   h    = h + Wdown . Q8(a)
- * then logits = LMhead . Q8(rmsnorm(h)) and argmax.  rmsnorm uses unit
- * weights, eps 1e-6, its scale computed in double; silu(g)*u is evaluated
- * in double and rounded once.  Wgu interleaves gate and up in 32-row
- * tiles: rows [64t, 64t+32) are gate rows [32t, 32t+32), rows
- * [64t+32, 64t+64) the up rows of the same range.  Weights are
- * caller-owned device buffers. */
+ * then logits = LMhead . Q8(rmsnorm(h, output norm)) and argmax.
+ * rmsnorm is rms_norm (runtime/lal_runtime.c:82-87): out = (x * s) * w with
+ * s = 1/sqrt(mean(x^2) + rms_eps), s computed in double and rounded to
+ * float once; a NULL weight vector means unit weights.  silu(g)*u is
+ * evaluated in double and rounded once.  Wgu interleaves gate and up in
+ * 32-row tiles: rows [64t, 64t+32) are gate rows [32t, 32t+32), rows
+ * [64t+32, 64t+64) the up rows of the same range.  Weights are caller-owned
+ * device buffers. */
 typedef struct {
     int n_layer;
     int hidden;     /* K of qkv / gate-up, rows of o / down */
@@ -191,13 +193,16 @@ typedef struct {
     int kv_rows;    /* n_kv_head * head_dim */
     int ffn;        /* intermediate size */
     int vocab;      /* LM-head rows */
+    float rms_eps;  /* RMSNorm epsilon; 0 selects 1e-5 (the reference's rms_norm) */
 } lalb_decoder_cfg;
 
 typedef struct {
-    const void *wqkv;   /* Q4_K [q_rows + 2*kv_rows][hidden] */
-    const void *wo;     /* Q4_K [hidden][q_rows] */
-    const void *wgu;    /* Q4_K [2*ffn][hidden], 32-row gate/up tiles */
-    const void *wdown;  /* Q4_K [hidden][ffn] */
+    const void *wqkv;        /* Q4_K [q_rows + 2*kv_rows][hidden] */
+    const void *wo;          /* Q4_K [hidden][q_rows] */
+    const void *wgu;         /* Q4_K [2*ffn][hidden], 32-row gate/up tiles */
+    const void *wdown;       /* Q4_K [hidden][ffn] */
+    const float *attn_norm;  /* [hidden] RMSNorm weights before qkv; NULL: unit */
+    const float *ffn_norm;   /* [hidden] RMSNorm weights before gate/up; NULL: unit */
 } lalb_layer_weights;
 
 typedef struct lalb_decoder lalb_decoder;
@@ -208,6 +213,9 @@ LALB_API int lalb_decoder_set_layer(lalb_decoder *dec, int layer,
                                     const lalb_layer_weights *w);
 LALB_API int lalb_decoder_set_lm_head(lalb_decoder *dec, const int8_t *w,
                                       const float *sw);
+/* RMSNorm weights [hidden] applied before the LM head (NULL: unit, the
+ * default).  Every rank of a tensor-parallel decoder holds them whole. */
+LALB_API int lalb_decoder_set_output_norm(lalb_decoder *dec, const float *w);
 /* One token on device buffers: h_in [hidden] (read only), h_out [hidden]
  * (nullable: final residual stream), logits [vocab] (nullable), argmax
  * (device int32, nullable).  On a non-default stream the token is captured

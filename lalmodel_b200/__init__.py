@@ -209,12 +209,13 @@ def shard_rows(t, r0, r1):
 class Decoder:
     """The Qwen2.5-shape decode matmul set (include/lalb.h, lalb_decoder_*)."""
 
-    def __init__(self, ctx, n_layer, hidden, q_rows, kv_rows, ffn, vocab, n_rank=1, rank=0):
+    def __init__(self, ctx, n_layer, hidden, q_rows, kv_rows, ffn, vocab, n_rank=1, rank=0,
+                 rms_eps=0.0):
         """n_rank > 1: tensor-parallel decoder holding rank `rank` (one GPU
         per rank, peers connected with ipc_handle()/connect()), or every rank
-        on this GPU with rank=-1."""
+        on this GPU with rank=-1.  rms_eps 0 selects 1e-5."""
         self.ctx = ctx
-        self.cfg = DecoderCfg(n_layer, hidden, q_rows, kv_rows, ffn, vocab)
+        self.cfg = DecoderCfg(n_layer, hidden, q_rows, kv_rows, ffn, vocab, rms_eps)
         self.n_rank, self.rank = n_rank, rank
         # the library keeps only device pointers: hold the weight tensors (a
         # shard built on the fly would otherwise be freed while still in use)
@@ -236,10 +237,12 @@ class Decoder:
             raise LalbError("lalb_tp_rows", st)
         return r0.value, r1.value
 
-    def set_layer_shard(self, rank, layer, wqkv, wo, wgu, wdown):
-        lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())
+    def set_layer_shard(self, rank, layer, wqkv, wo, wgu, wdown, attn_norm=None, ffn_norm=None):
+        """attn_norm / ffn_norm: RMSNorm weights [hidden] (None: unit)."""
+        lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr(),
+                          _p(attn_norm), _p(ffn_norm))
         self.ctx._call("lalb_decoder_set_layer_shard", self.h, rank, layer, ctypes.byref(lw))
-        self._keep[("layer", rank, layer)] = (wqkv, wo, wgu, wdown)
+        self._keep[("layer", rank, layer)] = (wqkv, wo, wgu, wdown, attn_norm, ffn_norm)
 
     def set_lm_head_shard(self, rank, w, sw):
         self.ctx._call("lalb_decoder_set_lm_head_shard", self.h, rank, _p(w), _p(sw))
@@ -276,10 +279,16 @@ class Decoder:
     def reset(self):
         self.ctx._call("lalb_decoder_reset", self.h, _stream())
 
-    def set_layer(self, layer, wqkv, wo, wgu, wdown):
-        lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr())
+    def set_layer(self, layer, wqkv, wo, wgu, wdown, attn_norm=None, ffn_norm=None):
+        lw = LayerWeights(wqkv.data_ptr(), wo.data_ptr(), wgu.data_ptr(), wdown.data_ptr(),
+                          _p(attn_norm), _p(ffn_norm))
         self.ctx._call("lalb_decoder_set_layer", self.h, layer, ctypes.byref(lw))
-        self._keep[("layer", 0, layer)] = (wqkv, wo, wgu, wdown)
+        self._keep[("layer", 0, layer)] = (wqkv, wo, wgu, wdown, attn_norm, ffn_norm)
+
+    def set_output_norm(self, w):
+        """RMSNorm weights [hidden] before the LM head (None: unit)."""
+        self.ctx._call("lalb_decoder_set_output_norm", self.h, _p(w))
+        self._keep[("out_norm",)] = w
 
     def set_lm_head(self, w, sw):
         self.ctx._call("lalb_decoder_set_lm_head", self.h, _p(w), _p(sw))

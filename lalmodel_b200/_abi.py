@@ -20,11 +20,12 @@ STATUS = {0: "LALB_OK", -1: "LALB_ERR_INVALID", -2: "LALB_ERR_CUDA", -3: "LALB_E
 
 class DecoderCfg(ctypes.Structure):
     _fields_ = [("n_layer", c_int), ("hidden", c_int), ("q_rows", c_int),
-                ("kv_rows", c_int), ("ffn", c_int), ("vocab", c_int)]
+                ("kv_rows", c_int), ("ffn", c_int), ("vocab", c_int), ("rms_eps", c_float)]
 
 
 class LayerWeights(ctypes.Structure):
-    _fields_ = [("wqkv", P), ("wo", P), ("wgu", P), ("wdown", P)]
+    _fields_ = [("wqkv", P), ("wo", P), ("wgu", P), ("wdown", P), ("attn_norm", P),
+                ("ffn_norm", P)]
 
 
 # name -> (restype, argtypes); mirrors include/lalb.h one to one
@@ -48,6 +49,7 @@ SIGNATURES = {
     "lalb_decoder_create": (c_int, [P, ctypes.POINTER(DecoderCfg), ctypes.POINTER(P)]),
     "lalb_decoder_set_layer": (c_int, [P, c_int, ctypes.POINTER(LayerWeights)]),
     "lalb_decoder_set_lm_head": (c_int, [P, P, P]),
+    "lalb_decoder_set_output_norm": (c_int, [P, P]),
     "lalb_decoder_step": (c_int, [P, P, P, P, P, P]),
     "lalb_decoder_step_host": (c_int, [P, P, P, P]),
     "lalb_decoder_profile_step": (c_int, [P, P, P, P]),

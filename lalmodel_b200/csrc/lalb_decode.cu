@@ -24,6 +24,7 @@ struct lalb_decoder {
     std::vector<std::vector<lalb_layer_weights>> layers;   // [ranks_here][n_layer] row shards
     std::vector<const int8_t *> lm_w;                     // [ranks_here]
     std::vector<const float *> lm_s;
+    const float *out_norm = nullptr;   // RMSNorm weights before the LM head (nullable)
     // activations of the per-phase kernel chain (device, owned; one rank only)
     float *qkv = nullptr;     // [q_rows + 2*kv_rows]
     float *h_res = nullptr;   // [hidden] residual stream
@@ -76,6 +77,8 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
             a.rows = qkv_rows;
             a.K = c.hidden;
             a.x = resid;
+            a.gamma = w.attn_norm;
+            a.eps = c.rms_eps;
             a.y = d->qkv;
             a.unit = 1;
             LALB_CUDA_TRY(ctx, mark());
@@ -100,6 +103,8 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
             a.rows = 2 * c.ffn;
             a.K = c.hidden;
             a.x = d->h_res;
+            a.gamma = w.ffn_norm;
+            a.eps = c.rms_eps;
             a.aq = d->aq;
             a.asx = d->asx;
             a.asumq = d->asumq;
@@ -129,6 +134,8 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
     a.row_begin = 0;
     a.row_end = c.vocab;
     a.x = c.n_layer > 0 ? d->h_res : h_in;
+    a.gamma = d->out_norm;
+    a.eps = c.rms_eps;
     a.logits = logits;
     a.argmax = argmax;
     LALB_CUDA_TRY(ctx, mark());
@@ -180,6 +187,8 @@ int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, fl
     }
     for (int j = 0; j < d->n_rank; ++j) a.xb[j] = d->xb[j];
     a.h_in = h_in;
+    a.rms_eps = c.rms_eps;
+    a.out_norm = d->out_norm;
     a.logits = logits;
     a.argmax = argmax;
     a.status = &ctx->scratch->status;
@@ -246,6 +255,9 @@ extern "C" int lalb_decoder_create_tp(lalb_ctx *ctx, const lalb_decoder_cfg *cfg
                          "decoder_create: hidden/q_rows/ffn must be multiples of 256, hidden <= 4096");
     if (c.vocab >= (1 << 24) || 2LL * c.ffn >= (1 << 24) || c.q_rows + 2LL * c.kv_rows >= (1 << 24))
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: matrices must have < 2^24 rows");
+    if (!(c.rms_eps >= 0.0f) || c.rms_eps > 1.0f)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: rms_eps %g outside [0, 1]",
+                         (double)c.rms_eps);
     if (n_rank < 1 || n_rank > kPersistMaxRanks || rank < -1 || rank >= n_rank)
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: rank %d of %d", rank, n_rank);
     LALB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
@@ -253,11 +265,11 @@ extern "C" int lalb_decoder_create_tp(lalb_ctx *ctx, const lalb_decoder_cfg *cfg
     if (!d) return LALB_ERR_NOMEM;
     d->ctx = ctx;
     d->cfg = c;
+    if (d->cfg.rms_eps == 0.0f) d->cfg.rms_eps = 1e-5f;   // rms_norm's constant (lal_runtime.c:84)
     d->n_rank = n_rank;
     d->rank0 = rank < 0 ? 0 : rank;
     d->ranks_here = rank < 0 ? n_rank : 1;
-    d->layers.assign(d->ranks_here, std::vector<lalb_layer_weights>(
-                                        c.n_layer, lalb_layer_weights{nullptr, nullptr, nullptr, nullptr}));
+    d->layers.assign(d->ranks_here, std::vector<lalb_layer_weights>(c.n_layer, lalb_layer_weights{}));
     d->lm_w.assign(d->ranks_here, nullptr);
     d->lm_s.assign(d->ranks_here, nullptr);
     d->xb_bytes = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.ffn).total;
@@ -320,9 +332,10 @@ extern "C" int lalb_decoder_set_layer_shard(lalb_decoder *d, int rank, int layer
         return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_layer: rank %d not held here", rank);
     if (!w || layer < 0 || layer >= d->cfg.n_layer || !w->wqkv || !w->wo || !w->wgu || !w->wdown)
         return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_layer: bad layer %d", layer);
-    if (((uintptr_t)w->wqkv | (uintptr_t)w->wo | (uintptr_t)w->wgu | (uintptr_t)w->wdown) & 15u)
+    if (((uintptr_t)w->wqkv | (uintptr_t)w->wo | (uintptr_t)w->wgu | (uintptr_t)w->wdown |
+         (uintptr_t)w->attn_norm | (uintptr_t)w->ffn_norm) & 15u)
         return lalb_fail(d->ctx, LALB_ERR_INVALID,
-                         "decoder_set_layer: weights must be 16-byte aligned");
+                         "decoder_set_layer: weights and norms must be 16-byte aligned");
     d->layers[rank - d->rank0][layer] = *w;
     d->layers_dirty = true;
     drop_graphs(d);
@@ -355,6 +368,15 @@ extern "C" int lalb_decoder_set_lm_head(lalb_decoder *d, const int8_t *w, const 
     if (d->n_rank != 1)
         return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_lm_head: use the shard call");
     return lalb_decoder_set_lm_head_shard(d, 0, w, sw);
+}
+
+extern "C" int lalb_decoder_set_output_norm(lalb_decoder *d, const float *w) {
+    if (!d) return LALB_ERR_INVALID;
+    if ((uintptr_t)w & 15u)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_output_norm: 16-byte alignment");
+    d->out_norm = w;
+    drop_graphs(d);
+    return LALB_OK;
 }
 
 extern "C" int lalb_decoder_ipc_handle(lalb_decoder *d, void *handle) {

@@ -102,6 +102,7 @@ enum : int { kQkv = 0, kO = 1, kGu = 2, kDown = 3, kHead = 4 };
 
 struct Phase {
     const uint8_t *W;                   // this rank's row shard
+    const float *gamma;                 // RMSNorm weights of the prologue (nullable: unit)
     int kind, layer, K, rows_total, unit, row_bytes, R;
     int goff;                           // global index of the shard's first row
     int r0, r1, nchunks;                // this CTA's rows, relative to the shard
@@ -127,9 +128,11 @@ __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const W
     c.ffn = a.ffn;
     c.vocab = a.vocab;
     int g0, g1;
+    d.gamma = nullptr;
     if (p == 4 * a.n_layer) {
         d.kind = kHead;
         d.W = reinterpret_cast<const uint8_t *>(rk.lm_w);
+        d.gamma = a.out_norm;
         d.K = a.hidden;
         d.unit = 1;
         d.row_bytes = a.hidden;
@@ -141,6 +144,7 @@ __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const W
             case kQkv:
                 d.W = static_cast<const uint8_t *>(lw.wqkv);
                 d.K = a.hidden;
+                d.gamma = lw.attn_norm;
                 break;
             case kO:
                 d.W = static_cast<const uint8_t *>(lw.wo);
@@ -149,6 +153,7 @@ __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const W
             case kGu:
                 d.W = static_cast<const uint8_t *>(lw.wgu);
                 d.K = a.hidden;
+                d.gamma = lw.ffn_norm;
                 break;
             default:
                 d.W = static_cast<const uint8_t *>(lw.wdown);
@@ -761,23 +766,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 sq_s[i] = __ldcg(own.asumq + i);
             }
         } else {
-            // one round trip to L2: every thread loads its quads' elements,
-            // then the RMS scale (sum of squares in double) and the quantizer
-            // work from registers
+            // one round trip to L2: every thread loads its quads' elements
+            // (and their RMSNorm weights), then the RMS scale (sum of squares
+            // in double) and the quantizer work from registers
             const float *src = d.kind == kO ? own.q : ((p == 0) ? a.h_in : own.h);
             const int quad = ct >> 2, qi = ct & 3;
-            float v[kPrepPasses][8];
+            float v[kPrepPasses][8], gv[kPrepPasses][8];
             double ss = 0.0;
 #pragma unroll
             for (int ps = 0; ps < kPrepPasses; ++ps) {
                 const int blk = ps * kQuads + quad;
                 if (blk < NS) {
                     load8_cg(src + blk * 32 + 8 * qi, v[ps]);
+                    if (d.gamma) load8_cg(d.gamma + blk * 32 + 8 * qi, gv[ps]);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) ss += (double)v[ps][i] * (double)v[ps][i];
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[ps][i] = 0.0f;
+                    for (int i = 0; i < 8; ++i) v[ps][i] = gv[ps][i] = 0.0f;
                 }
             }
             if (d.kind != kO) {
@@ -789,11 +795,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 double t = 0.0;
 #pragma unroll
                 for (int cw = 0; cw < kNC; ++cw) t += red_s[cw];
-                const float scale = (float)(1.0 / sqrt(t / (double)d.K + 1e-6));
+                const float scale = (float)(1.0 / sqrt(t / (double)d.K + (double)a.rms_eps));
+                // (x * s) * w, one rounding per product (rms_norm's order)
 #pragma unroll
                 for (int ps = 0; ps < kPrepPasses; ++ps)
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[ps][i] = __fmul_rn(v[ps][i], scale);
+                    for (int i = 0; i < 8; ++i) {
+                        v[ps][i] = __fmul_rn(v[ps][i], scale);
+                        if (d.gamma) v[ps][i] = __fmul_rn(v[ps][i], gv[ps][i]);
+                    }
             }
 #pragma unroll
             for (int ps = 0; ps < kPrepPasses; ++ps) {

@@ -220,11 +220,11 @@ __device__ __forceinline__ ScaleWords unpack_scale_words(uint32_t s0,
     return r;
 }
 
-// Unit-weight RMS normalisation factor 1/sqrt(mean(x^2) + 1e-6) of a
-// K-vector, for the whole CTA.  The sum of squares is accumulated in double
-// (each square is exact there), so the float result does not depend on the
-// summation order except in the rare case of a double-rounding tie.
-__device__ __forceinline__ float block_rms_scale(const float *x, int K) {
+// RMS normalisation factor 1/sqrt(mean(x^2) + eps) of a K-vector, for the
+// whole CTA.  The sum of squares is accumulated in double (each square is
+// exact there), so the float result does not depend on the summation order
+// except in the rare case of a double-rounding tie.
+__device__ __forceinline__ float block_rms_scale(const float *x, int K, float eps) {
     __shared__ double red[32];
     __shared__ float result;
     double ss = 0.0;
@@ -240,7 +240,7 @@ __device__ __forceinline__ float block_rms_scale(const float *x, int K) {
         double t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (threadIdx.x == 0) result = (float)(1.0 / sqrt(t / (double)K + 1e-6));
+        if (threadIdx.x == 0) result = (float)(1.0 / sqrt(t / (double)K + (double)eps));
     }
     __syncthreads();
     return result;

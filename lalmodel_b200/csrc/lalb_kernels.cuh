@@ -26,6 +26,7 @@ struct Q4kGemvArgs {
     int rows, K;
     const float *x;        // kInF32 / kInF32Rms
     const float *gamma;    // kInF32Rms, nullable (unit weights)
+    float eps;             // kInF32Rms: RMSNorm epsilon
     const int8_t *xq;      // kInQ8
     const float *sx;
     const int32_t *sumq;
@@ -50,7 +51,8 @@ struct Q8HeadArgs {
     const float *sw;       // [rows]
     int K, row_begin, row_end;
     const float *x;        // kInF32 / kInF32Rms
-    const float *gamma;
+    const float *gamma;    // kInF32Rms, nullable (unit weights)
+    float eps;             // kInF32Rms: RMSNorm epsilon
     const int8_t *xq;      // kInQ8
     const float *sx;
     float *logits;         // [row_end-row_begin], nullable
@@ -92,6 +94,8 @@ struct PersistArgs {
     PersistRank rk[kPersistMaxRanks];   // [rank - rank0]
     unsigned char *xb[kPersistMaxRanks];   // every rank's exchange buffer (peer pointers)
     const float *h_in;                  // [hidden] token input, same on every rank
+    float rms_eps;                      // RMSNorm epsilon
+    const float *out_norm;              // nullable: RMSNorm weights before the LM head
     float *logits;                      // nullable: [vocab] (each rank writes its rows)
     int32_t *argmax;                    // nullable
     unsigned int *status;

@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
                 double t = lane < (nthreads >> 5) ? red_s[lane] : 0.0;
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-                if (lane == 0) red_s[32] = (double)(float)(1.0 / sqrt(t / (double)K + 1e-6));
+                if (lane == 0) red_s[32] = (double)(float)(1.0 / sqrt(t / (double)K + (double)a.eps));
             }
             __syncthreads();
             scale = (float)red_s[32];

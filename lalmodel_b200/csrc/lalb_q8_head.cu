@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_head_kernel(const Q8HeadArgs a
         for (int i = tid; i < NB; i += kThreads) sx_s[i] = a.sx[i];
     } else {
         float scale = 1.0f;
-        if (IN == kInF32Rms) scale = block_rms_scale(a.x, K);
+        if (IN == kInF32Rms) scale = block_rms_scale(a.x, K, a.eps);
         for (int blk = warp; blk < NB; blk += kWarps) {
             float v = a.x[blk * 32 + lane];
             if (IN == kInF32Rms) {

@@ -345,6 +345,18 @@ void lalb_o_swiglu(const float *gate, const float *up, int n, float *act) {
     }
 }
 
+/* rms_norm, runtime/lal_runtime.c:82-87 (the scale's sum of squares in
+ * double instead of float; see lalb_oracle.h). */
+void lalb_o_rms_norm(const float *x, const float *w, int n, float eps, float *out) {
+    double ss = 0.0;
+    for (int i = 0; i < n; i++) ss += (double)x[i] * (double)x[i];
+    const float s = (float)(1.0 / sqrt(ss / (double)n + (double)eps));
+    for (int i = 0; i < n; i++) {
+        volatile float t = x[i] * s;     /* one rounding per product */
+        out[i] = w ? t * w[i] : t;
+    }
+}
+
 /* ------------------------------------------------------------------------ */
 /* seed STE model (per-element CORE/BINARY/PRUNE)                            */
 /* ------------------------------------------------------------------------ */

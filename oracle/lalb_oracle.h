@@ -93,6 +93,14 @@ int lalb_o_argmax(const float *v, int n);
 /* act[i] = (float)(g / (1 + exp(-g)) * up[i]) evaluated in double. */
 void lalb_o_swiglu(const float *gate, const float *up, int n, float *act);
 
+/* RMSNorm, after rms_norm (runtime/lal_runtime.c:82-87):
+ *   s = (float)(1 / sqrt(sum x^2 / n + eps)), the sum and root in double;
+ *   out[i] = (x[i] * s) * w[i], each product one IEEE float rounding.
+ * w may be NULL (unit weights: out[i] = x[i] * s).  The reference sums the
+ * squares in float; here the sum is in double, so s is the float rounding
+ * of the (nearly) exact value and does not depend on summation order. */
+void lalb_o_rms_norm(const float *x, const float *w, int n, float eps, float *out);
+
 /* --- seed STE model, per-element CORE/BINARY/PRUNE int8 encoding --------- */
 /* state[i] (0 CORE, 1 BINARY, 2 PRUNE) and w[i] (fp32) per weight, W [rows][K].
  * Per row j:  amax = max |w| over CORE entries, alpha = mean |w| over BINARY

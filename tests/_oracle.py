@@ -1,7 +1,8 @@
 """numpy-facing wrapper of the CPU oracle (oracle/liblalb_oracle.so).
 
 Test infrastructure: the checker that the GPU results are compared with.
-Builds the oracle with `make -C oracle` when the library is missing.
+Builds the oracle with `make -C oracle` when the library is missing or older
+than its sources.
 """
 import ctypes
 import os
@@ -29,6 +30,7 @@ _SIG = {
     "lalb_o_q8_lmhead_range": (c_int, [P, P, c_int, c_int, c_int, P, P, P, P]),
     "lalb_o_argmax": (c_int, [P, c_int]),
     "lalb_o_swiglu": (None, [P, P, c_int, P]),
+    "lalb_o_rms_norm": (None, [P, P, c_int, c_float, P]),
     "lalb_o_logic_state": (None, [c_u64, c_size_t, c_float, c_float, P]),
     "lalb_o_logic_pack": (None, [P, P, c_int, c_int, P, P]),
     "lalb_o_logic_forward": (None, [P, P, P, c_int, c_int, P, c_int, P]),
@@ -47,7 +49,9 @@ _lib = None
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(SO):
+        srcs = [os.path.join(ORACLE_DIR, f) for f in ("lalb_oracle.c", "lalb_oracle.h",
+                                                      "lalb_cpu_baseline.c")]
+        if not os.path.exists(SO) or any(os.path.getmtime(f) > os.path.getmtime(SO) for f in srcs):
             subprocess.run(["make", "-C", ORACLE_DIR], check=True, capture_output=True)
         L = ctypes.CDLL(SO)
         for k, (r, a) in _SIG.items():
@@ -132,36 +136,40 @@ def swiglu(gate, up):
     return act
 
 
-def rms_normalise(x):
-    """x * (float)(1/sqrt(mean(x^2) + 1e-6)), the scale computed in double."""
-    x = np.asarray(x, np.float32)
-    ss = np.sum(x.astype(np.float64) ** 2)
-    scale = np.float32(1.0 / np.sqrt(ss / x.size + 1e-6))
-    return (x * scale).astype(np.float32)
+def rms_normalise(x, w=None, eps=1e-5):
+    """rms_norm (runtime/lal_runtime.c:82-87) through the C oracle:
+    (x * s) * w with s = (float)(1/sqrt(mean(x^2) + eps)) in double."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    out = np.empty_like(x)
+    wc = None if w is None else np.ascontiguousarray(w, np.float32).reshape(-1)
+    lib().lalb_o_rms_norm(_p(x), _p(wc), x.size, eps, _p(out))
+    return out
 
 
-def decode_chain(layers, lm_q, lm_s, h_in, cfg):
+def decode_chain(layers, lm_q, lm_s, h_in, cfg, out_norm=None):
     """The decoder's per-token math on the CPU (see include/lalb.h).
 
-    layers: list of dicts with Q4_K byte arrays wqkv, wo, wgu, wdown.
-    Returns (h_final, logits, argmax)."""
+    layers: list of dicts with Q4_K byte arrays wqkv, wo, wgu, wdown and
+    optional RMSNorm weights attn_norm, ffn_norm; cfg["rms_eps"] (default
+    1e-5) is the norm epsilon.  Returns (h_final, logits, argmax)."""
     hid, q_rows, kv, ffn = cfg["hidden"], cfg["q_rows"], cfg["kv_rows"], cfg["ffn"]
+    eps = cfg.get("rms_eps", 0.0) or 1e-5
     h = np.array(h_in, np.float32)
     for lw in layers:
-        xq, sx, sq = quantize_act(rms_normalise(h))
+        xq, sx, sq = quantize_act(rms_normalise(h, lw.get("attn_norm"), eps))
         qkv, _ = q4k_matmul(lw["wqkv"], q_rows + 2 * kv, hid, xq, sx, sq)
         q = qkv[0, :q_rows]
         xq, sx, sq = quantize_act(q)
         o, _ = q4k_matmul(lw["wo"], hid, q_rows, xq, sx, sq)
         h = (h + o[0]).astype(np.float32)
-        xq, sx, sq = quantize_act(rms_normalise(h))
+        xq, sx, sq = quantize_act(rms_normalise(h, lw.get("ffn_norm"), eps))
         gu, _ = q4k_matmul(lw["wgu"], 2 * ffn, hid, xq, sx, sq)
         gu = gu[0].reshape(-1, 2, 32)          # 32-row gate/up tiles
         act = swiglu(gu[:, 0, :].reshape(-1), gu[:, 1, :].reshape(-1))
         xq, sx, sq = quantize_act(act)
         d, _ = q4k_matmul(lw["wdown"], hid, ffn, xq, sx, sq)
         h = (h + d[0]).astype(np.float32)
-    xq, sx, _ = quantize_act(rms_normalise(h))
+    xq, sx, _ = quantize_act(rms_normalise(h, out_norm, eps))
     logits, _, am = q8_lmhead(lm_q, lm_s, xq, sx, 0, lm_q.shape[0])
     return h, logits, am
 

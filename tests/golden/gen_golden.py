@@ -1,7 +1,5 @@
 """Generate the golden fixtures under tests/golden/ (run once, output committed).
 
-    python tests/golden/gen_golden.py
-
 Sources of truth, in this container only (neither travels to the GPU box):
   * gguf 0.19.0 (llama.cpp's own Python package, gguf/quants.py):
       - Q4_K.dequantize_blocks pins the 144-byte Q4_K super-block layout,
@@ -13,6 +11,10 @@ Sources of truth, in this container only (neither travels to the GPU box):
     bin_forward_pure_float :543), compiled from its source tree by
     `make -C oracle ref` into oracle/_ref/liblal_ref.so.
   * numpy's float32 -> float16 cast (IEEE round-to-nearest-even).
+  * the reference's decode-step pieces from the same library: rms_norm,
+    apply_rope and attention_forward (decode_ref.npz).
+
+    python tests/golden/gen_golden.py [formats] [binlayer] [decode]
 
 Inputs are seeded; nothing here reads a dataset.
 """
@@ -110,17 +112,70 @@ def binlayer_fixture(rng):
     return out
 
 
-def main():
-    rng = np.random.default_rng(20261201)
-    fx = {}
-    fx.update(q4k_fixture(rng))
-    fx.update(q8_fixture(rng))
-    fx.update(fp16_fixture(rng))
-    np.savez_compressed(os.path.join(HERE, "formats_gguf.npz"), **fx)
-    np.savez_compressed(os.path.join(HERE, "binlayer_ref.npz"),
-                        **binlayer_fixture(rng))
+def _ref_lib():
+    so = os.path.join(ROOT, "oracle", "_ref", "liblal_ref.so")
+    if not os.path.exists(so):
+        sys.exit("build the reference harness first: make -C oracle ref")
+    return ctypes.CDLL(so)
+
+
+def decode_ref_fixture(rng):
+    """The reference's own decode-step pieces from runtime/lal_runtime.c:
+    rms_norm (:82-87), apply_rope (:137-153) and attention_forward
+    (:833-882), called as the layer forward calls them (:310-311, :320-327):
+    RoPE on q and k at position seq_pos, then the causal attention, which
+    stores k and v at seq_pos in the layer's caches and attends 0..seq_pos."""
+    L = _ref_lib()
+    ci, f = ctypes.c_int, ctypes.c_float
+    L.rms_norm.argtypes = [P, P, P, ci]
+    L.apply_rope.argtypes = [P, P, ci, ci, ci, ci]
+    L.attention_forward.argtypes = [P, P, ci, ci, ci, P, P]
+    out = {}
+    for i, (n, scale) in enumerate([(3584, 1.0), (512, 30.0), (96, 1e-3), (3584, 1e3)]):
+        x = (rng.standard_normal(n) * scale).astype(np.float32)
+        w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+        y = np.zeros(n, np.float32)
+        L.rms_norm(ptr(y), ptr(x), ptr(w), n)
+        out[f"rms{i}_x"], out[f"rms{i}_w"], out[f"rms{i}_y"] = x, w, y
+    cases = [(256, 2, 0), (256, 2, 5), (512, 4, 37), (64, 4, 11), (256, 2, 130)]
+    for i, (n_embd, n_head, pos) in enumerate(cases):
+        hd = n_embd // n_head
+        qkv = rng.standard_normal(3 * n_embd).astype(np.float32)
+        kc = np.zeros((pos + 1, n_embd), np.float32)
+        vc = np.zeros((pos + 1, n_embd), np.float32)
+        kc[:pos] = rng.standard_normal((pos, n_embd)).astype(np.float32)
+        vc[:pos] = rng.standard_normal((pos, n_embd)).astype(np.float32)
+        out[f"att{i}_qkv"], out[f"att{i}_k_in"], out[f"att{i}_v_in"] = qkv.copy(), kc.copy(), vc.copy()
+        out[f"att{i}_shape"] = np.array([n_embd, n_head, pos], np.int32)
+        q = qkv.copy()
+        L.apply_rope(ptr(q[:n_embd]), ptr(q[n_embd:2 * n_embd]), pos, n_head, hd, n_embd)
+        out[f"att{i}_qkv_rope"] = q.copy()
+        o = np.zeros(n_embd, np.float32)
+        L.attention_forward(ptr(o), ptr(q), n_embd, n_head, pos, ptr(kc), ptr(vc))
+        # the caches change only at row pos
+        assert np.array_equal(kc[:pos], out[f"att{i}_k_in"][:pos])
+        out[f"att{i}_out"], out[f"att{i}_k_row"], out[f"att{i}_v_row"] = o, kc[pos], vc[pos]
+    return out
+
+
+def main(which=("formats", "binlayer", "decode")):
+    if "formats" in which or "binlayer" in which:
+        rng = np.random.default_rng(20261201)
+        fx = {}
+        fx.update(q4k_fixture(rng))
+        fx.update(q8_fixture(rng))
+        fx.update(fp16_fixture(rng))
+        if "formats" in which:
+            np.savez_compressed(os.path.join(HERE, "formats_gguf.npz"), **fx)
+        bl = binlayer_fixture(rng)
+        if "binlayer" in which:
+            np.savez_compressed(os.path.join(HERE, "binlayer_ref.npz"), **bl)
+    if "decode" in which:
+        np.savez_compressed(os.path.join(HERE, "decode_ref.npz"),
+                            **decode_ref_fixture(np.random.default_rng(20261202)))
     print("wrote", sorted(os.listdir(HERE)))
 
 
 if __name__ == "__main__":
-    main()
+    # no argument: every fixture; else a subset, e.g. `decode`
+    main(tuple(sys.argv[1:]) or ("formats", "binlayer", "decode"))

@@ -38,7 +38,7 @@ def test_binding_table_matches_header():
 
 def test_abi_version_and_status_strings():
     L = _abi.lib()
-    assert L.lalb_abi_version() == 1
+    assert L.lalb_abi_version() == 2
     for st in range(0, -8, -1):
         assert L.lalb_status_string(st)
 

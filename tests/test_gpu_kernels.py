@@ -201,7 +201,9 @@ def test_lm_head_empty_range_and_bad_k(ctx):
 
 
 # ---------------------------------------------------------------- decoder
-def make_decoder_weights(cfg, seed, n_vocab):
+def make_decoder_weights(cfg, seed, n_vocab, norms=False):
+    """Seeded Q4_K layers and an int8 LM head; with norms, every layer also
+    gets RMSNorm weights attn_norm / ffn_norm = 1 + 0.1 N(0, 1)."""
     layers, dev_layers = [], []
     hid, qr, kv, ffn = cfg["hidden"], cfg["q_rows"], cfg["kv_rows"], cfg["ffn"]
 
@@ -211,10 +213,19 @@ def make_decoder_weights(cfg, seed, n_vocab):
     for l in range(cfg["n_layer"]):
         lw = dict(wqkv=qw(qr + 2 * kv, hid, seed + 10 * l), wo=qw(hid, qr, seed + 10 * l + 1),
                   wgu=qw(2 * ffn, hid, seed + 10 * l + 2), wdown=qw(hid, ffn, seed + 10 * l + 3))
+        if norms:
+            lw["attn_norm"] = (1 + O.normal(hid, seed=seed + 10 * l + 4, sigma=0.1)).astype(np.float32)
+            lw["ffn_norm"] = (1 + O.normal(hid, seed=seed + 10 * l + 5, sigma=0.1)).astype(np.float32)
         layers.append(lw)
         dev_layers.append({k: dev(v) for k, v in lw.items()})
     lq, ls = O.q8_quantize_rows(O.normal(n_vocab * hid, seed=seed + 999, sigma=0.02).reshape(n_vocab, hid))
     return layers, dev_layers, lq, ls
+
+
+def set_layers(dec, dl):
+    for l, w in enumerate(dl):
+        dec.set_layer(l, w["wqkv"], w["wo"], w["wgu"], w["wdown"], w.get("attn_norm"),
+                      w.get("ffn_norm"))
 
 
 @pytest.mark.parametrize("path", [lb.Decoder.KERNELS, lb.Decoder.PERSISTENT],
@@ -270,6 +281,45 @@ def test_decoder_step_matches_oracle_chain(ctx, cfg, path):
     assert len(us) == 4 * cfg["n_layer"] + 1
     assert dec.launches_per_step() == (1 if path == lb.Decoder.PERSISTENT else len(us))
     assert all(u > 0 for u in us)
+    dec.close()
+
+
+@pytest.mark.parametrize("path", [lb.Decoder.KERNELS, lb.Decoder.PERSISTENT],
+                         ids=["kernels", "persistent"])
+@pytest.mark.parametrize("cfg", [
+    dict(n_layer=2, hidden=512, q_rows=512, kv_rows=128, ffn=1024, vocab=3000, rms_eps=1e-6),
+    dict(n_layer=1, hidden=3584, q_rows=3584, kv_rows=512, ffn=18944, vocab=20000, rms_eps=0.0),
+    dict(n_layer=0, hidden=768, q_rows=256, kv_rows=0, ffn=256, vocab=777, rms_eps=1e-3),
+])
+def test_decoder_weighted_rmsnorm_matches_oracle(ctx, cfg, path):
+    """rms_norm with weights (runtime/lal_runtime.c:82-87) before qkv, gate/up
+    and the LM head, at the reference's epsilon (0 selects 1e-5) and others."""
+    layers, dl, lq, ls = make_decoder_weights(cfg, seed=1500 + cfg["hidden"], n_vocab=cfg["vocab"],
+                                              norms=True)
+    out_norm = (1 + O.normal(cfg["hidden"], seed=1501, sigma=0.1)).astype(np.float32)
+    dec = lb.Decoder(ctx, **cfg)
+    dec.set_path(path)
+    set_layers(dec, dl)
+    lqd, lsd = dev(lq), dev(ls)
+    dec.set_lm_head(lqd, lsd)
+    dec.set_output_norm(dev(out_norm))
+    h_out = torch.empty(cfg["hidden"], dtype=torch.float32, device="cuda")
+    logits = torch.empty(cfg["vocab"], dtype=torch.float32, device="cuda")
+    am = torch.empty(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for tok in range(2):
+            h_in = O.normal(cfg["hidden"], seed=1502 + tok)
+            ref_h, ref_logits, ref_am = O.decode_chain(layers, lq, ls, h_in, cfg, out_norm)
+            dec.step(dev(h_in), h_out, logits, am)
+            s.synchronize()
+            assert_fp32_parity(host(h_out), ref_h, exact_frac=0.99)
+            assert_fp32_parity(host(logits), ref_logits, exact_frac=0.99)
+            assert int(host(am)[0]) == ref_am
+    # unit weights are not the same as these: the norms are really applied
+    _, unit_logits, _ = O.decode_chain([{k: v for k, v in lw.items() if "norm" not in k}
+                                        for lw in layers], lq, ls, h_in, cfg)
+    assert O.normwise_rel_err(unit_logits, ref_logits) > 1e-3
     dec.close()
 
 

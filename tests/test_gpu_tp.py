@@ -27,12 +27,14 @@ CFGS = [
 
 
 def load_shards(dec, rank, cfg, dl, lqd, lsd):
-    """Give `dec` rank `rank`'s row shards of the full device weights."""
+    """Give `dec` rank `rank`'s row shards of the full device weights (RMSNorm
+    weights, when present, whole)."""
     rows = [lb.tp_range(cfg, m, dec.n_rank, rank) for m in range(5)]
     for l, w in enumerate(dl):
         dec.set_layer_shard(rank, l, lb.shard_rows(w["wqkv"], *rows[0]),
                             lb.shard_rows(w["wo"], *rows[1]), lb.shard_rows(w["wgu"], *rows[2]),
-                            lb.shard_rows(w["wdown"], *rows[3]))
+                            lb.shard_rows(w["wdown"], *rows[3]), w.get("attn_norm"),
+                            w.get("ffn_norm"))
     dec.set_lm_head_shard(rank, lb.shard_rows(lqd, *rows[4]), lb.shard_rows(lsd, *rows[4]))
 
 
@@ -42,7 +44,8 @@ def test_tp_all_ranks_on_one_gpu_match_oracle(ctx, n_rank, ci):
     cfg = CFGS[ci]
     if ci == 1 and n_rank != 2:
         pytest.skip("Qwen-shape layer: two ranks suffice")
-    layers, dl, lq, ls = make_decoder_weights(cfg, seed=2000 + ci, n_vocab=cfg["vocab"])
+    layers, dl, lq, ls = make_decoder_weights(cfg, seed=2000 + ci, n_vocab=cfg["vocab"],
+                                              norms=(ci == 0))
     lqd, lsd = dev(lq), dev(ls)
     dec = lb.Decoder(ctx, **cfg, n_rank=n_rank, rank=-1)
     assert dec.launches_per_step() == 1

@@ -151,6 +151,21 @@ def test_swiglu_and_rms_oracle():
     assert abs(np.sqrt(np.mean(xn.astype(np.float64) ** 2)) - 1) < 1e-5
 
 
+def test_rms_norm_oracle_pinned_to_reference():
+    """The oracle's rms_norm against the reference's own (runtime/lal_runtime.c
+    :82-87, compiled from its source tree; tests/golden/decode_ref.npz).  The
+    reference sums the squares in float, the oracle in double: the scales
+    differ by at most a few float roundings."""
+    g = np.load(os.path.join(GOLD, "decode_ref.npz"))
+    for i in range(4):
+        x, w, y = g[f"rms{i}_x"], g[f"rms{i}_w"], g[f"rms{i}_y"]
+        o = O.rms_normalise(x, w, 1e-5)
+        assert O.normwise_rel_err(o, y) < 2e-6, i
+    # unit weights are rms_norm with w = 1
+    x = g["rms0_x"]
+    assert np.array_equal(O.rms_normalise(x), O.rms_normalise(x, np.ones_like(x)))
+
+
 def test_decode_chain_oracle_small():
     cfg = dict(hidden=256, q_rows=256, kv_rows=64, ffn=512)
     layers = []
