@@ -74,8 +74,9 @@ LALB_API int         lalb_init(int device, lalb_ctx **out);
 LALB_API int         lalb_destroy(lalb_ctx *ctx);
 /* Text of the last error recorded on this context ("" if none). */
 LALB_API const char *lalb_last_error(const lalb_ctx *ctx);
-/* Synchronises the device and returns the device-side status word
- * (0 = no bounded wait has expired); reset != 0 clears it. */
+/* Synchronises the device and returns the device-side status word, a set
+ * of bits: 1 = a bounded wait expired, 2 = a decode position outside the KV
+ * cache was refused (0 = neither); reset != 0 clears it. */
 LALB_API int         lalb_device_status(lalb_ctx *ctx, int reset);
 
 /* ---- formats ---------------------------------------------------------- */
@@ -142,6 +143,58 @@ LALB_API int lalb_lm_head_int8_q8(lalb_ctx *ctx, const int8_t *W, const float *s
                                   const int8_t *xq, const float *sx, float *logits,
                                   int32_t *isum, int32_t *argmax, lalb_stream stream);
 
+/* ---- decode attention (one layer, one token) ----------------------------
+ * attention_forward after apply_rope (runtime/lal_runtime.c:833-882 and
+ * :137-153, called as the layer forward calls them, :310-327), generalised
+ * to grouped KV heads.  qkv = q [n_head*head_dim] | k [n_kv_head*head_dim]
+ * | v [n_kv_head*head_dim] fp32.  RoPE at position pos on every q and k
+ * head (pairs d, d + head_dim/2; angle pos * rope_theta^(-2d/head_dim));
+ * the rotated k and the v go to row pos of k_cache / v_cache
+ * ([max_ctx][n_kv_head*head_dim] fp32, 16-byte aligned); head h attends KV
+ * head h / (n_head / n_kv_head) over positions 0..pos with scores scaled by
+ * 1/sqrt(head_dim): out [n_head*head_dim] = sum_j softmax_j v_j (the
+ * softmax's sum + 1e-12 in the denominator, as in the reference).  RoPE,
+ * scores, softmax and the weighted sum are computed in double and rounded
+ * to float once per value.  head_dim 32, 64, 128 or 256; n_kv_head divides
+ * n_head; 0 <= pos < max_ctx; rope_theta > 1 (the reference uses 10000). */
+LALB_API int lalb_attention_decode(lalb_ctx *ctx, const float *qkv, int n_head, int n_kv_head,
+                                   int head_dim, int pos, int max_ctx, float rope_theta,
+                                   float *k_cache, float *v_cache, float *out,
+                                   lalb_stream stream);
+
+/* ---- next-token sampling after the LM head --------------------------------
+ * generate_text's sampling (models/ste_train.c:2229-2318) on device logits:
+ *   adjusted = logits; ids < n_masked_low_ids -> -1e30 (the reference masks
+ *   its 3 special ids); every distinct token of history[0..n_history) once:
+ *   adjusted /= rep_penalty if > 0, else *= rep_penalty (the reference:
+ *   1.5); no_repeat_ngram = n >= 2 bans (-1e30) every token that would
+ *   complete an n-gram already in the history (the reference: 3);
+ *   temperature <= 0.01: the first maximum (sample_argmax, :1503-1509);
+ *   else the top_k largest (value descending, ties to the lower id),
+ *   p_j = exp((a_j - a_0) / temperature) (float subtraction and division,
+ *   the exponential in double rounded to float once), running float sums;
+ *   the nucleus ends at the first j whose running sum exceeds top_p * sum
+ *   (the reference: 0.9); r = u * (that running sum); the token is the
+ *   first j of the nucleus with r < running sum.
+ * u: device float in [0, 1) (nullable when greedy), so that a captured
+ * graph can be fed a new draw per token.  ws: device workspace of
+ * lalb_sample_ws_bytes(vocab, top_k) bytes (8-byte aligned; no contents
+ * carried between calls).  token (device int32) gets the id; topk_id /
+ * topk_prob (nullable, top_k entries) the ranked ids and their p_j.
+ * Limits: 1 <= top_k <= 256, vocab up to 8192 * (16384 / top_k) ids. */
+typedef struct {
+    float temperature;
+    int top_k;
+    float top_p;
+    float rep_penalty;     /* 1: off */
+    int no_repeat_ngram;   /* 0: off */
+    int n_masked_low_ids;  /* 0: none */
+} lalb_sampling;
+LALB_API int lalb_sample_ws_bytes(int vocab, int top_k, size_t *bytes);
+LALB_API int lalb_sample(lalb_ctx *ctx, const float *logits, int vocab, const int32_t *history,
+                         int n_history, const lalb_sampling *params, const float *u, void *ws,
+                         int32_t *token, int32_t *topk_id, float *topk_prob, lalb_stream stream);
+
 /* Allocation-free LM head.  This entry point has no counterpart in the
  * reference.  It is for callers that cannot call cudaMalloc: an engine whose
  * own memory pool owns the device and forbids libraries from allocating (a
@@ -171,11 +224,14 @@ LALB_API int lalb_lm_head_int8_range_noalloc(const int8_t *W, const float *sw, i
                                              float *logits, int32_t *argmax,
                                              lalb_stream stream);
 
-/* ---- Qwen2.5-shape decode matmul set (one token) -----------------------
+/* ---- Qwen2.5-shape decode (one token) -----------------------------------
  * Per layer, with h the fp32 residual stream [hidden]:
  *   qkv  = Wqkv . Q8(rmsnorm(h, attn_norm))    rows q_rows + 2*kv_rows
- *   h    = h + Wo . Q8(qkv[0:q_rows])          (the attention output is
- *                                              out of scope: q stands in)
+ *   att  = attention(qkv, KV cache, pos)       (lalb_attention_decode; with
+ *                                              head_dim = 0 there is no
+ *                                              attention and att = q, the
+ *                                              matmul set alone)
+ *   h    = h + Wo . Q8(att)
  *   a    = silu(gate) * up, gate/up = Wgu . Q8(rmsnorm(h, ffn_norm))
  *   h    = h + Wdown . Q8(a)
  * then logits = LMhead . Q8(rmsnorm(h, output norm)) and argmax.
@@ -194,6 +250,10 @@ typedef struct {
     int ffn;        /* intermediate size */
     int vocab;      /* LM-head rows */
     float rms_eps;  /* RMSNorm epsilon; 0 selects 1e-5 (the reference's rms_norm) */
+    int head_dim;   /* 0: no attention; else 32, 64, 128 or 256, dividing q_rows and
+                     * kv_rows (q_rows/head_dim heads over kv_rows/head_dim KV heads) */
+    int max_ctx;    /* positions of every layer's KV cache (attention only) */
+    float rope_theta; /* RoPE base; 0 selects 10000 (the reference's apply_rope) */
 } lalb_decoder_cfg;
 
 typedef struct {
@@ -216,6 +276,18 @@ LALB_API int lalb_decoder_set_lm_head(lalb_decoder *dec, const int8_t *w,
 /* RMSNorm weights [hidden] applied before the LM head (NULL: unit, the
  * default).  Every rank of a tensor-parallel decoder holds them whole. */
 LALB_API int lalb_decoder_set_output_norm(lalb_decoder *dec, const float *w);
+/* Attention only: layer `layer`'s KV cache, two caller-owned device buffers
+ * of max_ctx * kv_rows fp32 (16-byte aligned; row p holds position p).
+ * Every rank of a tensor-parallel decoder holds its own full cache (the
+ * attention is computed whole on every rank, like q and o). */
+LALB_API int lalb_decoder_set_kv_cache(lalb_decoder *dec, int layer, float *k_cache,
+                                       float *v_cache);
+/* Attention only: the position of the next token (0 at creation); every step
+ * attends positions 0..pos, writes row pos of the caches and advances pos.
+ * A step at pos >= max_ctx fails with LALB_ERR_INVALID.  Enqueued on the
+ * stream (no synchronisation); set the same position on every rank. */
+LALB_API int lalb_decoder_set_position(lalb_decoder *dec, int pos, lalb_stream stream);
+LALB_API int lalb_decoder_position(const lalb_decoder *dec);
 /* One token on device buffers: h_in [hidden] (read only), h_out [hidden]
  * (nullable: final residual stream), logits [vocab] (nullable), argmax
  * (device int32, nullable).  On a non-default stream the token is captured
@@ -229,13 +301,13 @@ LALB_API int lalb_decoder_step_host(lalb_decoder *dec, const float *h_in_host,
                                     int32_t *argmax_host, lalb_stream stream);
 /* One token on the per-phase kernel chain with a CUDA event between
  * consecutive kernels (no programmatic overlap): kernel_us (host,
- * 4*n_layer + 1 floats) receives each kernel's duration in launch order --
- * per layer qkv, o, gate/up, down; then the LM head.  Synchronises the
- * stream. */
+ * P*n_layer + 1 floats, P = 5 with attention, else 4) receives each
+ * kernel's duration in launch order -- per layer qkv, (attention,) o,
+ * gate/up, down; then the LM head.  Synchronises the stream. */
 LALB_API int lalb_decoder_profile_step(lalb_decoder *dec, const float *h_in,
                                        float *kernel_us, lalb_stream stream);
 /* One token on the persistent path with a phase timeline: trace_host
- * (host, trace_len >= n_cta * (4*n_layer + 1) * 8 values) receives, for
+ * (host, trace_len >= n_cta * (P*n_layer + 1) * 8 values, P as above) receives, for
  * each CTA and phase, six GPU global-timer figures (ns): [0] the CTA
  * finished the phase's work, [1] it left the grid barrier that ends the
  * phase, [2] its activation prologue was done, [3] the time its first

@@ -132,6 +132,41 @@ class Context:
                    _p(x), _p(logits), _p(am), _stream())
         return logits, am
 
+    def attention_decode(self, qkv, n_head, n_kv_head, head_dim, pos, k_cache, v_cache,
+                         rope_theta=10000.0, out=None):
+        """One layer's decode attention at position pos (lalb_attention_decode):
+        writes row pos of the caches (float32 [max_ctx][n_kv_head*head_dim])
+        and returns out [n_head*head_dim]."""
+        max_ctx = k_cache.numel() // (n_kv_head * head_dim)
+        if out is None:
+            out = torch.empty(n_head * head_dim, dtype=torch.float32, device=qkv.device)
+        self._call("lalb_attention_decode", self.h, _p(qkv), n_head, n_kv_head, head_dim, pos,
+                   max_ctx, ctypes.c_float(rope_theta), _p(k_cache), _p(v_cache), _p(out),
+                   _stream())
+        return out
+
+    def sample(self, logits, history=None, temperature=0.0, top_k=1, top_p=0.9,
+               rep_penalty=1.0, no_repeat_ngram=0, n_masked_low_ids=0, u=None, want_topk=False):
+        """Next token from device logits (lalb_sample).  history: int32 CUDA
+        tensor of earlier tokens (or None); u: float32 CUDA tensor [1] with
+        the draw in [0, 1) (needed above temperature 0.01).  Returns the
+        token tensor [1] (and the ranked ids and p_j with want_topk)."""
+        vocab = logits.numel()
+        n = ctypes.c_size_t()
+        st = _abi.lib().lalb_sample_ws_bytes(vocab, top_k, ctypes.byref(n))
+        if st:
+            raise LalbError("lalb_sample_ws_bytes", st)
+        ws = torch.empty(max(n.value, 8), dtype=torch.uint8, device=logits.device)
+        tok = torch.empty(1, dtype=torch.int32, device=logits.device)
+        k = min(top_k, vocab)
+        tid = torch.empty(k, dtype=torch.int32, device=logits.device) if want_topk else None
+        tpr = torch.empty(k, dtype=torch.float32, device=logits.device) if want_topk else None
+        p = _abi.Sampling(temperature, top_k, top_p, rep_penalty, no_repeat_ngram, n_masked_low_ids)
+        nh = 0 if history is None else history.numel()
+        self._call("lalb_sample", self.h, _p(logits), vocab, _p(history), nh, ctypes.byref(p),
+                   _p(u), _p(ws), _p(tok), _p(tid), _p(tpr), _stream())
+        return (tok, tid, tpr) if want_topk else tok
+
     def lm_head_int8_q8(self, W, sw, xq, sx, row_begin, row_end, want_isum=False):
         K = W.shape[1]
         n = row_end - row_begin
@@ -210,12 +245,15 @@ class Decoder:
     """The Qwen2.5-shape decode matmul set (include/lalb.h, lalb_decoder_*)."""
 
     def __init__(self, ctx, n_layer, hidden, q_rows, kv_rows, ffn, vocab, n_rank=1, rank=0,
-                 rms_eps=0.0):
+                 rms_eps=0.0, head_dim=0, max_ctx=0, rope_theta=0.0):
         """n_rank > 1: tensor-parallel decoder holding rank `rank` (one GPU
         per rank, peers connected with ipc_handle()/connect()), or every rank
-        on this GPU with rank=-1.  rms_eps 0 selects 1e-5."""
+        on this GPU with rank=-1.  rms_eps 0 selects 1e-5.  head_dim > 0
+        turns the decode attention on (KV caches of max_ctx positions, set per
+        layer with set_kv_cache; rope_theta 0 selects 10000)."""
         self.ctx = ctx
-        self.cfg = DecoderCfg(n_layer, hidden, q_rows, kv_rows, ffn, vocab, rms_eps)
+        self.cfg = DecoderCfg(n_layer, hidden, q_rows, kv_rows, ffn, vocab, rms_eps, head_dim,
+                              max_ctx, rope_theta)
         self.n_rank, self.rank = n_rank, rank
         # the library keeps only device pointers: hold the weight tensors (a
         # shard built on the fly would otherwise be freed while still in use)
@@ -285,6 +323,17 @@ class Decoder:
         self.ctx._call("lalb_decoder_set_layer", self.h, layer, ctypes.byref(lw))
         self._keep[("layer", 0, layer)] = (wqkv, wo, wgu, wdown, attn_norm, ffn_norm)
 
+    def set_kv_cache(self, layer, k_cache, v_cache):
+        """Layer `layer`'s caches: float32 CUDA tensors of max_ctx * kv_rows."""
+        self.ctx._call("lalb_decoder_set_kv_cache", self.h, layer, _p(k_cache), _p(v_cache))
+        self._keep[("kv", layer)] = (k_cache, v_cache)
+
+    def set_position(self, pos):
+        self.ctx._call("lalb_decoder_set_position", self.h, pos, _stream())
+
+    def position(self):
+        return _abi.lib().lalb_decoder_position(self.h)
+
     def set_output_norm(self, w):
         """RMSNorm weights [hidden] before the LM head (None: unit)."""
         self.ctx._call("lalb_decoder_set_output_norm", self.h, _p(w))
@@ -305,10 +354,13 @@ class Decoder:
                        _stream())
         return out.value
 
+    def phases_per_layer(self):
+        return 5 if self.cfg.head_dim > 0 else 4
+
     def profile_step(self, h_in):
         """Per-kernel durations (microseconds) of one token on the per-phase
-        kernel chain, in launch order (4*n_layer + 1 values)."""
-        n = 4 * self.cfg.n_layer + 1
+        kernel chain, in launch order (phases_per_layer() * n_layer + 1)."""
+        n = self.phases_per_layer() * self.cfg.n_layer + 1
         buf = (ctypes.c_float * n)()
         self.ctx._call("lalb_decoder_profile_step", self.h, _p(h_in), buf, _stream())
         return list(buf)
@@ -320,7 +372,7 @@ class Decoder:
         compute, producer done issuing), then the producer's and consumer 0's
         mbarrier polls."""
         import numpy as np
-        n_phase = 4 * self.cfg.n_layer + 1
+        n_phase = self.phases_per_layer() * self.cfg.n_layer + 1
         n = max_cta * n_phase * 8
         buf = (ctypes.c_ulonglong * n)()
         n_cta = ctypes.c_int(0)

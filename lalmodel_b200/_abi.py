@@ -20,12 +20,18 @@ STATUS = {0: "LALB_OK", -1: "LALB_ERR_INVALID", -2: "LALB_ERR_CUDA", -3: "LALB_E
 
 class DecoderCfg(ctypes.Structure):
     _fields_ = [("n_layer", c_int), ("hidden", c_int), ("q_rows", c_int),
-                ("kv_rows", c_int), ("ffn", c_int), ("vocab", c_int), ("rms_eps", c_float)]
+                ("kv_rows", c_int), ("ffn", c_int), ("vocab", c_int), ("rms_eps", c_float),
+                ("head_dim", c_int), ("max_ctx", c_int), ("rope_theta", c_float)]
 
 
 class LayerWeights(ctypes.Structure):
     _fields_ = [("wqkv", P), ("wo", P), ("wgu", P), ("wdown", P), ("attn_norm", P),
                 ("ffn_norm", P)]
+
+
+class Sampling(ctypes.Structure):
+    _fields_ = [("temperature", c_float), ("top_k", c_int), ("top_p", c_float),
+                ("rep_penalty", c_float), ("no_repeat_ngram", c_int), ("n_masked_low_ids", c_int)]
 
 
 # name -> (restype, argtypes); mirrors include/lalb.h one to one
@@ -50,6 +56,12 @@ SIGNATURES = {
     "lalb_decoder_set_layer": (c_int, [P, c_int, ctypes.POINTER(LayerWeights)]),
     "lalb_decoder_set_lm_head": (c_int, [P, P, P]),
     "lalb_decoder_set_output_norm": (c_int, [P, P]),
+    "lalb_decoder_set_kv_cache": (c_int, [P, c_int, P, P]),
+    "lalb_decoder_set_position": (c_int, [P, c_int, P]),
+    "lalb_decoder_position": (c_int, [P]),
+    "lalb_attention_decode": (c_int, [P, P, c_int, c_int, c_int, c_int, c_int, c_float, P, P, P, P]),
+    "lalb_sample_ws_bytes": (c_int, [c_int, c_int, ctypes.POINTER(c_size_t)]),
+    "lalb_sample": (c_int, [P, P, c_int, P, c_int, ctypes.POINTER(Sampling), P, P, P, P, P, P]),
     "lalb_decoder_step": (c_int, [P, P, P, P, P, P]),
     "lalb_decoder_step_host": (c_int, [P, P, P, P]),
     "lalb_decoder_profile_step": (c_int, [P, P, P, P]),

@@ -25,6 +25,14 @@ struct lalb_decoder {
     std::vector<const int8_t *> lm_w;                     // [ranks_here]
     std::vector<const float *> lm_s;
     const float *out_norm = nullptr;   // RMSNorm weights before the LM head (nullable)
+    // attention (cfg.head_dim > 0): phases per layer, KV caches, position
+    bool attn = false;
+    int ppl = 4;
+    std::vector<float *> kv_host;      // [n_layer][2] k, v cache pointers (caller-owned)
+    float **kv_dev = nullptr;          // device copy for the persistent kernel
+    bool kv_dirty = true;
+    int pos = 0;                       // host mirror of the position word
+    float *att = nullptr;              // chain: attention output [q_rows]
     // activations of the per-phase kernel chain (device, owned; one rank only)
     float *qkv = nullptr;     // [q_rows + 2*kv_rows]
     float *h_res = nullptr;   // [hidden] residual stream
@@ -85,12 +93,32 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
             if ((st = lalb_launch_q4k_gemv(ctx, a, kInF32Rms, kEpiStore, s, pdl, 2))) return st;
             pdl = true;
         }
+        if (d->attn) {
+            const PersistXLayout L = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.kv_rows,
+                                                          c.ffn, c.head_dim);
+            lalb::AttnStep a = {};
+            a.qkv = d->qkv;
+            a.k_cache = d->kv_host[2 * l];
+            a.v_cache = d->kv_host[2 * l + 1];
+            a.out = d->att;
+            a.part = reinterpret_cast<double *>(d->xb_own + L.att_part);
+            a.cnt = reinterpret_cast<unsigned int *>(d->xb_own + L.att_cnt);
+            a.n_head = c.q_rows / c.head_dim;
+            a.n_kv = c.kv_rows / c.head_dim;
+            a.hd = c.head_dim;
+            a.theta = (double)c.rope_theta;
+            LALB_CUDA_TRY(ctx, mark());
+            const int ctas = a.n_head * lalb::attn_chunks(a.n_head, c.max_ctx - 1, ctx->sm_count);
+            if ((st = lalb_launch_attention(ctx, a, reinterpret_cast<const int *>(d->xb_own + L.pos),
+                                            c.max_ctx, ctas, s)))
+                return st;
+        }
         {
             Q4kGemvArgs a = {};
             a.W = static_cast<const uint8_t *>(w.wo);
             a.rows = c.hidden;
             a.K = c.q_rows;
-            a.x = d->qkv;  // the attention output is out of scope: q stands in
+            a.x = d->attn ? d->att : d->qkv;  // without attention q stands in
             a.y = d->h_res;
             a.resid = resid;
             a.unit = 1;
@@ -142,6 +170,12 @@ int launch_token(lalb_decoder *d, const float *h_in, float *h_out, float *logits
     int st = lalb_launch_q8_head(ctx, a, kInF32Rms, s, pdl, 2);
     if (st) return st;
     LALB_CUDA_TRY(ctx, mark());
+    if (d->attn) {
+        const PersistXLayout L = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.kv_rows, c.ffn,
+                                                      c.head_dim);
+        if ((st = lalb_launch_advance_position(ctx, reinterpret_cast<int *>(d->xb_own + L.pos), s)))
+            return st;
+    }
     if (h_out)
         LALB_CUDA_TRY(ctx, cudaMemcpyAsync(h_out, c.n_layer > 0 ? d->h_res : h_in,
                                            sizeof(float) * c.hidden, cudaMemcpyDeviceToDevice, s));
@@ -168,6 +202,12 @@ int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, fl
         LALB_CUDA_TRY(ctx, cudaStreamSynchronize(s));  // the host vectors may change after
         d->layers_dirty = false;
     }
+    if (d->attn && d->kv_dirty) {
+        LALB_CUDA_TRY(ctx, cudaMemcpyAsync(d->kv_dev, d->kv_host.data(),
+                                           sizeof(float *) * 2 * c.n_layer, cudaMemcpyHostToDevice, s));
+        LALB_CUDA_TRY(ctx, cudaStreamSynchronize(s));
+        d->kv_dirty = false;
+    }
     PersistArgs a = {};
     a.n_layer = c.n_layer;
     a.hidden = c.hidden;
@@ -175,6 +215,15 @@ int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, fl
     a.kv_rows = c.kv_rows;
     a.ffn = c.ffn;
     a.vocab = c.vocab;
+    a.ppl = d->ppl;
+    a.norm = d->out_norm != nullptr;
+    for (int r = 0; r < d->ranks_here; ++r)
+        for (int l = 0; l < c.n_layer; ++l)
+            if (d->layers[r][l].attn_norm || d->layers[r][l].ffn_norm) a.norm = 1;
+    a.head_dim = c.head_dim;
+    a.max_ctx = c.max_ctx;
+    a.rope_theta = (double)c.rope_theta;
+    a.kv_cache = d->kv_dev;
     a.n_rank = d->n_rank;
     a.rank0 = d->rank0;
     a.ranks_here = d->ranks_here;
@@ -196,7 +245,8 @@ int launch_token_persistent(lalb_decoder *d, const float *h_in, float *h_out, fl
     a.trace = trace;
     if (int st = lalb_launch_persist(ctx, a, s)) return st;
     if (h_out) {
-        const PersistXLayout L = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.ffn);
+        const PersistXLayout L = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.kv_rows, c.ffn,
+                                                      c.head_dim);
         const float *hf = c.n_layer > 0 ? reinterpret_cast<const float *>(d->xb[d->rank0] + L.h) : h_in;
         LALB_CUDA_TRY(ctx, cudaMemcpyAsync(h_out, hf, sizeof(float) * c.hidden,
                                            cudaMemcpyDeviceToDevice, s));
@@ -226,6 +276,8 @@ void free_decoder(lalb_decoder *d) {
     cudaFree(d->argmax_dev);
     cudaFreeHost(d->argmax_host);
     cudaFree(d->layers_dev);
+    cudaFree(d->kv_dev);
+    cudaFree(d->att);
     for (int j = 0; j < kPersistMaxRanks; ++j)
         if (d->xb_opened[j]) cudaIpcCloseMemHandle(d->xb[j]);
     cudaFree(d->xb_own);
@@ -258,6 +310,18 @@ extern "C" int lalb_decoder_create_tp(lalb_ctx *ctx, const lalb_decoder_cfg *cfg
     if (!(c.rms_eps >= 0.0f) || c.rms_eps > 1.0f)
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: rms_eps %g outside [0, 1]",
                          (double)c.rms_eps);
+    if (c.head_dim != 0) {
+        if (c.head_dim < 0 || c.q_rows % c.head_dim || c.kv_rows <= 0 || c.kv_rows % c.head_dim ||
+            lalb_attention_check(c.q_rows / c.head_dim, c.kv_rows / c.head_dim, c.head_dim))
+            return lalb_fail(ctx, LALB_ERR_INVALID,
+                             "decoder_create: head_dim %d (32, 64, 128 or 256, dividing q_rows and "
+                             "kv_rows, KV heads dividing the heads)", c.head_dim);
+        if (c.max_ctx <= 0 || (long long)c.max_ctx * c.kv_rows >= (1LL << 31))
+            return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: max_ctx %d", c.max_ctx);
+        if (!(c.rope_theta == 0.0f || c.rope_theta > 1.0f))
+            return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: rope_theta %g",
+                             (double)c.rope_theta);
+    }
     if (n_rank < 1 || n_rank > kPersistMaxRanks || rank < -1 || rank >= n_rank)
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_create: rank %d of %d", rank, n_rank);
     LALB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
@@ -266,13 +330,18 @@ extern "C" int lalb_decoder_create_tp(lalb_ctx *ctx, const lalb_decoder_cfg *cfg
     d->ctx = ctx;
     d->cfg = c;
     if (d->cfg.rms_eps == 0.0f) d->cfg.rms_eps = 1e-5f;   // rms_norm's constant (lal_runtime.c:84)
+    if (d->cfg.rope_theta == 0.0f) d->cfg.rope_theta = 10000.0f;   // apply_rope's base (:143)
+    d->attn = c.head_dim > 0;
+    d->ppl = d->attn ? 5 : 4;
+    d->kv_host.assign(d->attn ? 2 * c.n_layer : 0, nullptr);
     d->n_rank = n_rank;
     d->rank0 = rank < 0 ? 0 : rank;
     d->ranks_here = rank < 0 ? n_rank : 1;
     d->layers.assign(d->ranks_here, std::vector<lalb_layer_weights>(c.n_layer, lalb_layer_weights{}));
     d->lm_w.assign(d->ranks_here, nullptr);
     d->lm_s.assign(d->ranks_here, nullptr);
-    d->xb_bytes = lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.ffn).total;
+    d->xb_bytes =
+        lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.kv_rows, c.ffn, c.head_dim).total;
     const bool chain = n_rank == 1;   // the per-phase kernel chain runs on one GPU only
     bool ok = (!chain || (cudaMalloc(&d->qkv, sizeof(float) * (c.q_rows + 2 * c.kv_rows)) == cudaSuccess &&
                           cudaMalloc(&d->h_res, sizeof(float) * c.hidden) == cudaSuccess &&
@@ -284,6 +353,8 @@ extern "C" int lalb_decoder_create_tp(lalb_ctx *ctx, const lalb_decoder_cfg *cfg
               cudaMallocHost(&d->argmax_host, sizeof(int32_t)) == cudaSuccess &&
               cudaMalloc(&d->layers_dev, sizeof(lalb_layer_weights) * (d->ranks_here * c.n_layer + 1)) ==
                   cudaSuccess &&
+              (!d->attn || (cudaMalloc(&d->kv_dev, sizeof(float *) * (2 * c.n_layer + 1)) == cudaSuccess &&
+                            (!chain || cudaMalloc(&d->att, sizeof(float) * c.q_rows) == cudaSuccess))) &&
               cudaMalloc(&d->xb_own, d->xb_bytes * d->ranks_here) == cudaSuccess &&
               cudaMemset(d->xb_own, 0, d->xb_bytes * d->ranks_here) == cudaSuccess &&
               cudaDeviceSynchronize() == cudaSuccess;
@@ -379,6 +450,47 @@ extern "C" int lalb_decoder_set_output_norm(lalb_decoder *d, const float *w) {
     return LALB_OK;
 }
 
+extern "C" int lalb_decoder_set_kv_cache(lalb_decoder *d, int layer, float *k_cache,
+                                         float *v_cache) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!d->attn)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_kv_cache: no attention (head_dim 0)");
+    if (layer < 0 || layer >= d->cfg.n_layer || !k_cache || !v_cache ||
+        (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15u))
+        return lalb_fail(d->ctx, LALB_ERR_INVALID,
+                         "decoder_set_kv_cache: layer %d, caches non-null and 16-byte aligned", layer);
+    d->kv_host[2 * layer] = k_cache;
+    d->kv_host[2 * layer + 1] = v_cache;
+    d->kv_dirty = true;
+    drop_graphs(d);
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_set_position(lalb_decoder *d, int pos, lalb_stream stream) {
+    if (!d) return LALB_ERR_INVALID;
+    if (!d->attn)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_position: no attention (head_dim 0)");
+    if (pos < 0 || pos > d->cfg.max_ctx)
+        return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder_set_position: %d outside [0, %d]", pos,
+                         d->cfg.max_ctx);
+    LALB_CUDA_TRY(d->ctx, cudaSetDevice(d->ctx->device));
+    const lalb_decoder_cfg &c = d->cfg;
+    const PersistXLayout L =
+        lalb_persist_xlayout(c.n_layer, c.hidden, c.q_rows, c.kv_rows, c.ffn, c.head_dim);
+    for (int r = 0; r < d->ranks_here; ++r)
+        if (int st = lalb_launch_set_position(
+                d->ctx, reinterpret_cast<int *>(d->xb_own + d->xb_bytes * r + L.pos), pos,
+                (cudaStream_t)stream))
+            return st;
+    d->pos = pos;
+    return LALB_OK;
+}
+
+extern "C" int lalb_decoder_position(const lalb_decoder *d) {
+    if (!d) return LALB_ERR_INVALID;
+    return d->pos;
+}
+
 extern "C" int lalb_decoder_ipc_handle(lalb_decoder *d, void *handle) {
     if (!d) return LALB_ERR_INVALID;
     if (!handle || d->ranks_here != 1)
@@ -453,6 +565,7 @@ extern "C" int lalb_decoder_reset(lalb_decoder *d, lalb_stream stream) {
     LALB_CUDA_TRY(d->ctx, cudaSetDevice(d->ctx->device));
     LALB_CUDA_TRY(d->ctx, cudaMemsetAsync(d->xb_own, 0, d->xb_bytes * d->ranks_here,
                                           (cudaStream_t)stream));
+    d->pos = 0;   // the position word is part of the buffer
     return LALB_OK;
 }
 
@@ -468,12 +581,30 @@ static int check_ready(lalb_decoder *d) {
     }
     if (!d->connected)
         return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: peers not connected");
+    if (d->attn) {
+        for (int l = 0; l < d->cfg.n_layer; ++l)
+            if (!d->kv_host[2 * l])
+                return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: KV cache of layer %d not set", l);
+        if (d->pos >= d->cfg.max_ctx)
+            return lalb_fail(d->ctx, LALB_ERR_INVALID, "decoder: position %d, the KV cache holds %d",
+                             d->pos, d->cfg.max_ctx);
+    }
     return LALB_OK;
 }
+
+static int step_impl(lalb_decoder *d, const float *h_in, float *h_out, float *logits,
+                     int32_t *argmax, lalb_stream stream);
 
 extern "C" int lalb_decoder_step(lalb_decoder *d, const float *h_in, float *h_out,
                                  float *logits, int32_t *argmax, lalb_stream stream) {
     if (!d) return LALB_ERR_INVALID;
+    const int st = step_impl(d, h_in, h_out, logits, argmax, stream);
+    if (st == LALB_OK && d->attn) ++d->pos;   // the token advances the device position word
+    return st;
+}
+
+static int step_impl(lalb_decoder *d, const float *h_in, float *h_out, float *logits,
+                     int32_t *argmax, lalb_stream stream) {
     lalb_ctx *ctx = d->ctx;
     if (!h_in) return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_step: null h_in");
     if (int st = check_ready(d)) return st;
@@ -546,7 +677,7 @@ extern "C" int lalb_decoder_profile_step(lalb_decoder *d, const float *h_in, flo
     cudaStream_t s = nullptr;
     LALB_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
     cudaEvent_t dep = nullptr;
-    const int n = 4 * d->cfg.n_layer + 1;
+    const int n = d->ppl * d->cfg.n_layer + 1;
     std::vector<cudaEvent_t> ev(n + 1, nullptr);
     int st = LALB_OK;
     for (auto &e : ev)
@@ -582,6 +713,7 @@ extern "C" int lalb_decoder_profile_step(lalb_decoder *d, const float *h_in, flo
     if (st == LALB_ERR_CUDA)
         return lalb_fail(ctx, st, "decoder_profile_step: event timing failed (%s)",
                          cudaGetErrorString(cudaGetLastError()));
+    if (st == LALB_OK && d->attn) ++d->pos;
     return st;
 }
 
@@ -595,7 +727,7 @@ extern "C" int lalb_decoder_trace_step(lalb_decoder *d, const float *h_in,
     if (int st = check_ready(d)) return st;
     if (!use_persistent(d))
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_trace_step: needs the persistent path");
-    const size_t n = (size_t)ctx->sm_count * (4 * d->cfg.n_layer + 1) * 8;
+    const size_t n = (size_t)ctx->sm_count * (d->ppl * d->cfg.n_layer + 1) * 8;
     if ((size_t)trace_len < n)
         return lalb_fail(ctx, LALB_ERR_INVALID, "decoder_trace_step: trace_len < %zu", n);
     cudaStream_t s = (cudaStream_t)stream;
@@ -608,6 +740,7 @@ extern "C" int lalb_decoder_trace_step(lalb_decoder *d, const float *h_in,
         st = lalb_cuda_fail(ctx, cudaGetLastError(), "decoder_trace_step: copy");
     cudaFree(tr);
     *n_cta = (ctx->sm_count / d->ranks_here) * d->ranks_here;
+    if (st == LALB_OK && d->attn) ++d->pos;
     return st;
 }
 
@@ -633,7 +766,8 @@ extern "C" int lalb_decoder_path(const lalb_decoder *d) {
 
 extern "C" int lalb_decoder_launches_per_step(const lalb_decoder *d) {
     if (!d) return LALB_ERR_INVALID;
-    return use_persistent(d) ? 1 : 4 * d->cfg.n_layer + 1;
+    // the chain: one kernel per phase, plus the position update with attention
+    return use_persistent(d) ? 1 : d->ppl * d->cfg.n_layer + 1 + (d->attn ? 1 : 0);
 }
 
 extern "C" int lalb_decoder_destroy(lalb_decoder *d) {

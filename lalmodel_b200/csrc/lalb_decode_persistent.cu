@@ -72,6 +72,8 @@ constexpr int kPrepPasses = (kPersistMaxHidden / 32 + kQuads - 1) / kQuads;
 static_assert(kNC < 24, "red_s holds kNC partial sums and the scale");
 static_assert((2 * kSlots) % kNC == 0, "slot reuse two uses back must be the same consumer");
 static_assert(kSlots % kNP == 0, "every slot is filled by one producer");
+static_assert(kNC == kAttnWarps, "the attention items run on the consumer warps");
+static_assert(kPersistMaxFfn >= (int)kAttnSmemBytes, "attention scratch lives in the xq area");
 
 struct Layout {
     uint32_t off_bar, off_xq, off_sx, off_sq, off_red, off_bestv, off_besti, off_tile, off_tcnt,
@@ -98,11 +100,18 @@ __host__ __device__ inline Layout make_layout() {
     return L;
 }
 
-enum : int { kQkv = 0, kO = 1, kGu = 2, kDown = 3, kHead = 4 };
+enum : int { kQkv = 0, kAttn = 1, kO = 2, kGu = 3, kDown = 4, kHead = 5 };
+
+// Kind of phase p: per layer qkv, (attention,) o, gate/up, down; then the head.
+template <int PPL>
+__device__ __forceinline__ int phase_kind(const PersistArgs &a, int p) {
+    if (p == PPL * a.n_layer) return kHead;
+    const int k = p % PPL;
+    return PPL == 5 ? k : (k == 0 ? kQkv : k + 1);
+}
 
 struct Phase {
     const uint8_t *W;                   // this rank's row shard
-    const float *gamma;                 // RMSNorm weights of the prologue (nullable: unit)
     int kind, layer, K, rows_total, unit, row_bytes, R;
     int goff;                           // global index of the shard's first row
     int r0, r1, nchunks;                // this CTA's rows, relative to the shard
@@ -116,9 +125,10 @@ struct Where {
     int cb;        // CTA index within the rank
 };
 
+template <int PPL>
 __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const Where &w) {
     Phase d;
-    d.layer = p >> 2;
+    d.layer = p / PPL;
     const PersistRank &rk = a.rk[w.rl];
     lalb_decoder_cfg c;
     c.n_layer = a.n_layer;
@@ -128,23 +138,30 @@ __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const W
     c.ffn = a.ffn;
     c.vocab = a.vocab;
     int g0, g1;
-    d.gamma = nullptr;
-    if (p == 4 * a.n_layer) {
-        d.kind = kHead;
+    d.kind = phase_kind<PPL>(a, p);
+    if (d.kind == kAttn) {
+        // no weights: the producers skip the phase (their L2 prefetch runs
+        // on into o's rows), the consumers run the attention items
+        d.W = nullptr;
+        d.K = a.q_rows;
+        d.unit = 1;
+        d.row_bytes = 0;
+        d.goff = d.rows_total = d.r0 = d.r1 = d.nchunks = 0;
+        d.R = 1;
+        return d;
+    }
+    if (d.kind == kHead) {
         d.W = reinterpret_cast<const uint8_t *>(rk.lm_w);
-        d.gamma = a.out_norm;
         d.K = a.hidden;
         d.unit = 1;
         d.row_bytes = a.hidden;
         lalb_tp_range(c, 4, a.n_rank, w.rank, &g0, &g1);
     } else {
         const lalb_layer_weights lw = rk.layers[d.layer];
-        d.kind = p & 3;
         switch (d.kind) {
             case kQkv:
                 d.W = static_cast<const uint8_t *>(lw.wqkv);
                 d.K = a.hidden;
-                d.gamma = lw.attn_norm;
                 break;
             case kO:
                 d.W = static_cast<const uint8_t *>(lw.wo);
@@ -153,7 +170,6 @@ __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const W
             case kGu:
                 d.W = static_cast<const uint8_t *>(lw.wgu);
                 d.K = a.hidden;
-                d.gamma = lw.ffn_norm;
                 break;
             default:
                 d.W = static_cast<const uint8_t *>(lw.wdown);
@@ -162,7 +178,9 @@ __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const W
         }
         d.unit = d.kind == kGu ? 64 : 1;
         d.row_bytes = (d.K >> 8) * 144;
-        lalb_tp_range(c, d.kind, a.n_rank, w.rank, &g0, &g1);
+        // matrix numbers of lalb_tp_range: 0 qkv, 1 o, 2 gate/up, 3 down
+        const int matrix = d.kind == kQkv ? 0 : d.kind == kO ? 1 : d.kind == kGu ? 2 : 3;
+        lalb_tp_range(c, matrix, a.n_rank, w.rank, &g0, &g1);
     }
     d.goff = g0;
     d.rows_total = g1 - g0;
@@ -181,19 +199,32 @@ __device__ __forceinline__ Phase phase_desc(const PersistArgs &a, int p, const W
 // Views of one rank's exchange buffer.
 struct XView {
     unsigned int *gbar, *seq, *ticket;
+    int *pos;
     unsigned long long *best, *keys;
-    float *h, *q;
+    float *h, *q, *att;
+    unsigned int *att_cnt;
+    double *att_part;
     int8_t *aq;
     float *asx;
     int *asumq;
 };
+template <int PPL>
+__device__ __forceinline__ PersistXLayout xlayout(const PersistArgs &a) {
+    return lalb_persist_xlayout(a.n_layer, a.hidden, a.q_rows, a.kv_rows, a.ffn,
+                                PPL == 5 ? a.head_dim : 0);
+}
+template <int PPL>
 __device__ __forceinline__ XView xview(const PersistArgs &a, int rank) {
-    const PersistXLayout L = lalb_persist_xlayout(a.n_layer, a.hidden, a.q_rows, a.ffn);
+    const PersistXLayout L = xlayout<PPL>(a);
     unsigned char *b = a.xb[rank];
     XView v;
     v.gbar = reinterpret_cast<unsigned int *>(b + L.gbar);
     v.seq = reinterpret_cast<unsigned int *>(b + L.seq);
     v.ticket = reinterpret_cast<unsigned int *>(b + L.ticket);
+    v.pos = reinterpret_cast<int *>(b + L.pos);
+    v.att = reinterpret_cast<float *>(b + L.att);
+    v.att_cnt = reinterpret_cast<unsigned int *>(b + L.att_cnt);
+    v.att_part = reinterpret_cast<double *>(b + L.att_part);
     v.best = reinterpret_cast<unsigned long long *>(b + L.best);
     v.keys = reinterpret_cast<unsigned long long *>(b + L.keys);
     v.h = reinterpret_cast<float *>(b + L.h);
@@ -222,6 +253,10 @@ __device__ __forceinline__ void cons_bar() {
     asm volatile("bar.sync 1, %0;" ::"r"(kConsThreads) : "memory");
 }
 
+struct ConsBar {
+    __device__ void operator()() const { cons_bar(); }
+};
+
 // Two-level phase barrier.  Every CTA arrives on its own rank's counter
 // lbar[ph] (GPU scope, release); the CTA whose arrival completes the rank
 // (it sees the count reach its target) acquires and then adds one to rbar[ph] of
@@ -237,11 +272,16 @@ __device__ __forceinline__ void cons_bar() {
 // Phases whose outputs go to other ranks (gate/up, down): their barrier waits
 // for every rank; after qkv and o (computed whole on every rank) a rank only
 // waits for its own CTAs.
-__device__ __forceinline__ bool cross_phase(int ph) { return (ph & 3) >= 2; }
+template <int PPL>
+__device__ __forceinline__ bool cross_phase(const PersistArgs &a, int ph) {
+    const int k = phase_kind<PPL>(a, ph);
+    return k == kGu || k == kDown;
+}
 
+template <int PPL>
 __device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &own, int rank,
                                             int ph, unsigned int seq) {
-    const unsigned int nl = a.cta_per_rank, nr = cross_phase(ph) ? a.n_rank - 1 : 0;
+    const unsigned int nl = a.cta_per_rank, nr = cross_phase<PPL>(a, ph) ? a.n_rank - 1 : 0;
     const unsigned int t_local = (seq + 1u) * nl;
     unsigned int *lbar = own.gbar + ph;
     if (nr == 0) {
@@ -254,7 +294,7 @@ __device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &o
             asm volatile("fence.acq_rel.gpu;" ::: "memory");
             for (int j = 0; j < a.n_rank; ++j) {
                 if (j == rank) continue;
-                unsigned int *ctr = xview(a, j).gbar + 4 * a.n_layer + ph;
+                unsigned int *ctr = xview<PPL>(a, j).gbar + PPL * a.n_layer + ph;
                 if (a.remote)
                     asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
                 else
@@ -264,12 +304,13 @@ __device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &o
     }
 }
 
+template <int PPL>
 __device__ __forceinline__ bool grid_wait(const PersistArgs &a, const XView &own, int ph,
                                           unsigned int seq) {
-    const unsigned int nl = a.cta_per_rank, nr = cross_phase(ph) ? a.n_rank - 1 : 0;
+    const unsigned int nl = a.cta_per_rank, nr = cross_phase<PPL>(a, ph) ? a.n_rank - 1 : 0;
     const unsigned int t_local = (seq + 1u) * nl, t_remote = (seq + 1u) * nr;
     unsigned int *lbar = own.gbar + ph;
-    unsigned int *rbar = own.gbar + 4 * a.n_layer + ph;
+    unsigned int *rbar = own.gbar + PPL * a.n_layer + ph;
     bool ok = true;
     unsigned long long t0 = 0;
     bool local_done = false;
@@ -309,17 +350,18 @@ __device__ __forceinline__ bool grid_wait(const PersistArgs &a, const XView &own
 // The ranks' LM-head keys: each rank's last CTA stored its key into every
 // rank's buffer, then arrives here once per rank (the counter after the
 // phase counters) and waits for all n_rank arrivals of this token.
+template <int PPL>
 __device__ __forceinline__ bool keys_arrive_wait(const PersistArgs &a, const XView &own,
                                                  unsigned int seq) {
     for (int j = 0; j < a.n_rank; ++j) {
-        unsigned int *ctr = xview(a, j).gbar + 8 * a.n_layer;
+        unsigned int *ctr = xview<PPL>(a, j).gbar + 2 * PPL * a.n_layer;
         if (a.remote)
             asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
         else
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
     }
     const unsigned int target = (seq + 1u) * (unsigned int)a.n_rank;
-    unsigned int *kb = own.gbar + 8 * a.n_layer;
+    unsigned int *kb = own.gbar + 2 * PPL * a.n_layer;
     unsigned long long t0 = 0;
     for (uint32_t k = 0;; ++k) {
         unsigned int v;
@@ -391,7 +433,7 @@ struct Cons {
 // of a slot the consumer waits until use u-1 has been consumed: use u-2 was
 // its own chunk (2*kSlots is a multiple of kNC), so both barriers are at
 // most one phase behind and the parity waits cannot match a stale phase.
-template <int KIND>
+template <int KIND, int PPL>
 __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase &d,
                                               uint32_t g_base, const PersistXLayout &XL,
                                               const XView &own, const PersistRank &rk, Cons &cs) {
@@ -560,10 +602,10 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                 const float prev = __shfl_sync(0xffffffffu, pre, (r4 + myrow) & 31);
                 const int lr = r4 + myrow, row = rs + lr, grow = d.goff + row;
                 if ((lane & 7) == 0 && lr < nr) {
-                    // every rank computes all of q and of the residual update, so
-                    // they stay in its own buffer; k and v are not read downstream
-                    // (the attention is out of scope)
-                    if (KIND == kQkv && grow < a.q_rows) own.q[grow] = (float)v;
+                    // every rank computes all of qkv and of the residual update, so
+                    // they stay in its own buffer (k and v are read by the
+                    // attention phase, when there is one)
+                    if (KIND == kQkv && (PPL == 5 || grow < a.q_rows)) own.q[grow] = (float)v;
                     if (KIND == kO) own.h[grow] = __fadd_rn(prev, (float)v);
                     if (KIND == kGu) cs.tile_s[row - d.r0] = (float)v;   // gate/up tile entry
                 }
@@ -604,6 +646,12 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
     }
 }
 
+// PPL (phases per layer) is 4 for the matmul set and 5 with the attention
+// phase; NORM is whether any RMSNorm weight vector is set.  Each combination
+// is its own instantiation, so that the matmul-only kernel with unit norms
+// carries neither the attention code nor the norm weights' registers in its
+// activation prologue (measured: 2-3 % of the token with them).
+template <int PPL, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const PersistArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const Layout L = make_layout();
@@ -620,13 +668,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     uint8_t *slot_s = smem + L.off_slot;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int NP = 4 * a.n_layer + 1;
+    const int NP = PPL * a.n_layer + 1;
     Where w;
     w.rl = blockIdx.x / a.cta_per_rank;
     w.rank = a.rank0 + w.rl;
     w.cb = blockIdx.x % a.cta_per_rank;
-    const PersistXLayout XL = lalb_persist_xlayout(a.n_layer, a.hidden, a.q_rows, a.ffn);
-    const XView own = xview(a, w.rank);
+    const PersistXLayout XL = xlayout<PPL>(a);
+    const XView own = xview<PPL>(a, w.rank);
     const PersistRank &rk = a.rk[w.rl];
 
     if (tid == 0) {
@@ -651,11 +699,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             // streaming while the ring is full across a phase boundary.
             int pf_p = 0, pf_j = 0;
             uint32_t pf_g = 0;
-            Phase pf_d = phase_desc(a, 0, w);
+            Phase pf_d = phase_desc<PPL>(a, 0, w);
             auto prefetch_to = [&](uint32_t g_end) {
                 for (; pf_g < g_end; ++pf_g, ++pf_j) {
                     while (pf_p < NP && pf_j >= pf_d.nchunks) {
-                        if (++pf_p < NP) pf_d = phase_desc(a, pf_p, w);
+                        if (++pf_p < NP) pf_d = phase_desc<PPL>(a, pf_p, w);
                         pf_j = 0;
                     }
                     if (pf_p >= NP) return;
@@ -669,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             prefetch_to(kPrefetchChunks);
             uint32_t g = 0;
             for (int p = 0; p < NP && !dead; ++p) {
-                const Phase d = phase_desc(a, p, w);
+                const Phase d = phase_desc<PPL>(a, p, w);
                 for (int j = 0; j < d.nchunks; ++j, ++g) {
                     if (g % kNP != (uint32_t)warp) continue;
                     const int slot = g % kSlots;
@@ -717,6 +765,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
     // the phase counters grow across tokens: their targets derive from seq
     const unsigned int seq = *(volatile unsigned int *)own.seq;
+    // the decode position of this token (attention); advanced by the rank's
+    // last CTA after every CTA of the rank has read it
+    const int pos = PPL == 5 ? *(volatile int *)own.pos : 0;
 
     for (int p = 0; p < NP; ++p) {
         Phase d;
@@ -734,21 +785,51 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     tr[7] = cs.polls;
                     cs.wait_ns = cs.busy_ns = cs.polls = 0;
                 }
-                grid_arrive(a, own, w.rank, p - 1, seq);
-                d = phase_desc(a, p, w);   // while the arrivals propagate
+                grid_arrive<PPL>(a, own, w.rank, p - 1, seq);
+                d = phase_desc<PPL>(a, p, w);   // while the arrivals propagate
                 // a grid barrier that gives up leaves the rest of the token
                 // to run on whatever data it has: later grid waits give up
                 // at once (the status word is raised), mbarrier waits stay
-                grid_wait(a, own, p - 1, seq);
+                grid_wait<PPL>(a, own, p - 1, seq);
                 if (tr) tr[1] = global_ns();
             } else {
-                d = phase_desc(a, p, w);
+                d = phase_desc<PPL>(a, p, w);
             }
             cons_bar();
         } else {
-            d = phase_desc(a, p, w);
+            d = phase_desc<PPL>(a, p, w);
         }
         const int NS = d.K >> 5;
+
+        if (PPL == 5 && d.kind == kAttn) {
+            // ---- attention over the KV cache: items (q head, position chunk)
+            // over this rank's CTAs; output to own.att ----------------------------
+            if (pos >= 0 && pos < a.max_ctx) {
+                AttnStep st;
+                st.qkv = own.q;
+                st.k_cache = a.kv_cache[2 * d.layer];
+                st.v_cache = a.kv_cache[2 * d.layer + 1];
+                st.out = own.att;
+                st.part = own.att_part;
+                st.cnt = own.att_cnt;
+                st.n_head = a.q_rows / a.head_dim;
+                st.n_kv = a.kv_rows / a.head_dim;
+                st.hd = a.head_dim;
+                st.pos = pos;
+                st.S = attn_chunks(st.n_head, pos, a.cta_per_rank);
+                st.theta = a.rope_theta;
+                attn_items(st, w.cb, a.cta_per_rank, ct, reinterpret_cast<unsigned char *>(xq_s),
+                           ConsBar());
+            } else {
+                // outside the cache: nothing is read or written there
+                if (ct == 0 && w.cb == 0) atomicOr(a.status, LALB_STATUS_BAD_POSITION);
+                for (int i = w.cb * kConsThreads + ct; i < a.q_rows; i += a.cta_per_rank * kConsThreads)
+                    own.att[i] = 0.0f;
+            }
+            if (ct == 0 && a.trace)
+                a.trace[((size_t)blockIdx.x * NP + p) * kTraceFields + 2] = global_ns();
+            continue;
+        }
 
         // ---- the phase's activation in shared memory -------------------------
         if (d.kind == kDown) {
@@ -769,7 +850,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             // one round trip to L2: every thread loads its quads' elements
             // (and their RMSNorm weights), then the RMS scale (sum of squares
             // in double) and the quantizer work from registers
-            const float *src = d.kind == kO ? own.q : ((p == 0) ? a.h_in : own.h);
+            const float *src = d.kind == kO ? (PPL == 5 ? own.att : own.q)
+                                            : ((p == 0) ? a.h_in : own.h);
+            // the prologue's RMSNorm weights (nullable: unit), looked up here
+            // rather than carried through the phase's matvec loops
+            const float *gamma = !NORM ? nullptr
+                                 : d.kind == kQkv ? rk.layers[d.layer].attn_norm
+                                 : d.kind == kGu ? rk.layers[d.layer].ffn_norm
+                                 : d.kind == kHead ? a.out_norm : nullptr;
             const int quad = ct >> 2, qi = ct & 3;
             float v[kPrepPasses][8], gv[kPrepPasses][8];
             double ss = 0.0;
@@ -778,12 +866,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 const int blk = ps * kQuads + quad;
                 if (blk < NS) {
                     load8_cg(src + blk * 32 + 8 * qi, v[ps]);
-                    if (d.gamma) load8_cg(d.gamma + blk * 32 + 8 * qi, gv[ps]);
+                    if (NORM && gamma) load8_cg(gamma + blk * 32 + 8 * qi, gv[ps]);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) ss += (double)v[ps][i] * (double)v[ps][i];
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[ps][i] = gv[ps][i] = 0.0f;
+                    for (int i = 0; i < 8; ++i) {
+                        v[ps][i] = 0.0f;
+                        if (NORM) gv[ps][i] = 0.0f;
+                    }
                 }
             }
             if (d.kind != kO) {
@@ -802,7 +893,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         v[ps][i] = __fmul_rn(v[ps][i], scale);
-                        if (d.gamma) v[ps][i] = __fmul_rn(v[ps][i], gv[ps][i]);
+                        if (NORM && gamma) v[ps][i] = __fmul_rn(v[ps][i], gv[ps][i]);
                     }
             }
 #pragma unroll
@@ -818,11 +909,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         if (ct == 0 && a.trace) a.trace[((size_t)blockIdx.x * NP + p) * kTraceFields + 2] = global_ns();
 
         switch (d.kind) {
-            case kQkv: consume_phase<kQkv>(a, d, g_base, XL, own, rk, cs); break;
-            case kO: consume_phase<kO>(a, d, g_base, XL, own, rk, cs); break;
-            case kGu: consume_phase<kGu>(a, d, g_base, XL, own, rk, cs); break;
-            case kDown: consume_phase<kDown>(a, d, g_base, XL, own, rk, cs); break;
-            default: consume_phase<kHead>(a, d, g_base, XL, own, rk, cs); break;
+            case kQkv: consume_phase<kQkv, PPL>(a, d, g_base, XL, own, rk, cs); break;
+            case kO: consume_phase<kO, PPL>(a, d, g_base, XL, own, rk, cs); break;
+            case kGu: consume_phase<kGu, PPL>(a, d, g_base, XL, own, rk, cs); break;
+            case kDown: consume_phase<kDown, PPL>(a, d, g_base, XL, own, rk, cs); break;
+            default: consume_phase<kHead, PPL>(a, d, g_base, XL, own, rk, cs); break;
         }
         g_base += d.nchunks;
     }
@@ -888,9 +979,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 unsigned long long kmax = key;
                 bool ok = true;
                 if (a.n_rank > 1) {
-                    for (int j = 0; j < a.n_rank; ++j) xview(a, j).keys[w.rank] = key;
+                    for (int j = 0; j < a.n_rank; ++j) xview<PPL>(a, j).keys[w.rank] = key;
                     __threadfence_system();
-                    ok = keys_arrive_wait(a, own, seq);
+                    ok = keys_arrive_wait<PPL>(a, own, seq);
                     kmax = 0;
                     for (int j = 0; j < a.n_rank; ++j) {
                         const unsigned long long kj = __ldcg(own.keys + j);
@@ -900,6 +991,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 if (a.argmax && w.rl == 0)
                     *a.argmax = ok && kmax ? (int32_t)(0xFFFFFFFFu - (uint32_t)(kmax & 0xFFFFFFFFull)) : -1;
                 *own.ticket = 0u;
+                if (PPL == 5) *own.pos = pos + 1;   // every CTA of the rank read pos
                 __threadfence();
                 atomicAdd(own.seq, 1u);   // the next token's counter targets
             }
@@ -914,8 +1006,12 @@ int lalb_persist_max_tiles() { return kMaxTiles; }
 
 int lalb_launch_persist(lalb_ctx *ctx, const PersistArgs &a, cudaStream_t stream) {
     const Layout L = make_layout();
+    const void *fn = a.ppl == 5 ? (a.norm ? (const void *)decode_persistent_kernel<5, true>
+                                          : (const void *)decode_persistent_kernel<5, false>)
+                                : (a.norm ? (const void *)decode_persistent_kernel<4, true>
+                                          : (const void *)decode_persistent_kernel<4, false>);
     {
-        const int st = lalb_set_smem_attr(ctx, (const void *)decode_persistent_kernel, (int)L.total);
+        const int st = lalb_set_smem_attr(ctx, fn, (int)L.total);
         if (st) return st;
     }
     cudaLaunchConfig_t cfg = {};
@@ -930,6 +1026,6 @@ int lalb_launch_persist(lalb_ctx *ctx, const PersistArgs &a, cudaStream_t stream
     cfg.numAttrs = 1;
     PersistArgs args = a;
     void *params[] = {&args};
-    LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, (const void *)decode_persistent_kernel, params));
+    LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, fn, params));
     return LALB_OK;
 }

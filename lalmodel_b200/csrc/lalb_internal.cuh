@@ -57,6 +57,7 @@ int lalb_cuda_fail(lalb_ctx *ctx, cudaError_t e, const char *what);
 
 // status word bits
 #define LALB_STATUS_WAIT_TIMEOUT 1u
+#define LALB_STATUS_BAD_POSITION 2u   // a decode position outside the KV cache
 
 // Bound on every wait: LALB_SPIN_LIMIT tries.  An mbarrier try_wait sleeps
 // until the phase completes or LALB_WAIT_HINT_NS passes, so a wait that can

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include "lalb.h"
+#include "lalb_attention.cuh"
 
 // activation input of a matvec
 enum : int {
@@ -70,6 +71,15 @@ int lalb_launch_q4k_gemv(lalb_ctx *ctx, const Q4kGemvArgs &a, int in, int epi,
 int lalb_launch_q8_head(lalb_ctx *ctx, const Q8HeadArgs &a, int in, cudaStream_t stream,
                         bool pdl, int ctas_per_sm);
 
+// Decode attention (lalb_attention.cu): shape check, the standalone kernel
+// (ctas CTAs; the position from *pos_ptr when given) and the kernel that
+// advances a decoder's position word after a token.
+int lalb_attention_check(int n_head, int n_kv, int hd);
+int lalb_launch_attention(lalb_ctx *ctx, const lalb::AttnStep &a, const int *pos_ptr, int max_ctx,
+                          int ctas, cudaStream_t s);
+int lalb_launch_advance_position(lalb_ctx *ctx, int *pos, cudaStream_t s);
+int lalb_launch_set_position(lalb_ctx *ctx, int *pos, int value, cudaStream_t s);
+
 // One decode token in a single persistent, cooperative kernel, optionally
 // tensor-parallel over n_rank GPUs.  Every rank holds a contiguous shard of
 // the rows of gate/up, down and the LM head, all rows of qkv and o
@@ -87,6 +97,11 @@ struct PersistRank {                    // one rank's weight shards (device)
 
 struct PersistArgs {
     int n_layer, hidden, q_rows, kv_rows, ffn, vocab;
+    int ppl;                            // phases per layer: 4, or 5 with attention
+    int norm;                           // nonzero: some RMSNorm weight vector is set
+    int head_dim, max_ctx;              // attention (ppl == 5)
+    double rope_theta;
+    float *const *kv_cache;             // attention: [n_layer][2] (k, v) cache pointers
     int n_rank;                         // ranks in total (1: one GPU holds every row)
     int rank0, ranks_here;              // the ranks this launch computes, one CTA group each
     int cta_per_rank;                   // CTAs per rank (equal on every rank)
@@ -106,32 +121,42 @@ struct PersistArgs {
 
 // Layout of one rank's exchange buffer (byte offsets; identical on every rank).
 struct PersistXLayout {
-    size_t gbar;      // u32 [4*n_layer]: this rank's CTAs done with each phase (monotonic
-                      //   across tokens), then u32 [4*n_layer]: other ranks done (one
+    size_t gbar;      // u32 [ppl*n_layer]: this rank's CTAs done with each phase (monotonic
+                      //   across tokens), then u32 [ppl*n_layer]: other ranks done (one
                       //   arrival per rank per phase), then u32: ranks' LM-head keys in
     size_t seq;       // u32: tokens completed by this rank
     size_t ticket;    // u32: this rank's CTAs done with the LM head (reset per token)
+    size_t pos;       // i32: decode position (attention), advanced after every token
     size_t best;      // u64: this rank's argmax key (reset per token)
     size_t keys;      // u64 [kPersistMaxRanks]: every rank's argmax key for the token
     size_t h;         // f32 [hidden]: residual stream
-    size_t q;         // f32 [q_rows]
+    size_t q;         // f32 [q_rows + 2*kv_rows]: the qkv projection
+    size_t att;       // f32 [q_rows]: attention output
+    size_t att_cnt;   // u32 [n_head]: attention chunk arrivals (0 between phases)
+    size_t att_part;  // f64 [n_head][8][head_dim + 2]: attention chunk partials
     size_t aq;        // i8  [ffn]: quantized SwiGLU product
     size_t asx;       // f32 [ffn/32]
     size_t asumq;     // i32 [ffn/32]
     size_t total;
 };
 __host__ __device__ inline PersistXLayout lalb_persist_xlayout(int n_layer, int hidden, int q_rows,
-                                                               int ffn) {
+                                                               int kv_rows, int ffn, int head_dim) {
     auto up = [](size_t v) { return (v + 127) / 128 * 128; };
+    const int ppl = head_dim > 0 ? 5 : 4;
+    const int n_head = head_dim > 0 ? q_rows / head_dim : 0;
     PersistXLayout L;
     L.gbar = 0;
-    L.seq = up((size_t)(8 * n_layer + 1) * 4);
+    L.seq = up((size_t)(2 * ppl * n_layer + 1) * 4);
     L.ticket = L.seq + 4;
-    L.best = L.seq + 8;
+    L.pos = L.seq + 8;
+    L.best = L.seq + 16;
     L.keys = L.seq + 128;
     L.h = L.keys + 128;
     L.q = L.h + up((size_t)hidden * 4);
-    L.aq = L.q + up((size_t)q_rows * 4);
+    L.att = L.q + up((size_t)(q_rows + 2 * kv_rows) * 4);
+    L.att_cnt = L.att + up((size_t)(head_dim > 0 ? q_rows : 0) * 4);
+    L.att_part = L.att_cnt + up((size_t)n_head * 4);
+    L.aq = L.att_part + up((size_t)n_head * 8 * (head_dim + 2) * 8);
     L.asx = L.aq + up((size_t)ffn);
     L.asumq = L.asx + up((size_t)(ffn / 32) * 4);
     L.total = L.asumq + up((size_t)(ffn / 32) * 4);

@@ -345,6 +345,150 @@ void lalb_o_swiglu(const float *gate, const float *up, int n, float *act) {
     }
 }
 
+/* apply_rope (runtime/lal_runtime.c:137-153) on one head, in double */
+static void rope_head(float *x, int hd, int pos, double theta) {
+    const int half = hd / 2;
+    for (int d = 0; d < half; d++) {
+        const double a = (double)pos * pow(theta, -(double)(2 * d) / (double)hd);
+        const double c = cos(a), s = sin(a);
+        const double x0 = x[d], x1 = x[d + half];
+        x[d] = (float)(x0 * c - x1 * s);
+        x[d + half] = (float)(x0 * s + x1 * c);
+    }
+}
+
+/* attention_forward (runtime/lal_runtime.c:833-882) with RoPE and grouped
+ * KV heads; see lalb_oracle.h. */
+void lalb_o_attention_decode(const float *qkv, int n_head, int n_kv, int hd, int pos,
+                             float theta, float *k_cache, float *v_cache, float *out) {
+    const int qr = n_head * hd, kvr = n_kv * hd, group = n_head / n_kv;
+    float *q = (float *)malloc(sizeof(float) * (size_t)qr);
+    double *sc = (double *)malloc(sizeof(double) * (size_t)(pos + 1));
+    memcpy(q, qkv, sizeof(float) * (size_t)qr);
+    for (int h = 0; h < n_head; h++) rope_head(q + (size_t)h * hd, hd, pos, theta);
+    float *krow = k_cache + (size_t)pos * kvr, *vrow = v_cache + (size_t)pos * kvr;
+    memcpy(krow, qkv + qr, sizeof(float) * (size_t)kvr);
+    memcpy(vrow, qkv + qr + kvr, sizeof(float) * (size_t)kvr);
+    for (int g = 0; g < n_kv; g++) rope_head(krow + (size_t)g * hd, hd, pos, theta);
+    const double scale = 1.0 / sqrt((double)hd);
+    for (int h = 0; h < n_head; h++) {
+        const int g = h / group;
+        const float *qh = q + (size_t)h * hd;
+        double mx = -INFINITY;
+        for (int j = 0; j <= pos; j++) {
+            const float *kj = k_cache + (size_t)j * kvr + (size_t)g * hd;
+            double dot = 0.0;
+            for (int d = 0; d < hd; d++) dot += (double)qh[d] * (double)kj[d];
+            sc[j] = dot * scale;
+            if (sc[j] > mx) mx = sc[j];
+        }
+        double sum = 0.0;
+        for (int j = 0; j <= pos; j++) {
+            sc[j] = exp(sc[j] - mx);
+            sum += sc[j];
+        }
+        const double inv = 1.0 / (sum + 1e-12);
+        for (int d = 0; d < hd; d++) {
+            double acc = 0.0;
+            for (int j = 0; j <= pos; j++)
+                acc += sc[j] * (double)v_cache[(size_t)j * kvr + (size_t)g * hd + d];
+            out[(size_t)h * hd + d] = (float)(acc * inv);
+        }
+    }
+    free(q);
+    free(sc);
+}
+
+/* generate_text's sampling (models/ste_train.c:2229-2318); see lalb_oracle.h */
+int lalb_o_sample(const float *logits, int vocab, const int32_t *history, int n_hist,
+                  float temp, int top_k, float top_p, float rep, int ngram, int n_mask,
+                  float u, int tie_rule, int32_t *idx_out, float *prob_out) {
+    float *adj = (float *)malloc(sizeof(float) * (size_t)vocab);
+    char *seen = (char *)calloc((size_t)vocab, 1);
+    memcpy(adj, logits, sizeof(float) * (size_t)vocab);
+    for (int i = 0; i < n_mask && i < vocab; i++) adj[i] = -1e30f;
+    for (int j = 0; j < n_hist; j++) {               /* :2254-2264, once per token */
+        const int t = history[j];
+        if (t >= 0 && t < vocab && !seen[t]) {
+            volatile float a = adj[t];
+            adj[t] = a > 0 ? a / rep : a * rep;
+            seen[t] = 1;
+        }
+    }
+    if (ngram >= 2 && n_hist >= ngram - 1) {          /* :2270-2281 for ngram = 3 */
+        const int m = ngram - 1;
+        for (int j = 0; j + m < n_hist; j++) {
+            int match = 1;
+            for (int q = 0; q < m && match; q++)
+                match = history[j + q] == history[n_hist - m + q];
+            if (match) {
+                const int banned = history[j + m];
+                if (banned >= 0 && banned < vocab) adj[banned] = -1e30f;
+            }
+        }
+    }
+    int token;
+    if (temp <= 0.01f) {                              /* sample_argmax, :1503-1509 */
+        token = 0;
+        for (int i = 1; i < vocab; i++)
+            if (adj[i] > adj[token]) token = i;
+        if (idx_out) idx_out[0] = token;
+        if (prob_out) prob_out[0] = 1.0f;
+    } else {
+        const int k = top_k < vocab ? top_k : vocab;
+        int *ind = (int *)malloc(sizeof(int) * (size_t)vocab);
+        float *pr = (float *)malloc(sizeof(float) * (size_t)k);
+        for (int j = 0; j < vocab; j++) ind[j] = j;
+        for (int j = 0; j < k; j++) {
+            int best = j;
+            for (int q = j + 1; q < vocab; q++) {
+                const float a = adj[ind[q]], b = adj[ind[best]];
+                if (a > b || (tie_rule == 0 && a == b && ind[q] < ind[best])) best = q;
+            }
+            const int tmp = ind[j];
+            ind[j] = ind[best];
+            ind[best] = tmp;
+        }
+        const float mx = adj[ind[0]];
+        float sum = 0.0f;
+        for (int j = 0; j < k; j++) {
+            volatile float d = adj[ind[j]] - mx;
+            volatile float x = d / temp;
+            pr[j] = (float)exp((double)x);
+            sum += pr[j];
+        }
+        const float thresh = top_p * sum;
+        int p_limit = k;
+        float cum = 0.0f;
+        for (int j = 0; j < k; j++) {
+            cum += pr[j];
+            if (cum > thresh) {
+                p_limit = j + 1;
+                break;
+            }
+        }
+        const float r = u * cum;
+        token = ind[0];
+        float c2 = 0.0f;
+        for (int j = 0; j < p_limit; j++) {
+            c2 += pr[j];
+            if (r < c2) {
+                token = ind[j];
+                break;
+            }
+        }
+        for (int j = 0; j < k; j++) {
+            if (idx_out) idx_out[j] = ind[j];
+            if (prob_out) prob_out[j] = pr[j];
+        }
+        free(ind);
+        free(pr);
+    }
+    free(adj);
+    free(seen);
+    return token;
+}
+
 /* rms_norm, runtime/lal_runtime.c:82-87 (the scale's sum of squares in
  * double instead of float; see lalb_oracle.h). */
 void lalb_o_rms_norm(const float *x, const float *w, int n, float eps, float *out) {

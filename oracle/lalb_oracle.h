@@ -101,6 +101,41 @@ void lalb_o_swiglu(const float *gate, const float *up, int n, float *act);
  * of the (nearly) exact value and does not depend on summation order. */
 void lalb_o_rms_norm(const float *x, const float *w, int n, float eps, float *out);
 
+/* One decode step of causal attention for one layer, after apply_rope
+ * (runtime/lal_runtime.c:137-153) and attention_forward (:833-882),
+ * generalised to grouped KV heads.  qkv = q [n_head*hd] | k [n_kv*hd] |
+ * v [n_kv*hd]; the caches are [max_ctx][n_kv*hd].
+ *   RoPE at position pos on every q and k head, pairs (d, d + hd/2):
+ *     a = pos * theta^(-2d/hd); (x0, x1) -> (x0 c - x1 s, x0 s + x1 c),
+ *     in double, each result rounded to float once;
+ *   k_cache[pos] = rotated k, v_cache[pos] = v;
+ *   head h reads KV head g = h / (n_head / n_kv): for j = 0..pos
+ *     s_j = (q_h . k_j) / sqrt(hd), w_j = exp(s_j - max s) / (sum + 1e-12),
+ *     out_h = sum_j w_j v_j, everything in double, rounded to float once.
+ * The reference computes the angle, cos/sin and sums in float. */
+void lalb_o_attention_decode(const float *qkv, int n_head, int n_kv, int hd, int pos,
+                             float theta, float *k_cache, float *v_cache, float *out);
+
+/* Next-token sampling after the LM head, after generate_text
+ * (models/ste_train.c:2229-2318) and sample_argmax (:1503-1509):
+ *   adjusted = logits; ids < n_mask -> -1e30;
+ *   every distinct token of history (once): adjusted /= rep if > 0, else *= rep;
+ *   ngram >= 2: every token t such that history[-(ngram-1):] + [t] already
+ *   occurs in history -> -1e30 (the reference: ngram = 3);
+ *   temp <= 0.01: the first maximum (sample_argmax);
+ *   else the top_k largest (value descending; ties: tie_rule 0 = lower index
+ *   first, 1 = the reference's selection sort, :2286-2297), p_j =
+ *   (float)exp((double)((a_j - a_0) / temp)) (float subtraction and
+ *   division, the exponential rounded once), cumulative float sums: the
+ *   nucleus ends at the first j whose running sum exceeds top_p * sum;
+ *   r = u * (that running sum); the token is the first j of the nucleus with
+ *   r < running sum (index 0 if none).
+ * idx/prob (nullable, top_k entries) receive the ranked ids and p_j.
+ * Returns the token. */
+int lalb_o_sample(const float *logits, int vocab, const int32_t *history, int n_hist,
+                  float temp, int top_k, float top_p, float rep, int ngram, int n_mask,
+                  float u, int tie_rule, int32_t *idx, float *prob);
+
 /* --- seed STE model, per-element CORE/BINARY/PRUNE int8 encoding --------- */
 /* state[i] (0 CORE, 1 BINARY, 2 PRUNE) and w[i] (fp32) per weight, W [rows][K].
  * Per row j:  amax = max |w| over CORE entries, alpha = mean |w| over BINARY

@@ -31,6 +31,9 @@ _SIG = {
     "lalb_o_argmax": (c_int, [P, c_int]),
     "lalb_o_swiglu": (None, [P, P, c_int, P]),
     "lalb_o_rms_norm": (None, [P, P, c_int, c_float, P]),
+    "lalb_o_attention_decode": (None, [P, c_int, c_int, c_int, c_int, c_float, P, P, P]),
+    "lalb_o_sample": (c_int, [P, c_int, P, c_int, c_float, c_int, c_float, c_float, c_int, c_int,
+                              c_float, c_int, P, P]),
     "lalb_o_logic_state": (None, [c_u64, c_size_t, c_float, c_float, P]),
     "lalb_o_logic_pack": (None, [P, P, c_int, c_int, P, P]),
     "lalb_o_logic_forward": (None, [P, P, P, c_int, c_int, P, c_int, P]),
@@ -146,19 +149,56 @@ def rms_normalise(x, w=None, eps=1e-5):
     return out
 
 
-def decode_chain(layers, lm_q, lm_s, h_in, cfg, out_norm=None):
+def attention_decode(qkv, n_head, n_kv, hd, pos, k_cache, v_cache, theta=10000.0):
+    """One layer's decode attention at position pos (C oracle,
+    lalb_o_attention_decode): writes row pos of the caches (float32 arrays
+    [max_ctx][n_kv*hd], modified in place) and returns out [n_head*hd]."""
+    qkv = np.ascontiguousarray(qkv, np.float32).reshape(-1)
+    assert k_cache.flags.c_contiguous and v_cache.flags.c_contiguous
+    assert k_cache.dtype == np.float32 and v_cache.dtype == np.float32
+    out = np.empty(n_head * hd, np.float32)
+    lib().lalb_o_attention_decode(_p(qkv), n_head, n_kv, hd, pos, theta, _p(k_cache),
+                                  _p(v_cache), _p(out))
+    return out
+
+
+def sample(logits, history=(), temperature=0.0, top_k=1, top_p=0.9, rep_penalty=1.0,
+           no_repeat_ngram=0, n_masked_low_ids=0, u=0.0, tie_rule=0):
+    """generate_text's sampling on the CPU (lalb_o_sample): returns (token,
+    ranked ids, p_j); tie_rule 1 is the reference's selection sort."""
+    logits = np.ascontiguousarray(logits, np.float32).reshape(-1)
+    hist = np.ascontiguousarray(np.asarray(history, np.int32).reshape(-1))
+    k = min(top_k, logits.size)
+    idx = np.empty(k, np.int32)
+    prob = np.empty(k, np.float32)
+    tok = lib().lalb_o_sample(_p(logits), logits.size, _p(hist) if hist.size else None, hist.size,
+                              temperature, top_k, top_p, rep_penalty, no_repeat_ngram,
+                              n_masked_low_ids, u, tie_rule, _p(idx), _p(prob))
+    return tok, idx, prob
+
+
+def decode_chain(layers, lm_q, lm_s, h_in, cfg, out_norm=None, kv=None, pos=0):
     """The decoder's per-token math on the CPU (see include/lalb.h).
 
     layers: list of dicts with Q4_K byte arrays wqkv, wo, wgu, wdown and
     optional RMSNorm weights attn_norm, ffn_norm; cfg["rms_eps"] (default
-    1e-5) is the norm epsilon.  Returns (h_final, logits, argmax)."""
-    hid, q_rows, kv, ffn = cfg["hidden"], cfg["q_rows"], cfg["kv_rows"], cfg["ffn"]
+    1e-5) is the norm epsilon.  With cfg["head_dim"] > 0 the attention runs
+    at position pos over kv, a list of per-layer (k_cache, v_cache) float32
+    arrays [max_ctx][kv_rows] that are updated in place (row pos).
+    Returns (h_final, logits, argmax)."""
+    hid, q_rows, kvr, ffn = cfg["hidden"], cfg["q_rows"], cfg["kv_rows"], cfg["ffn"]
     eps = cfg.get("rms_eps", 0.0) or 1e-5
+    hd = cfg.get("head_dim", 0)
+    theta = cfg.get("rope_theta", 0.0) or 10000.0
     h = np.array(h_in, np.float32)
-    for lw in layers:
+    for li, lw in enumerate(layers):
         xq, sx, sq = quantize_act(rms_normalise(h, lw.get("attn_norm"), eps))
-        qkv, _ = q4k_matmul(lw["wqkv"], q_rows + 2 * kv, hid, xq, sx, sq)
-        q = qkv[0, :q_rows]
+        qkv, _ = q4k_matmul(lw["wqkv"], q_rows + 2 * kvr, hid, xq, sx, sq)
+        if hd > 0:
+            kc, vc = kv[li]
+            q = attention_decode(qkv[0], q_rows // hd, kvr // hd, hd, pos, kc, vc, theta)
+        else:
+            q = qkv[0, :q_rows]
         xq, sx, sq = quantize_act(q)
         o, _ = q4k_matmul(lw["wo"], hid, q_rows, xq, sx, sq)
         h = (h + o[0]).astype(np.float32)

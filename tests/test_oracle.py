@@ -166,6 +166,78 @@ def test_rms_norm_oracle_pinned_to_reference():
     assert np.array_equal(O.rms_normalise(x), O.rms_normalise(x, np.ones_like(x)))
 
 
+def test_attention_oracle_pinned_to_reference():
+    """The oracle's decode attention with n_kv = n_head (the reference's
+    multi-head case) against the reference's apply_rope + attention_forward
+    (tests/golden/decode_ref.npz).  The reference forms the RoPE angle and
+    the softmax in float, the oracle in double: they agree to ~1e-5."""
+    g = np.load(os.path.join(GOLD, "decode_ref.npz"))
+    for i in range(5):
+        n_embd, n_head, pos = (int(v) for v in g[f"att{i}_shape"])
+        hd = n_embd // n_head
+        kc = np.zeros((pos + 1, n_embd), np.float32)
+        vc = np.zeros((pos + 1, n_embd), np.float32)
+        kc[:pos], vc[:pos] = g[f"att{i}_k_in"][:pos], g[f"att{i}_v_in"][:pos]
+        out = O.attention_decode(g[f"att{i}_qkv"], n_head, n_head, hd, pos, kc, vc)
+        assert O.normwise_rel_err(out, g[f"att{i}_out"]) < 1e-4, i
+        assert O.normwise_rel_err(kc[pos], g[f"att{i}_k_row"]) < 1e-5, i
+        assert np.array_equal(vc[pos], g[f"att{i}_v_row"]), i
+        # the rotated q/k the reference attended with
+        q_ref = g[f"att{i}_qkv_rope"][:n_embd]
+        assert q_ref.shape[0] == n_embd
+    # grouped KV heads: every head of a group attends the same cache rows
+    rng = np.random.default_rng(3)
+    n_head, n_kv, hd, pos = 8, 2, 64, 9
+    qkv = rng.standard_normal((n_head + 2 * n_kv) * hd).astype(np.float32)
+    kc = rng.standard_normal((pos + 1, n_kv * hd)).astype(np.float32)
+    vc = rng.standard_normal((pos + 1, n_kv * hd)).astype(np.float32)
+    out = O.attention_decode(qkv, n_head, n_kv, hd, pos, kc.copy(), vc.copy())
+    # head 5 is in group 1: the same as a one-head, one-KV-head call on its slices
+    q5 = qkv[5 * hd:6 * hd]
+    k1 = qkv[n_head * hd + hd:n_head * hd + 2 * hd]
+    v1 = qkv[(n_head + n_kv) * hd + hd:(n_head + n_kv) * hd + 2 * hd]
+    out5 = O.attention_decode(np.concatenate([q5, k1, v1]), 1, 1, hd, pos,
+                              np.ascontiguousarray(kc[:, hd:]), np.ascontiguousarray(vc[:, hd:]))
+    assert np.array_equal(out[5 * hd:6 * hd], out5)
+
+
+def test_sampling_oracle_known_answers():
+    """generate_text's sampling (models/ste_train.c:2229-2318), cases worked
+    out by hand from the reference code (it cannot be called on its own: it
+    lives inside the trainer's generation loop)."""
+    # greedy: the first maximum (sample_argmax, :1503-1509)
+    assert O.sample([1, 3, 3, 2])[0] == 1
+    # the special ids are masked (:2243-2245)
+    assert O.sample([9, 9, 9, 1, 2], n_masked_low_ids=3)[0] == 4
+    # repetition penalty once per distinct token (:2254-2264): 2/1.5 < 1.9
+    assert O.sample([2.0, 1.9, -1.0, -1.2], history=[0, 0, 3], rep_penalty=1.5)[0] == 1
+    tok, _, _ = O.sample([-1.0, -1.1], history=[0], rep_penalty=1.5)   # -1 * 1.5 < -1.1
+    assert tok == 1
+    # no-repeat trigram (:2270-2281): (5, 6) was followed by 7 once
+    lg = np.zeros(10, np.float32)
+    lg[7], lg[3] = 5.0, 4.0
+    assert O.sample(lg, history=[5, 6, 7, 5, 6], no_repeat_ngram=3)[0] == 3
+    assert O.sample(lg, history=[5, 6, 7, 5, 6], no_repeat_ngram=0)[0] == 7
+    # top-k / top-p (:2283-2318): probabilities 1, .75, .5, .25 (ids 3, 2, 1, 0)
+    lg = np.log(np.array([1, 2, 3, 4], np.float32))
+    tok, idx, prob = O.sample(lg, temperature=1.0, top_k=4, top_p=0.5, u=0.5)
+    assert list(idx) == [3, 2, 1, 0] and np.allclose(prob, [1, .75, .5, .25], rtol=1e-6)
+    assert tok == 3          # nucleus {3, 2}: running sum 1.75, r = 0.875 < 1
+    assert O.sample(lg, temperature=1.0, top_k=4, top_p=0.5, u=0.9)[0] == 2   # r = 1.575
+    assert O.sample(lg, temperature=1.0, top_k=4, top_p=1.0, u=0.5)[0] == 2   # r = 1.25
+    assert O.sample(lg, temperature=1.0, top_k=2, top_p=1.0, u=0.99)[0] == 2
+    # ties: lower id first here; the reference's selection sort reorders them
+    t = np.array([5, 9, 5, 9], np.float32)
+    assert list(O.sample(t, temperature=1.0, top_k=4, tie_rule=0)[1]) == [1, 3, 0, 2]
+    assert list(O.sample(t, temperature=1.0, top_k=4, tie_rule=1)[1]) == [1, 3, 2, 0]
+    # distinct values: both rules agree
+    r = np.random.default_rng(0).standard_normal(1000).astype(np.float32)
+    for k in (1, 8, 50):
+        a = O.sample(r, temperature=0.7, top_k=k, u=0.3, tie_rule=0)
+        b = O.sample(r, temperature=0.7, top_k=k, u=0.3, tie_rule=1)
+        assert a[0] == b[0] and np.array_equal(a[1], b[1]) and np.array_equal(a[2], b[2])
+
+
 def test_decode_chain_oracle_small():
     cfg = dict(hidden=256, q_rows=256, kv_rows=64, ffn=512)
     layers = []
