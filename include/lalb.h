@@ -405,6 +405,68 @@ LALB_API int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *packed, int row
                                       const float *X, int T, void *ws, float *Y,
                                       lalb_stream stream);
 
+/* ---- weight blobs: one file of named tensors, written and loaded here ----
+ * The reference ships its 7B weights pre-converted in one file
+ * (prebuilt/qwen7b_q4k_weights.bin from scripts/convert_qwen7b_q4k.py,
+ * README.md:18-20,154; neither is in its snapshot) and loads fp32 tensor
+ * files with tensor_load_all (runtime/lal_runtime.c:2798-2822).  This blob
+ * format is our own, version 1: a 64-byte header ("LQ4K", version,
+ * count, alignment 4096, table offset and size, file size), each tensor's
+ * bytes on a 4096-byte boundary, and a table of 128-byte entries at the end
+ * (key of at most 71 bytes, dtype, up to 3 dims, offset, size, FNV-1a-64
+ * checksum).  A 2-D tensor is row-major, so a row range is one byte range.
+ * Every call returns LALB_ERR_INVALID on a malformed file or argument. */
+enum {
+    LALB_DT_F32 = 0,
+    LALB_DT_Q4K = 1,   /* dims [rows, K], K % 256 == 0: rows * K/256 * 144 bytes */
+    LALB_DT_I8 = 2,
+    LALB_DT_F16 = 3,
+    LALB_DT_BF16 = 4
+};
+typedef struct {
+    char key[72];
+    int dtype;
+    int ndim;
+    uint64_t dims[3];
+    uint64_t bytes;      /* whole tensor */
+    uint64_t row_bytes;  /* bytes / dims[0] */
+} lalb_blob_tensor;
+
+typedef struct lalb_blob_writer lalb_blob_writer;
+LALB_API int lalb_blob_writer_open(const char *path, lalb_blob_writer **out);
+/* Host bytes of a tensor as they are (the key must be new). */
+LALB_API int lalb_blob_writer_add(lalb_blob_writer *w, const char *key, int dtype, int ndim,
+                                  const uint64_t *dims, const void *data);
+/* The converter: host weights [rows][K] in src_dtype (LALB_DT_F32 or
+ * LALB_DT_BF16) quantized on ctx's GPU by lalb_q4k_quantize (dtype
+ * LALB_DT_Q4K) or lalb_q8_quantize_rows (dtype LALB_DT_I8: the int8 rows
+ * under key, their fp32 scales under scale_key), then written. */
+LALB_API int lalb_blob_writer_add_quantized(lalb_ctx *ctx, lalb_blob_writer *w, const char *key,
+                                            const char *scale_key, int dtype, int src_dtype,
+                                            const void *host, int rows, int K);
+/* Writes the header and table; the file is complete only after this. */
+LALB_API int lalb_blob_writer_close(lalb_blob_writer *w);
+
+typedef struct lalb_blob lalb_blob;
+LALB_API int lalb_blob_open(const char *path, lalb_blob **out);
+LALB_API int lalb_blob_close(lalb_blob *b);
+LALB_API int lalb_blob_count(const lalb_blob *b);
+/* Index of the tensor named key, or LALB_ERR_INVALID. */
+LALB_API int lalb_blob_find(const lalb_blob *b, const char *key);
+LALB_API int lalb_blob_info(const lalb_blob *b, int index, lalb_blob_tensor *info);
+/* Recomputes the tensor's checksum from the file: LALB_OK if it matches. */
+LALB_API int lalb_blob_verify(const lalb_blob *b, int index);
+/* Rows [row0, row1) of tensor `index` into host memory. */
+LALB_API int lalb_blob_read_host(const lalb_blob *b, int index, uint64_t row0, uint64_t row1,
+                                 void *dst);
+/* Rows [row0, row1) of tensor `index` into caller-owned device memory dst
+ * (a tensor-parallel rank loads its shard), through two 32 MB pinned
+ * staging buffers that the blob allocates on its first load (one device per
+ * blob): the file read of one chunk overlaps the copy of the previous one on
+ * `stream`.  Returns when the last copy has finished. */
+LALB_API int lalb_blob_load(lalb_ctx *ctx, lalb_blob *b, int index, uint64_t row0, uint64_t row1,
+                            void *dst, lalb_stream stream);
+
 /* ---- the seed STE model's forward matmuls (tensor cores) -----------------
  * A BinLayer (runtime/lal_runtime.h:171-197) with one CORE (0) / BINARY (1)
  * / PRUNE (2) state per output row.  Built like bin_layer_init_logic

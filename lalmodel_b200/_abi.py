@@ -29,6 +29,11 @@ class LayerWeights(ctypes.Structure):
                 ("ffn_norm", P)]
 
 
+class BlobTensor(ctypes.Structure):
+    _fields_ = [("key", ctypes.c_char * 72), ("dtype", c_int), ("ndim", c_int),
+                ("dims", c_uint64 * 3), ("bytes", c_uint64), ("row_bytes", c_uint64)]
+
+
 class Sampling(ctypes.Structure):
     _fields_ = [("temperature", c_float), ("top_k", c_int), ("top_p", c_float),
                 ("rep_penalty", c_float), ("no_repeat_ngram", c_int), ("n_masked_low_ids", c_int)]
@@ -61,6 +66,19 @@ SIGNATURES = {
     "lalb_decoder_position": (c_int, [P]),
     "lalb_attention_decode": (c_int, [P, P, c_int, c_int, c_int, c_int, c_int, c_float, P, P, P, P]),
     "lalb_sample_ws_bytes": (c_int, [c_int, c_int, ctypes.POINTER(c_size_t)]),
+    "lalb_blob_writer_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(P)]),
+    "lalb_blob_writer_add": (c_int, [P, ctypes.c_char_p, c_int, c_int, ctypes.POINTER(c_uint64), P]),
+    "lalb_blob_writer_add_quantized": (c_int, [P, P, ctypes.c_char_p, ctypes.c_char_p, c_int, c_int,
+                                               P, c_int, c_int]),
+    "lalb_blob_writer_close": (c_int, [P]),
+    "lalb_blob_open": (c_int, [ctypes.c_char_p, ctypes.POINTER(P)]),
+    "lalb_blob_close": (c_int, [P]),
+    "lalb_blob_count": (c_int, [P]),
+    "lalb_blob_find": (c_int, [P, ctypes.c_char_p]),
+    "lalb_blob_info": (c_int, [P, c_int, ctypes.POINTER(BlobTensor)]),
+    "lalb_blob_verify": (c_int, [P, c_int]),
+    "lalb_blob_read_host": (c_int, [P, c_int, c_uint64, c_uint64, P]),
+    "lalb_blob_load": (c_int, [P, P, c_int, c_uint64, c_uint64, P, P]),
     "lalb_sample": (c_int, [P, P, c_int, P, c_int, ctypes.POINTER(Sampling), P, P, P, P, P, P]),
     "lalb_decoder_step": (c_int, [P, P, P, P, P, P]),
     "lalb_decoder_step_host": (c_int, [P, P, P, P]),
