@@ -157,8 +157,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
                 bulk_prefetch_l2(w0 + off, (uint32_t)(bytes - off < 32768 ? bytes - off : 32768));
         }
         pdl_wait();
-        if (kw == 0 && lane == 0)
-            for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
+        // the shared-memory stream starts after the activation prologue: its
+        // copies (a good part of the SM's L2 bandwidth for a microsecond or
+        // two) would otherwise delay the activation loads queued behind them
     } else {
         // The weights are never written by the preceding kernel, so their
         // stream starts before the dependency wait; activations come after it.
@@ -215,6 +216,27 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
             scale = (float)red_s[32];
         }
         const int quad = tid >> 2, qi = tid & 3;
+        if (IN == kInF32 && NS <= 2 * nquads) {
+            // both passes' loads in flight at once (one L2 round trip), then
+            // the weight stream, then the quantizer
+            float v[2][8];
+#pragma unroll
+            for (int ps = 0; ps < 2; ++ps) {
+                const int blk = ps * nquads + quad;
+                if (blk < NS) load8(a.x + blk * 32 + 8 * qi, vec, v[ps]);
+                else
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[ps][i] = 0.0f;
+            }
+            if (a.w_l2_first && kw == 0 && lane == 0)
+                for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
+#pragma unroll
+            for (int ps = 0; ps < 2; ++ps) {
+                const int blk = ps * nquads + quad;
+                if (ps * nquads + (tid & ~31) / 4 < NS)
+                    quantize_block_quad_swz(v[ps], qi, blk < NS, xq_s, blk, sx_s + blk, sq_s + blk);
+            }
+        } else
         for (int blk0 = 0; blk0 < NS; blk0 += nquads) {
             const int blk = blk0 + quad;
             const bool have = blk < NS;
@@ -238,6 +260,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) q4k_gemv_kernel(const Q4kGemvA
         }
     }
     __syncthreads();
+    // (the one-round-trip fp32 prologue above has issued them already)
+    if (a.w_l2_first && !(IN == kInF32 && NS <= 2 * (((nthreads >> 5) << 5) >> 2)) && kw == 0 &&
+        lane == 0)
+        for (int it = 0; it < kBufPerTeam && it < my_stages; ++it) issue(it, policy);
     pdl_launch_dependents();
 
     // ---- per-lane activation registers ------------------------------------
