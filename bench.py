@@ -202,18 +202,20 @@ def gemv_standalone(ctx, torch, stream, reps=200, ncopies=8):
 STE = dict(n_layer=8, d=448, ffn=1792, vocab=32768, rows=1024)
 
 
-def run_ste_case(args):
+def run_ste_case(args, ctx=None):
     """The seed STE model's forward matmuls (8 layers, d=448, FFN 1792, vocab
     32768) on X 1024 x 448 fp32: per-element CORE/BINARY/PRUNE weights drawn
     10/50/40, packed as int8 codes with a per-row scale; every matmul on the
     tcgen05 tf32-part GEMM.  Two weight sets (larger than L2 together) are
-    used on alternate steps.  Prints its own JSON line (not the decode line)."""
+    used on alternate steps.  Returns its own JSON line (`--case ste`; the
+    decode line carries it as "ste")."""
     import torch
 
     import lalmodel_b200 as lb
 
     c = STE
-    ctx = lb.Context(0)
+    own_ctx = ctx is None
+    ctx = ctx or lb.Context(0)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(55)
     M, d, f = c["rows"], c["d"], c["ffn"]
@@ -339,29 +341,31 @@ def run_ste_case(args):
                                                                 "traffic_bytes_per_launch")},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": len(shapes) * args.steps,
             "clocks": clocks}
-    print(json.dumps(line), flush=True)
     for layers in sets:
         for L in layers:
             L.close()
-    ctx.close()
+    if own_ctx:
+        ctx.close()
+    return line
 
 
 PREFILL_T = 512
 
 
-def run_prefill_case(args):
+def run_prefill_case(args, ctx=None):
     """Qwen2.5-7B-shape prefill: T = 512 tokens through every Q4_K matrix of
     the 28 layers (qkv 4608x3584, o 3584x3584, gate/up 37888x3584, down
     3584x18944) on the tcgen05 prefill kernel.  One step = the 112 matmuls;
-    the metric is int8-equivalent ops (2 T rows K) per second.  Prints its own
-    JSON line (not the decode line)."""
+    the metric is int8-equivalent ops (2 T rows K) per second.  Returns its own
+    JSON line (`--case prefill`; the decode line carries it as "prefill")."""
     import torch
 
     import lalmodel_b200 as lb
 
     c = CFG
     T = PREFILL_T
-    ctx = lb.Context(0)
+    own_ctx = ctx is None
+    ctx = ctx or lb.Context(0)
     mats = layer_mats(c)
     big = max(r * k for r, k in mats)
     tmp = torch.empty(big, dtype=torch.float32, device="cuda")
@@ -514,8 +518,11 @@ def run_prefill_case(args):
                     "d2h_bytes_per_step": hy.numel() * 4},
             "gpu_launches": args.steps * 2 * len(calls),
             "clocks": clocks}
-    print(json.dumps(line), flush=True)
-    ctx.close()
+    del packed, X, Y, ws
+    torch.cuda.empty_cache()
+    if own_ctx:
+        ctx.close()
+    return line
 
 
 def run_gemv_case(args):
@@ -685,6 +692,21 @@ def run_gpu(args, rank, world, local_rank):
         if tp else None
 
     gemv = gemv_standalone(ctx, torch, stream) if rank == 0 else None
+
+    # configs 4 and 5 on one GPU, each a compact sub-line of this one
+    subs = {}
+    if world == 1 and not args.no_sub:
+        sub_args = argparse.Namespace(**vars(args))
+        sub_args.steps, sub_args.warmup = 20, 3
+        sub_args.cpu_seconds = min(args.cpu_seconds, 5.0)
+        del dec
+        torch.cuda.empty_cache()
+        dec = None
+        for name, fn in (("prefill", run_prefill_case), ("ste", run_ste_case)):
+            sub = fn(sub_args, ctx)
+            subs[name] = {k: sub[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
+                                              "dtype", "config", "roofline", "e2e",
+                                              "cpu_baseline", "gpu_launches", "clocks")}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_sample(layers, lm, c, budget_s=args.cpu_seconds)
@@ -716,10 +738,12 @@ def run_gpu(args, rank, world, local_rank):
         }
         if tp_check is not None:
             line["tp_check"] = tp_check
+        line.update(subs)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()   # no rank unmaps its exchange buffer while a peer may still use it
-    dec.close()
+    if dec is not None:
+        dec.close()
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
@@ -910,6 +934,8 @@ def main():
     ap.add_argument("--impl", default="lalb", choices=["lalb", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="skip the prefill and seed-STE sub-measurements of the decode line")
     ap.add_argument("--n-layer", type=int, default=CFG["n_layer"],
                     help="fewer layers: only for profiling captures, not a bench line")
     ap.add_argument("--vocab", type=int, default=CFG["vocab"],
@@ -933,9 +959,9 @@ def main():
     elif args.case == "gemv":
         run_gemv_case(args)
     elif args.case == "ste":
-        run_ste_case(args)
+        print(json.dumps(run_ste_case(args)), flush=True)
     elif args.case == "prefill":
-        run_prefill_case(args)
+        print(json.dumps(run_prefill_case(args)), flush=True)
     else:
         run_gpu(args, rank, world, local_rank)
 

@@ -278,29 +278,36 @@ __device__ __forceinline__ bool cross_phase(const PersistArgs &a, int ph) {
     return k == kGu || k == kDown;
 }
 
+// Called by the 32 threads of the CTA's first consumer warp (lane = 0..31).
+// The rank's last arrival signals the other ranks from one warp instruction:
+// lane j adds to rank j's counter, so the system-scope releases to the peers
+// are issued together rather than one after another (n_rank <= 8 <= 32).
 template <int PPL>
 __device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &own, int rank,
-                                            int ph, unsigned int seq) {
+                                            int ph, unsigned int seq, int lane) {
     const unsigned int nl = a.cta_per_rank, nr = cross_phase<PPL>(a, ph) ? a.n_rank - 1 : 0;
     const unsigned int t_local = (seq + 1u) * nl;
     unsigned int *lbar = own.gbar + ph;
     if (nr == 0) {
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(lbar) : "memory");
-    } else {
+        if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(lbar) : "memory");
+        return;
+    }
+    unsigned int last = 0;
+    if (lane == 0) {
         unsigned int old;
         asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(lbar) : "memory");
-        if (old + 1u == t_local) {
-            // the rank's last arrival: acquire every other CTA's release first
-            asm volatile("fence.acq_rel.gpu;" ::: "memory");
-            for (int j = 0; j < a.n_rank; ++j) {
-                if (j == rank) continue;
-                unsigned int *ctr = xview<PPL>(a, j).gbar + PPL * a.n_layer + ph;
-                if (a.remote)
-                    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
-                else
-                    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
-            }
-        }
+        last = old + 1u == t_local;
+        // the rank's last arrival: acquire every other CTA's release first
+        if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();   // lane 0's acquire happens before the other lanes' releases
+    if (last && lane < a.n_rank && lane != rank) {
+        unsigned int *ctr = xview<PPL>(a, lane).gbar + PPL * a.n_layer + ph;
+        if (a.remote)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+        else
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
     }
 }
 
@@ -775,17 +782,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         // ---- every CTA must have finished phase p-1 --------------------------
         if (p > 0) {
             cons_bar();
+            unsigned long long *tr =
+                a.trace && ct == 0 ? a.trace + ((size_t)blockIdx.x * NP + p - 1) * kTraceFields
+                                   : nullptr;
+            if (tr) {
+                tr[0] = global_ns();
+                tr[3] = cs.wait_ns;
+                tr[4] = cs.busy_ns;
+                tr[7] = cs.polls;
+                cs.wait_ns = cs.busy_ns = cs.polls = 0;
+            }
+            if (ct < 32) grid_arrive<PPL>(a, own, w.rank, p - 1, seq, ct);
             if (ct == 0) {
-                unsigned long long *tr =
-                    a.trace ? a.trace + ((size_t)blockIdx.x * NP + p - 1) * kTraceFields : nullptr;
-                if (tr) {
-                    tr[0] = global_ns();
-                    tr[3] = cs.wait_ns;
-                    tr[4] = cs.busy_ns;
-                    tr[7] = cs.polls;
-                    cs.wait_ns = cs.busy_ns = cs.polls = 0;
-                }
-                grid_arrive<PPL>(a, own, w.rank, p - 1, seq);
                 d = phase_desc<PPL>(a, p, w);   // while the arrivals propagate
                 // a grid barrier that gives up leaves the rest of the token
                 // to run on whatever data it has: later grid waits give up
