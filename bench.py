@@ -538,6 +538,63 @@ def run_gemv_case(args):
     ctx.close()
 
 
+def run_trace_case(args, rank, world, local_rank):
+    """Phase timeline of the persistent decode (one process per GPU under
+    torchrun, tensor-parallel when N > 1): one traced token after 30 untimed
+    ones; rank 0 prints, per phase kind, the median over layers of the grid
+    barrier after the phase, the next phase's prologue and its work (us).
+    A profiling aid, not a bench line."""
+    import torch
+    import torch.distributed as dist
+
+    import lalmodel_b200 as lb
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=300))
+    c = CFG
+    ctx = lb.Context(local_rank)
+    dec, _, _ = build_decoder(ctx, lb, torch, c, seed=1234, n_rank=world, rank=rank)
+    if world > 1:
+        dec.connect(lb.exchange_handles(dec.ipc_handle()))
+        dist.barrier()
+    h = torch.empty(c["hidden"], dtype=torch.float32, device="cuda")
+    ctx.fill_normal(h, seed=77, sigma=1.0)
+    am = torch.empty(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(30):
+            dec.step(h, None, None, am)
+        tr = dec.trace_step(h)
+    s.synchronize()
+    if rank == 0:
+        n_p = tr.shape[1]
+        t0 = tr[:, 0, 0].min()
+        work_end = tr[:, :, 0].max(0) - t0
+        bar_left = np.median(tr[:, :, 1], 0) - t0
+        pro = np.median(tr[:, :, 2], 0) - t0
+        kinds = ["qkv", "o", "gate/up", "down"]
+        rows = {k: [] for k in kinds}
+        for p in range(n_p - 1):
+            rows[kinds[p % 4]].append(((bar_left[p] - work_end[p]) / 1e3,
+                                       (pro[p + 1] - bar_left[p]) / 1e3,
+                                       (work_end[p + 1] - pro[p + 1]) / 1e3))
+        out = {"case": "trace", "n_gpus": world,
+               "token_us": round(float(tr[:, n_p - 1, 0].max() - t0) / 1e3, 1),
+               "after_phase_us": {k: dict(zip(("barrier", "next_prologue", "next_work"),
+                                              (round(float(v), 2)
+                                               for v in np.median(np.array(rows[k]), 0))))
+                                  for k in kinds}}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+    dec.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def shard_bytes(lb, c, n_rank, rank):
     """Weight and activation bytes that rank `rank` of `n_rank` streams per token."""
     total = 0
@@ -942,10 +999,11 @@ def main():
                     help="smaller LM head: only for profiling captures, not a bench line")
     ap.add_argument("--path", default="auto", choices=["auto", "kernels", "persistent"],
                     help="decoder path: one persistent kernel per token, or one kernel per matvec")
-    ap.add_argument("--case", default="decode", choices=["decode", "gemv", "ste", "prefill"],
+    ap.add_argument("--case", default="decode", choices=["decode", "gemv", "ste", "prefill", "trace"],
                     help="gemv: only the single 18944x3584 GEMV, for profiler captures; "
                          "ste: the seed STE model's forward matmuls (its own line); "
-                         "prefill: the 7B-shape prefill of 512 tokens (its own line)")
+                         "prefill: the 7B-shape prefill of 512 tokens (its own line); "
+                         "trace: the persistent decode's phase timeline (profiling aid)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -960,6 +1018,8 @@ def main():
         run_gemv_case(args)
     elif args.case == "ste":
         print(json.dumps(run_ste_case(args)), flush=True)
+    elif args.case == "trace":
+        run_trace_case(args, rank, world, local_rank)
     elif args.case == "prefill":
         print(json.dumps(run_prefill_case(args)), flush=True)
     else:
