@@ -369,26 +369,23 @@ def run_prefill_case(args, ctx=None):
     mats = layer_mats(c)
     big = max(r * k for r, k in mats)
     tmp = torch.empty(big, dtype=torch.float32, device="cuda")
-    packed, q4k_o = [], None
+    wq, q4k_o = [], None
     for l in range(c["n_layer"]):
         for j, (rows, K) in enumerate(mats):
             w = tmp[: rows * K].view(rows, K)
             ctx.fill_normal(w, seed=1234 + 16 * l + j, sigma=0.02)
-            q = ctx.q4k_quantize(w)
-            packed.append(ctx.q4k_prefill_pack(q, rows, K))
+            wq.append(ctx.q4k_quantize(w))
             if l == 0 and j == 1:
-                q4k_o = q.cpu().numpy()   # the CPU sample's matrix
-            del q
+                q4k_o = wq[-1].cpu().numpy()   # the CPU sample's matrix
     torch.cuda.synchronize()
     del tmp, w
     torch.cuda.empty_cache()
     X = {K: torch.empty((T, K), dtype=torch.float32, device="cuda") for K in {k for _, k in mats}}
     for i, K in enumerate(sorted(X)):
         ctx.fill_normal(X[K], seed=70 + i, sigma=1.0)
-    ws = torch.empty(max(lb.prefill_sizes(r, k, T)[1] for r, k in mats), dtype=torch.uint8,
-                     device="cuda")
+    ws = torch.empty(max(lb.prefill_ws_bytes(k, T) for _, k in mats), dtype=torch.uint8, device="cuda")
     Y = {r: torch.empty((T, r), dtype=torch.float32, device="cuda") for r in {r for r, _ in mats}}
-    calls = [(packed[4 * l + j], rows, K) for l in range(c["n_layer"]) for j, (rows, K) in enumerate(mats)]
+    calls = [(wq[4 * l + j], rows, K) for l in range(c["n_layer"]) for j, (rows, K) in enumerate(mats)]
     ops = sum(2.0 * T * rows * K for _, rows, K in calls)
     stream = torch.cuda.Stream()
 
@@ -502,9 +499,10 @@ def run_prefill_case(args, ctx=None):
                                    "o 3584x3584, gate/up 37888x3584, down 3584x18944) Q4_K"
                                    % (T, c["n_layer"]),
                        "tokens": T, "matmuls_per_step": len(calls), "ops_per_step": ops,
-                       "l2": "inputs larger than L2: %.1f GB of packed weights per step"
-                             % (sum(lb.prefill_sizes(r, k, T)[0] for _, r, k in calls) / 1e9)},
-            "roofline": {"kernel": "prefill_tc_kernel", "bound": "tensor",
+                       "l2": "inputs larger than L2: %.2f GB of Q4_K weights per step, read as "
+                             "they are (0.5625 B/weight)"
+                             % (sum(r * k // 256 * 144 for _, r, k in calls) / 1e9)},
+            "roofline": {"kernel": "prefill_q4k_kernel", "bound": "tensor",
                          "achieved": round(work, 1), "peak": bf16, "peak_kind": kind,
                          "unit": "TFLOP/s", "frac": round(work / bf16, 4),
                          "note": "achieved = issued fp16/bf16 tensor work (2.25 x the int8-"
@@ -518,7 +516,7 @@ def run_prefill_case(args, ctx=None):
                     "d2h_bytes_per_step": hy.numel() * 4},
             "gpu_launches": args.steps * 2 * len(calls),
             "clocks": clocks}
-    del packed, X, Y, ws
+    del wq, X, Y, ws
     torch.cuda.empty_cache()
     if own_ctx:
         ctx.close()

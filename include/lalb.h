@@ -45,7 +45,7 @@ extern "C" {
 #define LALB_API
 #endif
 
-#define LALB_ABI_VERSION 2
+#define LALB_ABI_VERSION 3
 #define LALB_QK_K 256
 #define LALB_QB 32
 #define LALB_Q4K_BLOCK_BYTES 144
@@ -388,20 +388,18 @@ LALB_API int lalb_decoder_destroy(lalb_decoder *dec);
 
 /* ---- prefill: the Q4_K x Q8 matmul for T tokens at once (tcgen05) --------
  * Y [T][rows] fp32 = lal_matmul_q4_k (README.md:130,210) applied to each of
- * the T rows of X [T][K] fp32, with the same per-32 activation quantizer.
+ * the T rows of X [T][K] fp32, with the same per-32 activation quantizer,
+ * straight from the Q4_K rows W (as for lalb_matmul_q4_k; 16-byte aligned).
  * On the tensor cores (tcgen05.mma kind::f16, fp32 accumulators in TMEM):
- * A = sc*q per weight as fp16 (exact), B = xq*sx per token as two fp16
- * parts under a per-token power of two, the min terms as bf16 parts; each
- * 256-weight super-block is scaled by d in the epilogue.  Every output is
- * within 1e-5 of the exact value relative to the sum of its term
- * magnitudes.  The weights are first unpacked once into `packed`
- * (weight_bytes: fp16 sc*q, bf16 min parts and d per super-block); `ws`
- * holds the prepared tokens (ws_bytes).  K % 256 == 0; packed and ws
- * 256-byte aligned. */
-LALB_API int lalb_prefill_sizes(int rows, int K, int T, size_t *weight_bytes, size_t *ws_bytes);
-LALB_API int lalb_q4k_prefill_pack(lalb_ctx *ctx, const void *W, int rows, int K, void *packed,
-                                   lalb_stream stream);
-LALB_API int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *packed, int rows, int K,
+ * each row's 4-bit quants are decoded on chip into A = sc*q as fp16
+ * (exact), B = xq*sx per token as two fp16 parts under a per-token power of
+ * two, the min terms as bf16 parts; each 256-weight super-block is scaled
+ * by d in the epilogue.  Every output is within 1e-5 of the exact value
+ * relative to the sum of its term magnitudes.  `ws` (ws_bytes from
+ * lalb_prefill_ws_bytes, 256-byte aligned) holds the prepared tokens.
+ * K % 256 == 0. */
+LALB_API int lalb_prefill_ws_bytes(int K, int T, size_t *ws_bytes);
+LALB_API int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *W, int rows, int K,
                                       const float *X, int T, void *ws, float *Y,
                                       lalb_stream stream);
 

@@ -177,32 +177,25 @@ class Context:
                    _p(sx), _p(logits), _p(isum), _p(am), _stream())
         return logits, isum, am
 
-    # ---- prefill: T tokens at once on the int8 tensor cores ------------------
-    def q4k_prefill_pack(self, W, rows, K):
-        """Unpacks Q4_K rows once into the prefill layout (int8 quants + scales)."""
-        wb, _ = prefill_sizes(rows, K, 1)
-        packed = torch.empty(wb, dtype=torch.uint8, device=W.device)
-        self._call("lalb_q4k_prefill_pack", self.h, _p(W), rows, K, _p(packed), _stream())
-        return packed
-
-    def matmul_q4_k_prefill(self, packed, rows, K, X, ws=None, out=None):
-        """Y [T][rows] = the Q4_K x Q8 matmul of each token row of X [T][K]."""
+    # ---- prefill: T tokens at once on the tensor cores ----------------------
+    def matmul_q4_k_prefill(self, W, rows, K, X, ws=None, out=None):
+        """Y [T][rows] = the Q4_K x Q8 matmul of each token row of X [T][K],
+        straight from the Q4_K rows W (as for matmul_q4_k)."""
         T = X.shape[0]
         if ws is None:
-            ws = torch.empty(prefill_sizes(rows, K, T)[1], dtype=torch.uint8, device=X.device)
+            ws = torch.empty(prefill_ws_bytes(K, T), dtype=torch.uint8, device=X.device)
         Y = out if out is not None else torch.empty((T, rows), dtype=torch.float32, device=X.device)
-        self._call("lalb_matmul_q4_k_prefill", self.h, _p(packed), rows, K, _p(X), T, _p(ws),
-                   _p(Y), _stream())
+        self._call("lalb_matmul_q4_k_prefill", self.h, _p(W), rows, K, _p(X), T, _p(ws), _p(Y), _stream())
         return Y
 
 
-def prefill_sizes(rows, K, T):
-    """(packed weight bytes, per-call workspace bytes) of the prefill matmul."""
-    wb, ws = ctypes.c_size_t(), ctypes.c_size_t()
-    st = _abi.lib().lalb_prefill_sizes(rows, K, T, ctypes.byref(wb), ctypes.byref(ws))
+def prefill_ws_bytes(K, T):
+    """Workspace bytes of a prefill call of T tokens of width K (the prepared tokens)."""
+    ws = ctypes.c_size_t()
+    st = _abi.lib().lalb_prefill_ws_bytes(K, T, ctypes.byref(ws))
     if st != 0:
-        raise LalbError("lalb_prefill_sizes", st, "rows=%d K=%d T=%d" % (rows, K, T))
-    return wb.value, ws.value
+        raise LalbError("lalb_prefill_ws_bytes", st, "K=%d T=%d" % (K, T))
+    return ws.value
 
 
 IPC_HANDLE_BYTES = 64   # LALB_IPC_HANDLE_BYTES

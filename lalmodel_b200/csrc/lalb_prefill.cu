@@ -1,4 +1,5 @@
-// lalb_prefill.cu -- batched (prefill) Q4_K x Q8 matmul on the tcgen05 tensor cores.
+// lalb_prefill.cu -- batched (prefill) Q4_K x Q8 matmul on the tcgen05 tensor cores,
+// straight from the Q4_K bytes.
 //
 //   Y[t][r] = sum_j sx[t][j] * (d_r sc_rj * isum[t][r][j] - dmin_r m_rj * sumq[t][j])
 //
@@ -26,26 +27,25 @@
 // for the two sub-blocks' min terms.  The epilogue only adds D * S_b (paired
 // __ffma2_rn) and undoes 2^e_t.  Within 1e-5 of the exact dot.
 //
-// Layouts (the weights prepared once by lalb_q4k_prefill_pack, the tokens per
-// call):
-//   weights  A    fp16 [rows][K] = sc_j * q
-//            Ax   bf16 [rows][K/4]: per 64 weights 16 values, for their two
-//                 sub-blocks {c0 c0 c1 c0 c1 c2} each, then 4 zeros
-//            rs   fp32 [K/256][rows128] = D
-//   tokens   Bhi, Blo  fp16 [T][K]
-//            Bx   bf16 [T][K/4]: per 64 weights, for their two sub-blocks
-//                 {a0 a1 a0 a2 a1 a0} (parts of a 2^e_t) each, then 4 zeros
-//            inv  fp32 [Tp] = 2^-e_t   (Tp = T rounded up to 128)
+// The weights stay the caller's Q4_K rows (0.5625 bytes per weight in HBM):
+// the 128-row x 256-weight tile of a super-block comes into shared memory as
+// its raw 144-byte blocks (18 KB), and worker warps decode it in registers
+// (row = TMEM lane) into the MMA's A operand, stored straight into TMEM with
+// tcgen05.st: per 64-weight K-block the fp16 sc_j * q (32 columns) and the
+// bf16 min-term parts (8 columns).  The MMAs read A from TMEM and only the
+// token tiles from shared memory.
 //
-// One CTA per 128-row x 128-token tile, 18 warps:
-//   warp 0     TMA producer: per 64-wide K-block the A, B_hi, B_lo (128-byte
-//              swizzle), Ax and Bx (32-byte swizzle) tiles into a 4-stage
-//              ring; per super-block the rows' D into a 2-slot ring;
-//   warp 1     allocates 512 TMEM columns (4 super-block slots of 128) and
-//              issues the MMAs, one commit per stage and one per super-block;
-//   warps 2-17 epilogue, four groups of four (32 tokens each), each warp on its
-//              TMEM lane quarter (32 weight rows): per super-block, read the
-//              slot (tcgen05.ld 32x32b.x16 twice), free it, acc += D * S.
+// Tokens, prepared per call (prefill_act_kernel) in the workspace:
+//   Bhi, Blo  fp16 [T][K]
+//   Bx        bf16 [T][K/4]: per 64 weights, for their two sub-blocks
+//             {a0 a1 a0 a2 a1 a0} (parts of a 2^e_t) each, then 4 zeros
+//   inv       fp32 [Tp] = 2^-e_t   (Tp = T rounded up to 128)
+//
+// TMEM (all 512 columns of the SM):
+//   columns   0..255   two super-block accumulator slots of 128 (fp32): the
+//                      B_hi and B_lo products of a K-step accumulate into the
+//                      same slot (two N = 128 MMAs)
+//   columns 256..511   four A stages of 64: sc * q (32), min-term parts (8)
 // Every wait is bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -62,37 +62,41 @@ using namespace lalb;
 namespace {
 
 constexpr int PM = 128, PN = 128, PK = 64;   // PK fp16 = 128 B: one swizzle row
-constexpr int kPStages = 4;
 constexpr int kSlotsT = 2;                   // TMEM super-block slots
-constexpr int kSlotW = 2 * PN;               // a slot: B_hi products (PN columns), then B_lo's
-constexpr int kTmemCols = kSlotsT * kSlotW;
+constexpr int kTmemCols = 512;
 constexpr int kEpiWarps = 16;
-constexpr int kPThreads = 32 * (2 + kEpiWarps);
-constexpr uint32_t kPA = PM * PK * 2;        // 16 KB
 constexpr uint32_t kPB = PN * PK * 2;        // 16 KB (each of B_hi, B_lo)
-constexpr uint32_t kPAX = PM * 16 * 2;       // 4 KB: 128 rows x 16 bf16
-constexpr uint32_t kPBX = PN * 16 * 2;       // 4 KB
-constexpr uint32_t kOffBh = kPA, kOffBl = kPA + kPB, kOffAx = kPA + 2 * kPB, kOffBx = kOffAx + kPAX;
-constexpr uint32_t kPStage = kOffBx + kPBX;  // 56 KB
-constexpr uint32_t kSbBytes = PM * 4;        // the tile rows' D of one super-block
-constexpr int kSbSlots = 2;
-constexpr uint32_t kPSmem = 1024 + kPStages * kPStage + kSbSlots * kSbBytes + 512;
-static_assert(kPStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
-static_assert(kPSmem <= 232448, "fits the 227 KB opt-in shared memory");
+constexpr uint32_t kPBX = PN * 16 * 2;       // 4 KB: 128 tokens x 16 bf16
+constexpr int kRBStages = 4;                    // token tiles: B_hi, B_lo, Bx
+constexpr uint32_t kRBStage = 2 * kPB + kPBX;   // 36 KB
+constexpr uint32_t kRBOffBx = 2 * kPB;
+constexpr int kRawSlots = 3;                    // raw super-block tiles
+constexpr uint32_t kRawBytes = PM * 144;        // 18 KB
+constexpr int kRThreads = 32 * (2 + kEpiWarps);   // producer, MMA, 16 workers
+constexpr int kRAccW = PN;                      // accumulator slot: 128 columns
+constexpr int kRAStages = 4;                    // A stages in TMEM
+constexpr int kRAColW = 64;                     // columns per A stage
+constexpr int kRAColBase = kSlotsT * kRAccW;    // 256
+constexpr int kRAColX = 32;                     // min-term parts within the stage
+static_assert(kRAColBase + kRAStages * kRAColW <= kTmemCols, "A stages fit the TMEM allocation");
+constexpr uint32_t kRSmem = 1024 + kRBStages * kRBStage + kRawSlots * kRawBytes + 512;
+static_assert(kRSmem <= 232448, "fits the 227 KB opt-in shared memory");
+static_assert(kRBStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+static_assert(kRawBytes % 128 == 0, "raw slots keep 128-byte alignment");
+static_assert(kRAStages == kRBStages && kRAStages == 4, "A stage g holds K-block g of each super-block");
 constexpr int kActThreads = 128;   // token preparation: 4 warps per token, 4 tokens per SM at once
 constexpr int kActCache = 20;      // 128-element groups a warp keeps in registers between the passes
                                    // (K <= 4 x 20 x 128 = 10240 reads X once, longer rows
                                    // re-read the rest)
 
-// kind::f16: f32 accumulator, fp16 A and B, both K-major, M = 128, N = 256:
-// B is B_hi's 128 token rows followed by B_lo's (adjacent in the stage), so
-// one MMA reads A once for both parts.
-constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(kSlotW >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
-// bf16 A and B, N = 128 (the min-term MMA, into the B_hi half)
+// kind::f16, f32 accumulator, fp16 A (TMEM) and B (shared memory), both
+// K-major, M = 128, N = 128
+constexpr uint32_t kIdescF16N128 = (1u << 4) | ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
+// bf16 A and B, N = 128 (the min-term MMA)
 constexpr uint32_t kIdescBF16 =
     (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
-static_assert(kOffBl == kOffBh + PN * 128, "B_lo's rows follow B_hi's in the stage");
 
+// K-major, 128-byte swizzle (one 64-element fp16 K-block per row): 8-row atoms of 1 KB.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
@@ -112,21 +116,6 @@ __device__ __forceinline__ void tma2d(void *dst, const CUtensorMap *map, int x, 
         : "memory");
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -138,7 +127,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-
 struct PfArgs {
     int rows, K, T;
     const float *inv;       // [Tp] 2^-e_t
@@ -146,19 +134,159 @@ struct PfArgs {
     unsigned int *status;
 };
 
-__global__ void __launch_bounds__(kPThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mBh,
-                      const __grid_constant__ CUtensorMap mBl, const __grid_constant__ CUtensorMap mAx,
-                      const __grid_constant__ CUtensorMap mBx, const __grid_constant__ CUtensorMap mRS,
-                      const PfArgs a) {
+// x = p0 + p1 + p2, three bf16 parts (each the round-to-nearest of what is left).
+__device__ __forceinline__ void split3_bf16(float x, __nv_bfloat16 &p0, __nv_bfloat16 &p1, __nv_bfloat16 &p2) {
+    p0 = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(p0);
+    p1 = __float2bfloat16_rn(r1);
+    p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+}
+
+// D (TMEM) += A (TMEM) x B (shared memory descriptor), issued by one elected
+// lane of a converged warp: the whole warp runs the issue loop, so the
+// operands are warp-uniform values.
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// tcgen05.commit from one elected lane of a converged warp
+__device__ __forceinline__ void commit_elect(uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+// A bounded wait that first tests the phase without suspending: a try_wait on
+// a phase that has already completed still costs on the order of a hundred
+// cycles, and most waits of the MMA warp find their phase complete.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t *bar, uint32_t parity, unsigned int *status) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done || mbar_wait_bounded(bar, parity, status);
+}
+
+__device__ __forceinline__ bool warp_wait_fast(uint64_t *bar, uint32_t parity, unsigned int *status) {
+    return __all_sync(0xffffffffu, mbar_wait_fast(bar, parity, status));
+}
+
+// 8 (32) columns of the warp's 32 TMEM lanes: register j of lane i -> (lane i, column + j)
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// The 64 fp16 values sc * q of one row's 64-weight K-block kbl, from its raw
+// 144-byte block, as 32 half2 words in weight order: the 32 quant bytes of
+// group kbl hold sub-block 2 kbl (weights 0..31) in their low and 2 kbl + 1
+// (weights 32..63) in their high nibbles.  sc * q is an integer <= 945, exact
+// in fp16: (1024 + q) as fp16 times sc minus 1024 sc, one fused rounding of
+// an exact result.
+__device__ __forceinline__ void conv_kblock(const uint8_t *blk, int kbl, uint32_t sc0, uint32_t sc1,
+                                            uint32_t (&o)[32]) {
+    const uint4 v0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * kbl);
+    const uint4 v1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * kbl);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    const __half2 s0 = __half2half2(__uint2half_rn(sc0)), s1 = __half2half2(__uint2half_rn(sc1));
+    const __half2 m0 = __hneg2(__half2half2(__uint2half_rn(1024u * sc0)));
+    const __half2 m1 = __hneg2(__half2half2(__uint2half_rn(1024u * sc1)));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t l = w[k] & 0x0F0F0F0Fu, h = (w[k] >> 4) & 0x0F0F0F0Fu;
+        const uint32_t l01 = __byte_perm(l, 0x64646464u, 0x5140), l23 = __byte_perm(l, 0x64646464u, 0x7362);
+        const uint32_t h01 = __byte_perm(h, 0x64646464u, 0x5140), h23 = __byte_perm(h, 0x64646464u, 0x7362);
+        const __half2 a = __hfma2(*reinterpret_cast<const __half2 *>(&l01), s0, m0);
+        const __half2 b = __hfma2(*reinterpret_cast<const __half2 *>(&l23), s0, m0);
+        const __half2 c = __hfma2(*reinterpret_cast<const __half2 *>(&h01), s1, m1);
+        const __half2 d = __hfma2(*reinterpret_cast<const __half2 *>(&h23), s1, m1);
+        o[2 * k] = *reinterpret_cast<const uint32_t *>(&a);
+        o[2 * k + 1] = *reinterpret_cast<const uint32_t *>(&b);
+        o[16 + 2 * k] = *reinterpret_cast<const uint32_t *>(&c);
+        o[16 + 2 * k + 1] = *reinterpret_cast<const uint32_t *>(&d);
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+    return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// The 16 bf16 min-term values of one row's K-block (sub-blocks 2 kbl and
+// 2 kbl + 1) as 8 words: {c0 c0 c1 c0 c1 c2} of each sub-block's
+// c = -dmin m / D, then four zeros (the prefill_pack_kernel layout).
+__device__ __forceinline__ void conv_minparts(float dmin, float D, int m0, int m1, uint32_t (&o)[8]) {
+    __nv_bfloat16 a0, a1, a2, b0, b1, b2;
+    split3_bf16(-__fdiv_rn(__fmul_rn(dmin, (float)m0), D), a0, a1, a2);
+    split3_bf16(-__fdiv_rn(__fmul_rn(dmin, (float)m1), D), b0, b1, b2);
+    o[0] = pack_bf16(a0, a0);
+    o[1] = pack_bf16(a1, a0);
+    o[2] = pack_bf16(a1, a2);
+    o[3] = pack_bf16(b0, b0);
+    o[4] = pack_bf16(b1, b0);
+    o[5] = pack_bf16(b1, b2);
+    o[6] = 0u;
+    o[7] = 0u;
+}
+
+// One CTA per 128-row x 128-token tile, 18 warps:
+//   warp 0      TMA producer: the first three raw 128 x 144-byte super-block
+//               tiles, then per K-block the B_hi, B_lo and Bx token tiles into
+//               a 4-stage ring;
+//   warp 1      the MMAs, the whole warp in the loop and one elected lane
+//               issuing: per K-step A x B_hi and A x B_lo into the
+//               super-block's slot, per K-block the min-term MMA, and one
+//               commit that frees the K-block's token stage and A stage (the
+//               two rings share their stage index kb % 4);
+//   warps 2-17  workers, each on its TMEM lane quarter q = warp % 4 (rows
+//               32 q .. 32 q + 31, lane = row) and group g = (warp - 2) / 4:
+//               of every super-block, K-block g into A stage g (64 sc * q
+//               values and the 16 min-term parts per row), then the epilogue
+//               of the previous super-block (tokens 32 g .. 32 g + 31 of its
+//               slot), whose D the thread kept from the row's header.  The
+//               raw tiles have a 3-slot ring: once every worker has decoded
+//               super-block sb, the first worker thread loads sb + 3 into its
+//               slot, two super-blocks ahead of its use.
+// TMEM: all 512 columns are allocated, so its base address is column 0 and
+// the MMA warp's TMEM operands are constants plus the loop's offsets.
+__global__ void __launch_bounds__(kRThreads, 1)
+    prefill_q4k_kernel(const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mBh,
+                       const __grid_constant__ CUtensorMap mBl, const __grid_constant__ CUtensorMap mBx,
+                       const PfArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    float *sbring = reinterpret_cast<float *>(smem + kPStages * kPStage);   // [2][128] D
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kPStages * kPStage + kSbSlots * kSbBytes);
-    uint64_t *empty = full + kPStages;
-    uint64_t *sbfull = empty + kPStages;      // a super-block's D arrived
-    uint64_t *sbempty = sbfull + kSbSlots;    // every epilogue warp is done with it
-    uint64_t *sfull = sbempty + kSbSlots;     // TMEM slot holds a super-block's sums
+    uint8_t *bring = smem;                                      // [4] B_hi | B_lo | Bx
+    uint8_t *rawring = bring + kRBStages * kRBStage;            // [3] raw super-block tiles
+    uint64_t *bfull = reinterpret_cast<uint64_t *>(rawring + kRawSlots * kRawBytes);
+    uint64_t *afull = bfull + kRBStages;      // the four workers of the stage stored their rows
+    uint64_t *kempty = afull + kRAStages;     // the K-block's MMAs completed: token and A stage free
+    uint64_t *rfull = kempty + kRBStages;     // a raw super-block tile landed
+    uint64_t *rempty = rfull + kRawSlots;     // every worker has decoded it
+    uint64_t *sfull = rempty + kRawSlots;     // TMEM slot holds a super-block's sums
     uint64_t *sempty = sfull + kSlotsT;       // the epilogue has read the slot
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sempty + kSlotsT);
 
@@ -168,25 +296,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int nsb = a.K / 256;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kPStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);              // the MMA commit
+        for (int s = 0; s < kRBStages; ++s) {
+            mbar_init(&bfull[s], 1);
+            mbar_init(&afull[s], 4);
+            mbar_init(&kempty[s], 1);             // the MMA commit
         }
-        for (int s = 0; s < kSbSlots; ++s) {
-            mbar_init(&sbfull[s], 1);
-            mbar_init(&sbempty[s], kEpiWarps);
+        for (int s = 0; s < kRawSlots; ++s) {
+            mbar_init(&rfull[s], 1);
+            mbar_init(&rempty[s], kEpiWarps);
         }
         for (int s = 0; s < kSlotsT; ++s) {
             mbar_init(&sfull[s], 1);
             mbar_init(&sempty[s], kEpiWarps);
         }
         fence_barrier_init();
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mW)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mBh)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mBl)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mAx)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mBx)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mRS)) : "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -199,95 +326,137 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    // programmatic dependent launch: the setup above overlapped the previous
-    // kernel's tail; the token parts it wrote are read only after it completes
-    pdl_wait();
-    pdl_launch_dependents();
+    // every role reads the same word; a base other than column 0 (impossible
+    // with the whole of TMEM allocated) raises a status bit and skips the work
+    const bool tmem_ok = tmem == 0;
+    if (!tmem_ok && threadIdx.x == 0) atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
 
     if (warp == 0) {
-        if (lane == 0) {
-            for (int kb = 0; kb < nkb; ++kb) {
-                if ((kb & 3) == 0) {   // a new super-block: its rows' D
-                    const int sb = kb >> 2, slot = sb & 1;
-                    if (sb >= kSbSlots && !mbar_wait_bounded(&sbempty[slot], ((sb >> 1) - 1) & 1u, a.status))
-                        break;
-                    mbar_arrive_expect_tx(&sbfull[slot], kSbBytes);
-                    tma2d(sbring + slot * PM, &mRS, r0, sb, &sbfull[slot]);
-                }
-                const int s = kb % kPStages;
-                const uint32_t use = kb / kPStages;
-                if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u, a.status)) break;
-                uint8_t *st = smem + (size_t)s * kPStage;
-                mbar_arrive_expect_tx(&full[s], kPStage);
-                tma2d(st, &mA, kb * PK, r0, &full[s]);
-                tma2d(st + kOffBh, &mBh, kb * PK, t0, &full[s]);
-                tma2d(st + kOffBl, &mBl, kb * PK, t0, &full[s]);
-                tma2d(st + kOffAx, &mAx, kb * 16, r0, &full[s]);
-                tma2d(st + kOffBx, &mBx, kb * 16, t0, &full[s]);
+        if (lane == 0 && tmem_ok) {
+            // the weights are not written by the previous kernel (the token
+            // preparation): their first tiles go out before the dependency wait
+            for (int sb = 0; sb < kRawSlots && sb < nsb; ++sb) {
+                mbar_arrive_expect_tx(&rfull[sb], kRawBytes);
+                tma2d(rawring + sb * kRawBytes, &mW, sb * 144, r0, &rfull[sb]);
             }
+            pdl_wait();
+            pdl_launch_dependents();
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % kRBStages;
+                const uint32_t use = kb / kRBStages;
+                if (use > 0 && !mbar_wait_fast(&kempty[s], (use - 1) & 1u, a.status)) break;
+                uint8_t *st = bring + (size_t)s * kRBStage;
+                mbar_arrive_expect_tx(&bfull[s], kRBStage);
+                tma2d(st, &mBh, kb * PK, t0, &bfull[s]);
+                tma2d(st + kPB, &mBl, kb * PK, t0, &bfull[s]);
+                tma2d(st + kRBOffBx, &mBx, kb * 16, t0, &bfull[s]);
+            }
+        } else {
+            pdl_wait();
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % kPStages;
-                const int sb = kb >> 2;
-                const uint32_t slot = sb % kSlotsT;
-                if ((kb & 3) == 0 && sb >= kSlotsT &&
-                    !mbar_wait_bounded(&sempty[slot], (uint32_t)(sb / kSlotsT - 1) & 1u, a.status))
-                    break;
-                if (!mbar_wait_bounded(&full[s], (uint32_t)(kb / kPStages) & 1u, a.status)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t st = smem_u32(smem + (size_t)s * kPStage);
-                const uint32_t d = tmem + slot * kSlotW;
+        pdl_wait();
+        const uint32_t bring_s = smem_u32(bring);
+        for (int kb = 0; kb < nkb && tmem_ok; ++kb) {
+            const int sb = kb >> 2;
+            const uint32_t slot = sb % kSlotsT;
+            if ((kb & 3) == 0 && sb >= kSlotsT &&
+                !warp_wait_fast(&sempty[slot], (uint32_t)(sb / kSlotsT - 1) & 1u, a.status))
+                break;
+            const int s = kb % kRBStages;
+            if (!warp_wait_fast(&bfull[s], (uint32_t)(kb / kRBStages) & 1u, a.status) ||
+                !warp_wait_fast(&afull[s], (uint32_t)(kb / kRAStages) & 1u, a.status))
+                break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t bst = bring_s + (uint32_t)s * kRBStage;
+            const uint32_t ta = kRAColBase + s * kRAColW;
+            const uint32_t d = slot * kRAccW;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {   // 16 weights per step, B_hi and B_lo at once
-                    mma_f16(d, sw128_desc(st + kk * 32), sw128_desc(st + kOffBh + kk * 32), kIdescF16,
-                            ((kb & 3) | kk) != 0 ? 1u : 0u);
-                }
-                // the two sub-blocks' min terms
-                mma_f16(d, sw32_desc(st + kOffAx), sw32_desc(st + kOffBx), kIdescBF16, 1u);
-                commit(&empty[s]);                         // the stage's tiles are read once these complete
-                if ((kb & 3) == 3) commit(&sfull[slot]);   // the super-block's sums are complete
+            for (int kk = 0; kk < 4; ++kk) {   // 16 weights (8 columns of A) per step
+                mma_f16_ta(d, ta + kk * 8, sw128_desc(bst + kk * 32), kIdescF16N128,
+                           ((kb & 3) | kk) != 0 ? 1u : 0u);
+                mma_f16_ta(d, ta + kk * 8, sw128_desc(bst + kPB + kk * 32), kIdescF16N128, 1u);
             }
+            mma_f16_ta(d, ta + kRAColX, sw32_desc(bst + kRBOffBx), kIdescBF16, 1u);   // min terms
+            commit_elect(&kempty[s]);
+            if ((kb & 3) == 3) commit_elect(&sfull[slot]);
         }
     } else {
-        // ---- epilogue: warp -> TMEM lane quarter (weight rows), group -> tokens ----
-        const int ew = warp - 2;
-        const int q = warp & 3;              // lane quarter
-        const int grp = ew >> 2;             // tokens 32*grp .. 32*grp + 31
-        const int row = q * 32 + lane;       // weight row within the tile
-        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + grp * 32;
+        pdl_wait();
+        const int q = warp & 3;             // TMEM lane quarter: rows 32 q .. 32 q + 31
+        const int grp = (warp - 2) >> 2;    // K-block of each super-block; tokens 32 grp .. of the epilogue
+        const int row = q * 32 + lane;
+        const uint32_t lanes = (uint32_t)(q * 32) << 16;
+        const uint32_t tacc = lanes + grp * 32;
+        const uint32_t ta = lanes + kRAColBase + grp * kRAColW;   // A stage grp
         float2 acc[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
-        bool ok = true;
-        for (int sb = 0; sb < nsb; ++sb) {
-            const int sslot = sb & 1;
+        bool ok = tmem_ok;
+        auto epilogue = [&](int sb, float D) -> bool {
             const uint32_t slot = sb % kSlotsT;
-            if (!mbar_wait_bounded(&sbfull[sslot], (uint32_t)(sb >> 1) & 1u, a.status) ||
-                !mbar_wait_bounded(&sfull[slot], (uint32_t)(sb / kSlotsT) & 1u, a.status)) {
+            if (!warp_wait_fast(&sfull[slot], (uint32_t)(sb / kSlotsT) & 1u, a.status)) return false;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            float S[32];
+            tmem_ld16(tacc + slot * kRAccW, *reinterpret_cast<float(*)[16]>(S));
+            tmem_ld16(tacc + slot * kRAccW + 16, *reinterpret_cast<float(*)[16]>(S + 16));
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sempty[slot]);
+            const float2 D2 = make_float2(D, D);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = __ffma2_rn(make_float2(S[2 * i], S[2 * i + 1]), D2, acc[i]);
+            return true;
+        };
+        float Dprev = 1.0f;
+        for (int sb = 0; sb < nsb && ok; ++sb) {
+            const int rs = sb % kRawSlots;
+            if (!warp_wait_fast(&rfull[rs], (uint32_t)(sb / kRawSlots) & 1u, a.status)) {
+                ok = false;
+                break;
+            }
+            const uint8_t *blk = rawring + rs * kRawBytes + row * 144;
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+            const ScaleWords sw = unpack_scale_words(hdr.y, hdr.z, hdr.w);
+            float D = f16_bits_to_f32(hdr.x & 0xFFFFu);
+            if (D == 0.0f) D = 1.0f;   // every sc is 0: only the min terms count
+            const float dmin = f16_bits_to_f32(hdr.x >> 16);
+            // K-block kb = 4 sb + grp into A stage grp, free once K-block kb - 4 completed
+            if (sb > 0 && !warp_wait_fast(&kempty[grp], (uint32_t)(sb - 1) & 1u, a.status)) {
                 ok = false;
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const float D = sbring[sslot * PM + row];
-            const float2 D2 = make_float2(D, D);
-            float S[32], L[32];
-            tmem_ld16(tbase + slot * kSlotW, *reinterpret_cast<float(*)[16]>(S));
-            tmem_ld16(tbase + slot * kSlotW + 16, *reinterpret_cast<float(*)[16]>(S + 16));
-            tmem_ld16(tbase + slot * kSlotW + PN, *reinterpret_cast<float(*)[16]>(L));
-            tmem_ld16(tbase + slot * kSlotW + PN + 16, *reinterpret_cast<float(*)[16]>(L + 16));
+            const uint32_t scw = grp < 2 ? sw.sc_lo : sw.sc_hi, mnw = grp < 2 ? sw.mn_lo : sw.mn_hi;
+            const int sh = 16 * (grp & 1);
+            {
+                uint32_t v[32];
+                conv_kblock(blk, grp, (scw >> sh) & 0xFF, (scw >> (sh + 8)) & 0xFF, v);
+                tmem_st32(ta, v);
+            }
+            {
+                uint32_t v[8];
+                conv_minparts(dmin, D, (mnw >> sh) & 0xFF, (mnw >> (sh + 8)) & 0xFF, v);
+                tmem_st8(ta + kRAColX, v);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-#pragma unroll
-            for (int i = 0; i < 32; ++i) S[i] = __fadd_rn(S[i], L[i]);   // B_hi + B_lo products
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&sempty[slot]);
-                mbar_arrive(&sbempty[sslot]);
+                mbar_arrive(&afull[grp]);
+                mbar_arrive(&rempty[rs]);
+                if (warp == 2 && sb + kRawSlots < nsb) {   // refill the raw slot
+                    if (mbar_wait_bounded(&rempty[rs], (uint32_t)(sb / kRawSlots) & 1u, a.status)) {
+                        mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
+                        tma2d(rawring + rs * kRawBytes, &mW, (sb + kRawSlots) * 144, r0, &rfull[rs]);
+                    }
+                }
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = __ffma2_rn(make_float2(S[2 * i], S[2 * i + 1]), D2, acc[i]);
+            __syncwarp();
+            if (sb > 0) ok = epilogue(sb - 1, Dprev);
+            Dprev = D;
         }
+        if (ok) ok = epilogue(nsb - 1, Dprev);
         // undo 2^e_t; rows are the fast dimension of Y: lane = row gives 128-byte stores
         const int r = r0 + row;
         if (ok && r < a.rows) {
@@ -307,67 +476,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(kTmemCols)
                      : "memory");
-    }
-}
-
-// x = p0 + p1 + p2, three bf16 parts (each the round-to-nearest of what is left).
-__device__ __forceinline__ void split3_bf16(float x, __nv_bfloat16 &p0, __nv_bfloat16 &p1, __nv_bfloat16 &p2) {
-    p0 = __float2bfloat16_rn(x);
-    const float r1 = x - __bfloat162float(p0);
-    p1 = __float2bfloat16_rn(r1);
-    p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
-}
-
-// Q4_K rows -> fp16 A = sc_j * q, the min-term parts Ax and the rows' D:
-// one warp per 256-weight super-block.
-__global__ void prefill_pack_kernel(const uint8_t *__restrict__ W, int rows, int K, int rows128,
-                                    __half *__restrict__ A, __nv_bfloat16 *__restrict__ Ax,
-                                    float *__restrict__ rs) {
-    const int lane = threadIdx.x & 31;
-    const int nsr = K / 256;
-    const long long nsb = (long long)rows * nsr;
-    const long long w0 = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
-    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
-    for (long long b = w0; b < nsb; b += nw) {
-        const uint8_t *blk = W + b * 144;
-        const uint32_t s0 = *reinterpret_cast<const uint32_t *>(blk + 4);
-        const uint32_t s1 = *reinterpret_cast<const uint32_t *>(blk + 8);
-        const uint32_t s2 = *reinterpret_cast<const uint32_t *>(blk + 12);
-        const ScaleWords sw = unpack_scale_words(s0, s1, s2);
-        // lane handles quant bytes 4*lane .. 4*lane+3 of the 128: group g = lane / 8;
-        // low nibbles -> sub-block 2g, high nibbles -> sub-block 2g+1
-        const int g = lane >> 3, off = (lane & 7) * 4;
-        const uint32_t scw = g < 2 ? sw.sc_lo : sw.sc_hi;
-        const int sc_lo = (scw >> (16 * (g & 1))) & 0xFF, sc_hi = (scw >> (16 * (g & 1) + 8)) & 0xFF;
-        const uint32_t qs = *reinterpret_cast<const uint32_t *>(blk + 16 + 4 * lane);
-        __align__(8) __half lo[4], hi[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lo[i] = __int2half_rn(sc_lo * (int)((qs >> (8 * i)) & 0xF));
-            hi[i] = __int2half_rn(sc_hi * (int)((qs >> (8 * i + 4)) & 0xF));
-        }
-        __half *dst = A + b * 256;
-        *reinterpret_cast<uint2 *>(dst + (2 * g) * 32 + off) = *reinterpret_cast<const uint2 *>(lo);
-        *reinterpret_cast<uint2 *>(dst + (2 * g + 1) * 32 + off) = *reinterpret_cast<const uint2 *>(hi);
-        const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
-        float D = f16_bits_to_f32(dd & 0xFFFFu);
-        if (D == 0.0f) D = 1.0f;   // every sc is 0: only the min terms count
-        __nv_bfloat16 *ax = Ax + b * 64;
-        if (lane < 8) {            // sub-block j = lane: c = -dmin m_j / D as three bf16 parts
-            const uint32_t mnw = lane < 4 ? sw.mn_lo : sw.mn_hi;
-            const int mn = (mnw >> (8 * (lane & 3))) & 0xFF;
-            const float c = -__fdiv_rn(__fmul_rn(f16_bits_to_f32(dd >> 16), (float)mn), D);
-            __nv_bfloat16 c0, c1, c2;
-            split3_bf16(c, c0, c1, c2);
-            __nv_bfloat16 *o = ax + (lane >> 1) * 16 + (lane & 1) * 6;
-            o[0] = c0; o[1] = c0; o[2] = c1; o[3] = c0; o[4] = c1; o[5] = c2;
-        } else if (lane < 24) {    // the four zeros after each pair of sub-blocks
-            const int k = lane - 8;
-            ax[(k >> 2) * 16 + 12 + (k & 3)] = __float2bfloat16_rn(0.0f);
-        } else if (lane == 24) {
-            const long long r = b / nsr, sbi = b % nsr;
-            rs[sbi * rows128 + r] = D;
-        }
     }
 }
 
@@ -509,48 +617,23 @@ int map2d(lalb_ctx *ctx, CUtensorMap *m, const void *base, CUtensorMapDataType d
     return LALB_OK;
 }
 
-int rows_padded(int rows) { return (rows + PM - 1) / PM * PM; }
 int tokens_padded(int T) { return (T + PN - 1) / PN * PN; }
 size_t up256(size_t n) { return (n + 255) / 256 * 256; }
 
-// packed weights: A | Ax | rs
-size_t weight_a_bytes(int rows, int K) { return (size_t)rows * K * sizeof(__half); }
-size_t weight_ax_bytes(int rows, int K) { return up256((size_t)rows * (K / 4) * sizeof(__nv_bfloat16)); }
 // workspace: Bh | Bl | Bx | inv
 size_t act_b_bytes(int T, int K) { return up256((size_t)T * K * sizeof(__half)); }
 size_t act_bx_bytes(int T, int K) { return up256((size_t)T * (K / 4) * sizeof(__nv_bfloat16)); }
 
 }  // namespace
 
-size_t lalb_prefill_weight_bytes(int rows, int K) {
-    return weight_a_bytes(rows, K) + weight_ax_bytes(rows, K) +
-           (size_t)(K / 256) * rows_padded(rows) * sizeof(float);
-}
-
 size_t lalb_prefill_act_bytes(int T, int K) {
     return 2 * act_b_bytes(T, K) + act_bx_bytes(T, K) + (size_t)tokens_padded(T) * sizeof(float);
 }
 
-int lalb_prefill_pack(lalb_ctx *ctx, const void *W, int rows, int K, void *packed, cudaStream_t s) {
-    uint8_t *p = static_cast<uint8_t *>(packed);
-    __half *A = reinterpret_cast<__half *>(p);
-    __nv_bfloat16 *Ax = reinterpret_cast<__nv_bfloat16 *>(p + weight_a_bytes(rows, K));
-    float *rs = reinterpret_cast<float *>(p + weight_a_bytes(rows, K) + weight_ax_bytes(rows, K));
-    LALB_CUDA_TRY(ctx, cudaMemsetAsync(rs, 0, (size_t)(K / 256) * rows_padded(rows) * sizeof(float), s));
-    const long long nsb = (long long)rows * (K / 256);
-    const int blocks = (int)std::min<long long>((nsb * 32 + 255) / 256, (long long)ctx->sm_count * 16);
-    prefill_pack_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t *>(W), rows, K, rows_padded(rows),
-                                                A, Ax, rs);
-    LALB_LAUNCH_CHECK(ctx, "prefill_pack_kernel");
-    return LALB_OK;
-}
-
-int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, const float *X, int T,
-                        void *ws, float *Y, cudaStream_t s) {
-    const uint8_t *p = static_cast<const uint8_t *>(packed);
-    const __half *A = reinterpret_cast<const __half *>(p);
-    const __nv_bfloat16 *Ax = reinterpret_cast<const __nv_bfloat16 *>(p + weight_a_bytes(rows, K));
-    const float *rs = reinterpret_cast<const float *>(p + weight_a_bytes(rows, K) + weight_ax_bytes(rows, K));
+// W: rows x K/256 Q4_K blocks of 144 bytes, 16-byte aligned; ws: the prepared
+// tokens (lalb_prefill_act_bytes), 256-byte aligned.
+int lalb_prefill_matmul(lalb_ctx *ctx, const void *W, int rows, int K, const float *X, int T, void *ws,
+                            float *Y, cudaStream_t s) {
     uint8_t *w = static_cast<uint8_t *>(ws);
     __half *Bh = reinterpret_cast<__half *>(w);
     __half *Bl = reinterpret_cast<__half *>(w + act_b_bytes(T, K));
@@ -562,9 +645,11 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, cons
                          {&X, &T, &K, &Bh, &Bl, &Bx, &inv})))
         return st;
     LALB_LAUNCH_CHECK(ctx, "prefill_act_kernel");
-    CUtensorMap mA, mBh, mBl, mAx, mBx, mRS;
-    if ((st = map2d(ctx, &mA, A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, rows, PK, PM,
-                    CU_TENSOR_MAP_SWIZZLE_128B)))
+    CUtensorMap mW, mBh, mBl, mBx;
+    // a row's blocks as bytes: the box is one 144-byte block of 128 rows, its
+    // x coordinate sb * 144 a multiple of 16
+    if ((st = map2d(ctx, &mW, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (long long)(K / 256) * 144, rows, 144, PM,
+                    CU_TENSOR_MAP_SWIZZLE_NONE)))
         return st;
     if ((st = map2d(ctx, &mBh, Bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, T, PK, PN,
                     CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -572,16 +657,10 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, cons
     if ((st = map2d(ctx, &mBl, Bl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, T, PK, PN,
                     CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = map2d(ctx, &mAx, Ax, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K / 4, rows, 16, PM,
-                    CU_TENSOR_MAP_SWIZZLE_32B)))
-        return st;
     if ((st = map2d(ctx, &mBx, Bx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K / 4, T, 16, PN,
                     CU_TENSOR_MAP_SWIZZLE_32B)))
         return st;
-    if ((st = map2d(ctx, &mRS, rs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows_padded(rows), K / 256, PM, 1,
-                    CU_TENSOR_MAP_SWIZZLE_NONE)))
-        return st;
-    if ((st = lalb_set_smem_attr(ctx, (const void *)prefill_tc_kernel, (int)kPSmem))) return st;
+    if ((st = lalb_set_smem_attr(ctx, (const void *)prefill_q4k_kernel, (int)kRSmem))) return st;
     PfArgs a = {};
     a.rows = rows;
     a.K = K;
@@ -590,37 +669,26 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, cons
     a.Y = Y;
     a.status = &ctx->scratch->status;
     const dim3 grid(Tp / PN, (rows + PM - 1) / PM);
-    if ((st = launch_pdl(ctx, (const void *)prefill_tc_kernel, grid, dim3(kPThreads), kPSmem, s,
-                         {&mA, &mBh, &mBl, &mAx, &mBx, &mRS, &a})))
+    if ((st = launch_pdl(ctx, (const void *)prefill_q4k_kernel, grid, dim3(kRThreads), kRSmem, s,
+                         {&mW, &mBh, &mBl, &mBx, &a})))
         return st;
-    LALB_LAUNCH_CHECK(ctx, "prefill_tc_kernel");
+    LALB_LAUNCH_CHECK(ctx, "prefill_q4k_kernel");
     return LALB_OK;
 }
 
 // ---- C ABI -------------------------------------------------------------------
-extern "C" int lalb_prefill_sizes(int rows, int K, int T, size_t *weight_bytes, size_t *ws_bytes) {
-    if (rows <= 0 || K <= 0 || K % 256 || T <= 0 || !weight_bytes || !ws_bytes) return LALB_ERR_INVALID;
-    *weight_bytes = lalb_prefill_weight_bytes(rows, K);
+extern "C" int lalb_prefill_ws_bytes(int K, int T, size_t *ws_bytes) {
+    if (K <= 0 || K % 256 || T <= 0 || !ws_bytes) return LALB_ERR_INVALID;
     *ws_bytes = lalb_prefill_act_bytes(T, K);
     return LALB_OK;
 }
 
-extern "C" int lalb_q4k_prefill_pack(lalb_ctx *ctx, const void *W, int rows, int K, void *packed,
-                                     lalb_stream stream) {
+extern "C" int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *W, int rows, int K, const float *X, int T,
+                                        void *ws, float *Y, lalb_stream stream) {
     if (!ctx) return LALB_ERR_INVALID;
-    if (!W || !packed || rows <= 0 || K <= 0 || K % 256)
-        return lalb_fail(ctx, LALB_ERR_INVALID, "q4k_prefill_pack: K a multiple of 256, non-null buffers");
-    if (((uintptr_t)W & 3u) || ((uintptr_t)packed & 255u))
-        return lalb_fail(ctx, LALB_ERR_INVALID, "q4k_prefill_pack: W 4-byte, packed 256-byte aligned");
-    return lalb_prefill_pack(ctx, W, rows, K, packed, (cudaStream_t)stream);
-}
-
-extern "C" int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *packed, int rows, int K,
-                                        const float *X, int T, void *ws, float *Y, lalb_stream stream) {
-    if (!ctx) return LALB_ERR_INVALID;
-    if (!packed || !X || !ws || !Y || rows <= 0 || K <= 0 || K % 256 || T <= 0)
+    if (!W || !X || !ws || !Y || rows <= 0 || K <= 0 || K % 256 || T <= 0)
         return lalb_fail(ctx, LALB_ERR_INVALID, "matmul_q4_k_prefill: bad arguments");
-    if (((uintptr_t)packed | (uintptr_t)ws) & 255u || ((uintptr_t)X & 15u) || ((uintptr_t)Y & 3u))
+    if (((uintptr_t)W & 15u) || ((uintptr_t)ws & 255u) || ((uintptr_t)X & 15u) || ((uintptr_t)Y & 3u))
         return lalb_fail(ctx, LALB_ERR_INVALID, "matmul_q4_k_prefill: misaligned buffer");
-    return lalb_prefill_matmul(ctx, packed, rows, K, X, T, ws, Y, (cudaStream_t)stream);
+    return lalb_prefill_matmul(ctx, W, rows, K, X, T, ws, Y, (cudaStream_t)stream);
 }

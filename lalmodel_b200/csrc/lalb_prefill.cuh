@@ -6,8 +6,6 @@
 
 #include "lalb_internal.cuh"
 
-size_t lalb_prefill_weight_bytes(int rows, int K);
 size_t lalb_prefill_act_bytes(int T, int K);
-int lalb_prefill_pack(lalb_ctx *ctx, const void *W, int rows, int K, void *packed, cudaStream_t s);
-int lalb_prefill_matmul(lalb_ctx *ctx, const void *packed, int rows, int K, const float *X, int T,
-                        void *ws, float *Y, cudaStream_t s);
+int lalb_prefill_matmul(lalb_ctx *ctx, const void *W, int rows, int K, const float *X, int T, void *ws,
+                        float *Y, cudaStream_t s);

@@ -38,7 +38,7 @@ def test_binding_table_matches_header():
 
 def test_abi_version_and_status_strings():
     L = _abi.lib()
-    assert L.lalb_abi_version() == 2
+    assert L.lalb_abi_version() == 3
     for st in range(0, -8, -1):
         assert L.lalb_status_string(st)
 
@@ -67,15 +67,14 @@ def test_null_arguments_rejected_without_device():
     assert L.lalb_decoder_step(None, None, None, None, None, None) == -1
 
 
-def test_prefill_sizes_host_only():
-    wb, ws = lb.prefill_sizes(3584, 3584, 512)
-    # fp16 sc*q per weight + bf16 min-term parts (16 per 64 weights) + D per
-    # (super-block, row), rows padded to 128
-    assert wb == 3584 * 3584 * 2 + 3584 * 896 * 2 + 14 * 3584 * 4
-    # two fp16 parts per token element + bf16 min-term parts + 2^-e per token
-    assert ws == 2 * 512 * 3584 * 2 + 512 * 896 * 2 + 512 * 4
-    assert lb.prefill_sizes(1, 256, 1) == (512 + 256 + 128 * 4, 2 * 512 + 256 + 128 * 4)
+def test_prefill_ws_bytes_host_only():
+    # two fp16 parts per token element + bf16 min-term parts (16 per 64
+    # weights) + 2^-e per token, tokens padded to 128; the weights need no
+    # prepared copy: the kernel reads the Q4_K rows themselves
+    assert lb.prefill_ws_bytes(3584, 512) == 2 * 512 * 3584 * 2 + 512 * 896 * 2 + 512 * 4
+    assert lb.prefill_ws_bytes(256, 1) == 2 * 512 + 256 + 128 * 4
     L = _abi.lib()
-    a, b = ctypes.c_size_t(), ctypes.c_size_t()
-    for rows, K, T in [(0, 256, 1), (8, 100, 1), (8, 256, 0)]:
-        assert L.lalb_prefill_sizes(rows, K, T, ctypes.byref(a), ctypes.byref(b)) != 0
+    n = ctypes.c_size_t()
+    for K, T in [(256, 0), (100, 1), (0, 1)]:
+        assert L.lalb_prefill_ws_bytes(K, T, ctypes.byref(n)) != 0
+    assert L.lalb_prefill_ws_bytes(256, 1, None) != 0

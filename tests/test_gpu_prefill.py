@@ -1,13 +1,14 @@
-"""GPU parity of the prefill matmul (T tokens on the tcgen05 int8 tensor cores).
+"""GPU parity of the prefill matmul (T tokens on the tcgen05 tensor cores,
+straight from the Q4_K rows).
 
 The oracle computes the exact int32 sub-block sums isum[t][r][j] and the
-fp32 result of the exact dot.  The prefill kernel accumulates each 256-weight
-super-block, min terms included, on the tensor cores (fp16 sc * q exact,
-xq * sx in two fp16 parts, the min terms in three bf16 parts each) and scales
-it by the super-block's d in fp32.  Bar: the unpacked weight layout bit-exact; every
-output within 1e-5 of the exact value, relative to the sum of the magnitudes
-of its sub-block terms (the fp32 combine's error scale), and the normwise
-relative error below 1e-5.
+fp32 result of the exact dot.  The prefill kernel decodes each row's 4-bit
+quants on chip and accumulates each 256-weight super-block, min terms
+included, on the tensor cores (fp16 sc * q exact, xq * sx in two fp16 parts,
+the min terms in three bf16 parts each) and scales it by the super-block's d
+in fp32.  Bar: every output within 1e-5 of the exact value, relative to the
+sum of the magnitudes of its sub-block terms (the fp32 combine's error
+scale), and the normwise relative error below 1e-5.
 """
 import numpy as np
 import pytest
@@ -77,40 +78,6 @@ def check(W, X, rows, K, Y):
     assert O.normwise_rel_err(Y, yref) < TOL
 
 
-def bf16_to_f64(u16):
-    return (u16.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
-
-
-@pytest.mark.parametrize("rows,K", [(128, 256), (200, 3584), (64, 18944)])
-def test_prefill_pack_layout_bit_exact(ctx, rows, K):
-    """A = sc * q in fp16 (exact); Ax = per 64 weights, for each of their two
-    sub-blocks, the bf16 parts {c0 c0 c1 c0 c1 c2} of c = -dmin m / D, then 4
-    zeros; rs = D per (super-block, row) (D = d, or 1 where d = 0)."""
-    W, _ = make(rows, K, 1, seed=rows + K)
-    W.reshape(rows, K // 256, 144)[0, 0, 0:2] = 0          # one super-block with d = 0
-    packed = host(ctx.q4k_prefill_pack(dev(W), rows, K))
-    q, _, _ = block_fields(W, rows, K)
-    b = W.reshape(rows, K // 256, 144)
-    d = b[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
-    dmin = b[:, :, 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
-    sc, mn = scales_mins(W, rows, K)
-    na = rows * K * 2
-    A = packed[:na].view(np.float16).reshape(rows, K)
-    assert np.array_equal(A.astype(np.int32), (np.repeat(sc, 32, axis=2).reshape(rows, K) * q))
-    nx = (rows * K // 4 * 2 + 255) // 256 * 256
-    Ax = packed[na:na + rows * K // 4 * 2].view(np.uint16).reshape(rows, K // 256, 4, 16)
-    rows128 = (rows + 127) // 128 * 128
-    D = packed[na + nx:].view(np.float32).reshape(K // 256, rows128)[:, :rows].T
-    Dref = np.where(d == 0, np.float32(1), d)
-    assert np.array_equal(D.view(np.uint32), Dref.view(np.uint32))
-    c = -((dmin[..., None] * mn.astype(np.float32)).astype(np.float32) / Dref[..., None])
-    parts = bf16_to_f64(Ax[..., :12]).reshape(rows, K // 256, 8, 6)
-    assert np.all(Ax[..., 12:] == 0)
-    assert np.array_equal(parts[..., 0], parts[..., 1]) and np.array_equal(parts[..., 0], parts[..., 3])
-    assert np.array_equal(parts[..., 2], parts[..., 4])
-    assert np.array_equal(parts[..., 0] + parts[..., 2] + parts[..., 5], c.astype(np.float32).astype(np.float64))
-
-
 @pytest.mark.parametrize("rows,K,T", [
     (128, 256, 64),      # one tile
     (128, 512, 64),      # several K-blocks in one stage ring pass
@@ -118,19 +85,37 @@ def test_prefill_pack_layout_bit_exact(ctx, rows, K):
     (200, 3584, 100),    # ragged rows and tokens (partial tiles)
     (96, 1024, 1),       # a single token
     (512, 3584, 512),    # the prefill batch, q/o-shaped slice
+    (130, 512, 7),       # two row tiles, the second with 2 rows
+    (256, 768, 130),     # three super-blocks: the raw-tile ring's first refill
+    (128, 2048, 64),     # eight super-blocks: every raw slot and TMEM slot reused
 ])
 def test_prefill_matmul_matches_exact(ctx, rows, K, T):
     W, X = make(rows, K, T, seed=7 * rows + K + T)
-    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
-    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    Y = host(ctx.matmul_q4_k_prefill(dev(W), rows, K, dev(X)))
+    check(W, X, rows, K, Y)
+
+
+def test_prefill_zero_scale_super_blocks(ctx):
+    """A super-block whose d is 0 (the quantizer writes d = 0 only with every
+    sc 0): its weights are -dmin m, the min terms alone."""
+    rows, K, T = 256, 1024, 40
+    W, X = make(rows, K, T, seed=404)
+    b = W.reshape(rows, K // 256, 144)
+    for r, sb in [(0, 0), (1, 3), (129, 2), (255, 1)]:
+        b[r, sb, 0:2] = 0          # d = 0 (dmin in bytes 2:4 kept)
+        b[r, sb, 4:8] = 0          # sc 0..3, and the high bits of sc 4..7
+        b[r, sb, 12:16] &= 0xF0    # the low bits of sc 4..7 (bytes 8:12 and the high
+                                   # nibbles here are the mins, kept)
+    sc, mn = scales_mins(W, rows, K)
+    assert not sc[0, 0].any() and mn[0, 0].any()
+    Y = host(ctx.matmul_q4_k_prefill(dev(W), rows, K, dev(X)))
     check(W, X, rows, K, Y)
 
 
 def test_prefill_down_shape_long_k(ctx):
     rows, K, T = 384, 18944, 128
     W, X = make(rows, K, T, seed=31)
-    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
-    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    Y = host(ctx.matmul_q4_k_prefill(dev(W), rows, K, dev(X)))
     check(W, X, rows, K, Y)
 
 
@@ -141,8 +126,7 @@ def test_prefill_token_magnitudes(ctx):
     W, X = make(rows, K, T, seed=8)
     for t, e in enumerate([-60, -20, 0, 13, 25, 40]):
         X[t] *= np.float32(2.0 ** e)
-    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
-    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    Y = host(ctx.matmul_q4_k_prefill(dev(W), rows, K, dev(X)))
     check(W, X, rows, K, Y)
     xq, sx, sq = O.quantize_act(X)
     yref, _ = O.q4k_matmul(W, rows, K, xq, sx, sq)
@@ -157,8 +141,7 @@ def test_prefill_zero_and_spike_tokens(ctx):
     X[4, :32] = 0.0            # one zero block
     X[5, 7] = 1e4              # a spike: that block quantizes to one +-127
     X[6, 40] = -1e4
-    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
-    Y = host(ctx.matmul_q4_k_prefill(packed, rows, K, dev(X)))
+    Y = host(ctx.matmul_q4_k_prefill(dev(W), rows, K, dev(X)))
     check(W, X, rows, K, Y)
     assert np.all(Y[3] == 0.0)
 
@@ -168,7 +151,7 @@ def test_prefill_matches_per_token_gemv(ctx):
     rows, K, T = 256, 3584, 8
     W, X = make(rows, K, T, seed=77)
     Wd = dev(W)
-    Y = host(ctx.matmul_q4_k_prefill(ctx.q4k_prefill_pack(Wd, rows, K), rows, K, dev(X)))
+    Y = host(ctx.matmul_q4_k_prefill(Wd, rows, K, dev(X)))
     for t in range(T):
         y = host(ctx.matmul_q4_k(Wd, dev(X[t]), rows, K))
         assert O.normwise_rel_err(Y[t], y) < TOL
@@ -177,9 +160,14 @@ def test_prefill_matches_per_token_gemv(ctx):
 def test_prefill_rejects_bad_arguments(ctx):
     rows, K = 128, 256
     W, X = make(rows, K, 4, seed=3)
-    packed = ctx.q4k_prefill_pack(dev(W), rows, K)
+    Wd = dev(W)
     with pytest.raises(lb.LalbError):
-        ctx.matmul_q4_k_prefill(packed, rows, 200, dev(X[:, :200]))
-    ws = torch.empty(lb.prefill_sizes(rows, K, 4)[1] + 256, dtype=torch.uint8, device="cuda")
+        ctx.matmul_q4_k_prefill(Wd, rows, 200, dev(X[:, :200]))        # K not a multiple of 256
+    ws = torch.empty(lb.prefill_ws_bytes(K, 4) + 256, dtype=torch.uint8, device="cuda")
     with pytest.raises(lb.LalbError):
-        ctx.matmul_q4_k_prefill(packed, rows, K, dev(X), ws=ws[16:])
+        ctx.matmul_q4_k_prefill(Wd, rows, K, dev(X), ws=ws[16:])       # workspace not 256-aligned
+    Wo = torch.empty(W.size + 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(lb.LalbError):
+        ctx.matmul_q4_k_prefill(Wo[8:8 + W.size], rows, K, dev(X))     # rows not 16-aligned
+    torch.cuda.synchronize()
+    assert ctx.device_status() == 0
