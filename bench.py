@@ -462,6 +462,11 @@ def run_prefill_case(args, ctx=None):
     # tensor work actually issued: per 64 weights 8 fp16 MMAs (two B parts)
     # + 1 bf16 min-term MMA of the same width = 2.25 x the int8-equivalent ops
     work = 2.25 * tops
+    # the tensor pipe's own peaks, measured here: back-to-back M=128 N=256 MMAs
+    # on every SM (kind::i8 is the int8 rate the metric's ops are counted in)
+    with torch.cuda.stream(stream):
+        peak_i8 = ctx.measure_mma_peak(lb.MMA_I8)
+        peak_f16 = ctx.measure_mma_peak(lb.MMA_F16)
 
     cpu = None
     if not args.no_cpu:
@@ -507,6 +512,11 @@ def run_prefill_case(args, ctx=None):
                          "unit": "TFLOP/s", "frac": round(work / bf16, 4),
                          "note": "achieved = issued fp16/bf16 tensor work (2.25 x the int8-"
                                  "equivalent ops) over the whole step",
+                         "mma_peaks": {"i8_tops": round(peak_i8, 1), "f16_tflops": round(peak_f16, 1),
+                                       "how": "lalb_measure_mma_peak: back-to-back tcgen05.mma "
+                                              "M=128 N=256 on every SM, this run"},
+                         "frac_of_i8_mma_peak": round(tops / peak_i8, 4),
+                         "frac_of_f16_mma_peak": round(work / peak_f16, 4),
                          "gate_up_launch_us": round(gu_us, 2),
                          "gate_up_tensor_tflops": round(2.25 * 2 * T * mats[2][0] * mats[2][1]
                                                         / (gu_us * 1e-6) / 1e12, 1),

@@ -403,6 +403,14 @@ LALB_API int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *W, int rows, in
                                       const float *X, int T, void *ws, float *Y,
                                       lalb_stream stream);
 
+/* Measured tensor-core throughput: back-to-back tcgen05.mma (M = 128,
+ * N = 256) from shared memory on every SM for a few milliseconds; *tera_ops =
+ * 2 M N K per instruction over the time, in units of 10^12 (TFLOP/s for
+ * kind::f16, TOPS for kind::i8).  The dense peak at the clock the GPU holds
+ * under that load: the denominator of the prefill kernel's tensor fractions. */
+enum { LALB_MMA_F16 = 0, LALB_MMA_I8 = 1 };
+LALB_API int lalb_measure_mma_peak(lalb_ctx *ctx, int kind, double *tera_ops);
+
 /* ---- weight blobs: one file of named tensors, written and loaded here ----
  * The reference ships its 7B weights pre-converted in one file
  * (prebuilt/qwen7b_q4k_weights.bin from scripts/convert_qwen7b_q4k.py,

@@ -177,6 +177,13 @@ class Context:
                    _p(sx), _p(logits), _p(isum), _p(am), _stream())
         return logits, isum, am
 
+    def measure_mma_peak(self, kind):
+        """Back-to-back tcgen05.mma throughput on every SM (TFLOP/s for
+        MMA_F16, TOPS for MMA_I8)."""
+        v = ctypes.c_double()
+        self._call("lalb_measure_mma_peak", self.h, kind, ctypes.byref(v))
+        return v.value
+
     # ---- prefill: T tokens at once on the tensor cores ----------------------
     def matmul_q4_k_prefill(self, W, rows, K, X, ws=None, out=None):
         """Y [T][rows] = the Q4_K x Q8 matmul of each token row of X [T][K],
@@ -187,6 +194,9 @@ class Context:
         Y = out if out is not None else torch.empty((T, rows), dtype=torch.float32, device=X.device)
         self._call("lalb_matmul_q4_k_prefill", self.h, _p(W), rows, K, _p(X), T, _p(ws), _p(Y), _stream())
         return Y
+
+
+MMA_F16, MMA_I8 = 0, 1   # LALB_MMA_F16, LALB_MMA_I8
 
 
 def prefill_ws_bytes(K, T):

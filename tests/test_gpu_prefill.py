@@ -171,3 +171,15 @@ def test_prefill_rejects_bad_arguments(ctx):
         ctx.matmul_q4_k_prefill(Wo[8:8 + W.size], rows, K, dev(X))     # rows not 16-aligned
     torch.cuda.synchronize()
     assert ctx.device_status() == 0
+
+
+def test_measured_mma_peaks(ctx):
+    """Back-to-back tcgen05.mma on every SM: dense kind::f16 near its 2.25
+    PFLOP/s nominal (at the clock under that load), kind::i8 above it."""
+    f16 = ctx.measure_mma_peak(lb.MMA_F16)
+    i8 = ctx.measure_mma_peak(lb.MMA_I8)
+    assert 900.0 < f16 < 2600.0, f16
+    assert i8 > 1.2 * f16, (i8, f16)
+    with pytest.raises(lb.LalbError):
+        ctx.measure_mma_peak(7)
+    assert ctx.device_status() == 0
