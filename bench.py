@@ -352,12 +352,24 @@ def run_ste_case(args, ctx=None):
 PREFILL_T = 512
 
 
-def run_prefill_case(args, ctx=None):
+def run_prefill_case(args, ctx=None, rank=0, world=1, dist=None):
     """Qwen2.5-7B-shape prefill: T = 512 tokens through every Q4_K matrix of
     the 28 layers (qkv 4608x3584, o 3584x3584, gate/up 37888x3584, down
     3584x18944) on the tcgen05 prefill kernel.  One step = the 112 matmuls;
     the metric is int8-equivalent ops (2 T rows K) per second.  Returns its own
-    JSON line (`--case prefill`; the decode line carries it as "prefill")."""
+    JSON line (`--case prefill`; the decode line carries it as "prefill").
+
+    At N GPUs (one process each, `dist` initialised) the layer is split the
+    tensor-parallel way, so that each attention and MLP block needs one
+    exchange: qkv by rows (rows / N), o along K, gate/up by rows in pairs (the
+    gate and up rows of the rank's FFN slice, so SwiGLU stays on the rank),
+    down along K (the same FFN slice); after o and after down an NCCL
+    all-reduce sums the [T][hidden] partial outputs.  K splits follow
+    super-block boundaries (o: 14 super-blocks, down: 74, as even as they go).
+    value = the whole model's ops over the slowest rank's step time.  A check
+    on rank 0 compares its gate/up shard with those rows of the whole matrix
+    (bit-identical) and the all-reduced down output with the whole down matrix
+    on one GPU (the partial sums are added in another order: within 1e-5)."""
     import torch
 
     import lalmodel_b200 as lb
@@ -365,33 +377,72 @@ def run_prefill_case(args, ctx=None):
     c = CFG
     T = PREFILL_T
     own_ctx = ctx is None
-    ctx = ctx or lb.Context(0)
+    ctx = ctx or lb.Context(torch.cuda.current_device())
     mats = layer_mats(c)
+    hid, ffn = c["hidden"], c["ffn"]
+
+    def part(n):
+        """[lo, hi) of this rank's share of n items, as even as it goes."""
+        return n * rank // world, n * (rank + 1) // world
+
+    q0, q1 = part(mats[0][0])                    # qkv rows
+    o0, o1 = (256 * v for v in part(hid // 256))  # o: K columns
+    f0, f1 = (256 * v for v in part(ffn // 256))  # FFN slice: gate/up rows, down K columns
     big = max(r * k for r, k in mats)
     tmp = torch.empty(big, dtype=torch.float32, device="cuda")
-    wq, q4k_o = [], None
+    wq, q4k_o, w_check = [], None, {}
+
+    def shard(q, j, rows, K):
+        """This rank's part of the whole Q4_K matrix q (rows x K), as its own
+        contiguous Q4_K matrix: (bytes, rows, K)."""
+        b = q.view(rows, K // 256, 144)
+        if j == 0:
+            return b[q0:q1].reshape(-1).clone(), q1 - q0, K
+        if j == 2:
+            half = rows // 2
+            return (torch.cat((b[f0:f1], b[half + f0:half + f1])).reshape(-1).clone(),
+                    2 * (f1 - f0), K)
+        k0, k1 = (o0, o1) if j == 1 else (f0, f1)
+        return b[:, k0 // 256:k1 // 256].reshape(-1).clone(), rows, k1 - k0
+
     for l in range(c["n_layer"]):
         for j, (rows, K) in enumerate(mats):
             w = tmp[: rows * K].view(rows, K)
             ctx.fill_normal(w, seed=1234 + 16 * l + j, sigma=0.02)
-            wq.append(ctx.q4k_quantize(w))
+            q = ctx.q4k_quantize(w)   # the whole matrix, the same bytes on every rank
             if l == 0 and j == 1:
-                q4k_o = wq[-1].cpu().numpy()   # the CPU sample's matrix
+                q4k_o = q.cpu().numpy()   # the CPU sample's matrix
+            if world > 1:
+                if l == 0 and j in (2, 3) and rank == 0:
+                    w_check[j] = q        # layer 0's gate/up and down, whole, for the check
+                wq.append(shard(q, j, rows, K))
+            else:
+                wq.append((q, rows, K))
+            del q
     torch.cuda.synchronize()
     del tmp, w
     torch.cuda.empty_cache()
     X = {K: torch.empty((T, K), dtype=torch.float32, device="cuda") for K in {k for _, k in mats}}
     for i, K in enumerate(sorted(X)):
         ctx.fill_normal(X[K], seed=70 + i, sigma=1.0)
-    ws = torch.empty(max(lb.prefill_ws_bytes(k, T) for _, k in mats), dtype=torch.uint8, device="cuda")
-    Y = {r: torch.empty((T, r), dtype=torch.float32, device="cuda") for r in {r for r, _ in mats}}
-    calls = [(wq[4 * l + j], rows, K) for l in range(c["n_layer"]) for j, (rows, K) in enumerate(mats)]
-    ops = sum(2.0 * T * rows * K for _, rows, K in calls)
+    # the inputs of the K-split matrices: this rank's columns of the attention
+    # output (o) and of the SwiGLU output (down), which the rank computes itself
+    Xo = X[hid][:, o0:o1].contiguous() if world > 1 else X[hid]
+    Xd = X[ffn][:, f0:f1].contiguous() if world > 1 else X[ffn]
+    x_in = [X[hid], Xo, X[hid], Xd]
+    ws = torch.empty(max(lb.prefill_ws_bytes(k, T) for _, _, k in wq), dtype=torch.uint8, device="cuda")
+    # outputs: qkv and gate/up shards; o and down [T][hidden] partial sums, all-reduced
+    Y = [torch.empty((T, wq[j][1]), dtype=torch.float32, device="cuda") for j in range(4)]
+    calls = [(wq[4 * l + j][0], wq[4 * l + j][1], wq[4 * l + j][2], x_in[j], Y[j], world > 1 and j in (1, 3))
+             for l in range(c["n_layer"]) for j in range(4)]
+    ops = sum(2.0 * T * rows * K for _ in range(c["n_layer"]) for rows, K in mats)
     stream = torch.cuda.Stream()
 
     def step():
-        for P, rows, K in calls:
-            ctx.matmul_q4_k_prefill(P, rows, K, X[K], ws=ws, out=Y[rows])
+        for P, rows, K, x, y, reduce in calls:
+            ctx.matmul_q4_k_prefill(P, rows, K, x, ws=ws, out=y)
+            if reduce:
+                dist.all_reduce(y)
 
     with torch.cuda.stream(stream):
         step()   # first calls set kernel attributes outside the capture
@@ -406,6 +457,9 @@ def run_prefill_case(args, ctx=None):
         for _ in range(args.warmup):
             g.replay()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -414,20 +468,54 @@ def run_prefill_case(args, ctx=None):
             g.replay()
         e1.record(stream)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(torch, dist, world, e0.elapsed_time(e1) / args.steps)
     tops = ops / (ms * 1e-3) / 1e12
 
+    tp_check = None
+    if world > 1:
+        # layer 0's gate/up shard and all-reduced down against the whole matrices on rank 0
+        with torch.cuda.stream(stream):
+            for j in (2, 3):
+                P, rows, K, x, y, reduce = calls[j]
+                ctx.matmul_q4_k_prefill(P, rows, K, x, ws=ws, out=y)
+                if reduce:
+                    dist.all_reduce(y)
+        torch.cuda.synchronize()
+        bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+        if rank == 0:
+            (gr, gk), (dr, dk) = mats[2], mats[3]
+            gu = ctx.matmul_q4_k_prefill(w_check[2], gr, gk, X[hid])
+            dn = ctx.matmul_q4_k_prefill(w_check[3], dr, dk, X[ffn])
+            torch.cuda.synchronize()
+            half = gr // 2
+            gu_mine = torch.cat((gu[:, f0:f1], gu[:, half + f0:half + f1]), dim=1)
+            same = bool(torch.equal(gu_mine, Y[2]))
+            rel = float(((Y[3].double() - dn.double()).norm() / dn.double().norm()).item())
+            tp_check = {"gate_up_shard": "rank 0's %d of %d rows, T=%d" % (Y[2].shape[1], gr, T),
+                        "gate_up_bit_identical": same,
+                        "down_allreduced_normwise_rel_err": rel, "tolerance": 1e-5}
+            bad.fill_(0 if same and rel < 1e-5 else 1)
+            del gu, dn, gu_mine, w_check
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if int(bad.item()):
+            if rank == 0:
+                print(json.dumps({"case": "prefill-7b", "n_gpus": world, "tp_check": tp_check}), flush=True)
+            raise SystemExit(3)
+
     # the tensor-core kernel alone: one gate/up launch, by events around it
-    P, rows, K = calls[2]
+    P, rows, K, x, y, _ = calls[2]
     with torch.cuda.stream(stream):
-        ctx.matmul_q4_k_prefill(P, rows, K, X[K], ws=ws, out=Y[rows])   # tokens prepared
+        ctx.matmul_q4_k_prefill(P, rows, K, x, ws=ws, out=y)   # tokens prepared
         k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         n_k = 20
         gk = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gk, stream=stream):
         for _ in range(n_k):
-            ctx.matmul_q4_k_prefill(P, rows, K, X[K], ws=ws, out=Y[rows])
+            ctx.matmul_q4_k_prefill(P, rows, K, x, ws=ws, out=y)
     with torch.cuda.stream(stream):
         gk.replay()
         k0.record(stream)
@@ -439,8 +527,10 @@ def run_prefill_case(args, ctx=None):
     # end to end through the public entry point: the step's token activations
     # copied in from pinned host memory, the last output copied back
     hx = {K: v.cpu().pin_memory() for K, v in X.items()}
-    hy = torch.empty(Y[mats[-1][0]].shape, dtype=torch.float32).pin_memory()
+    hy = torch.empty(Y[3].shape, dtype=torch.float32).pin_memory()
     n_e2e = max(5, min(args.steps, 30))
+    if world > 1:
+        dist.barrier()
     with torch.cuda.stream(stream):
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
@@ -448,10 +538,11 @@ def run_prefill_case(args, ctx=None):
             for K, v in hx.items():
                 X[K].copy_(v, non_blocking=True)
             g.replay()
-            hy.copy_(Y[mats[-1][0]], non_blocking=True)
+            hy.copy_(Y[3], non_blocking=True)
         f1.record(stream)
     torch.cuda.synchronize()
-    e2e_tops = ops * n_e2e / (f0.elapsed_time(f1) * 1e-3) / 1e12
+    e2e_ms = max_over_ranks(torch, dist, world, f0.elapsed_time(f1))
+    e2e_tops = ops * n_e2e / (e2e_ms * 1e-3) / 1e12
 
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
@@ -469,7 +560,7 @@ def run_prefill_case(args, ctx=None):
         peak_f16 = ctx.measure_mma_peak(lb.MMA_F16)
 
     cpu = None
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:
         O = _cpu_lib()
         L = O.lib()
         rows, K = mats[1]
@@ -493,9 +584,9 @@ def run_prefill_case(args, ctx=None):
                          "rate %.1f s" % (n, rows, K, dt * 1e3, ops / (cpu_tops * 1e12))}
     in_bytes = sum(v.numel() * 4 for v in hx.values())
     line = {"case": "prefill-7b", "metric": "Qwen2.5-7B-shape prefill int8 TOPS (M=512)",
-            "value": round(tops, 2), "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
+            "value": round(tops, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "int8 x uint4 semantics; tensor cores: fp16 sc*q (exact) x xq*sx in two fp16 "
                      "parts, min terms in three bf16 parts, fp32 accumulate",
             "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_K on the GPU, seeded "
@@ -504,9 +595,12 @@ def run_prefill_case(args, ctx=None):
                                    "o 3584x3584, gate/up 37888x3584, down 3584x18944) Q4_K"
                                    % (T, c["n_layer"]),
                        "tokens": T, "matmuls_per_step": len(calls), "ops_per_step": ops,
+                       "parallelism": ("tp%d: qkv and gate/up by rows, o and down along K, an "
+                                       "NCCL all-reduce of [T][hidden] after o and after down"
+                                       % world) if world > 1 else "single",
                        "l2": "inputs larger than L2: %.2f GB of Q4_K weights per step, read as "
                              "they are (0.5625 B/weight)"
-                             % (sum(r * k // 256 * 144 for _, r, k in calls) / 1e9)},
+                             % (sum(r * k // 256 * 144 for _, r, k, _, _, _ in calls) / 1e9)},
             "roofline": {"kernel": "prefill_q4k_kernel", "bound": "tensor",
                          "achieved": round(work, 1), "peak": bf16, "peak_kind": kind,
                          "unit": "TFLOP/s", "frac": round(work / bf16, 4),
@@ -518,7 +612,7 @@ def run_prefill_case(args, ctx=None):
                          "frac_of_i8_mma_peak": round(tops / peak_i8, 4),
                          "frac_of_f16_mma_peak": round(work / peak_f16, 4),
                          "gate_up_launch_us": round(gu_us, 2),
-                         "gate_up_tensor_tflops": round(2.25 * 2 * T * mats[2][0] * mats[2][1]
+                         "gate_up_tensor_tflops": round(2.25 * 2 * T * calls[2][1] * calls[2][2]
                                                         / (gu_us * 1e-6) / 1e12, 1),
                          "traffic": None},
             "cpu_baseline": cpu,
@@ -526,11 +620,40 @@ def run_prefill_case(args, ctx=None):
                     "d2h_bytes_per_step": hy.numel() * 4},
             "gpu_launches": args.steps * 2 * len(calls),
             "clocks": clocks}
-    del wq, X, Y, ws
+    if tp_check is not None:
+        line["tp_check"] = tp_check
+    del g, gk
+    del wq, X, Xo, Xd, x_in, Y, ws, calls
     torch.cuda.empty_cache()
     if own_ctx:
         ctx.close()
     return line
+
+
+def run_prefill_standalone(args, rank, world, local_rank):
+    """`--case prefill`: one GPU, or N under torchrun with row-sharded weights."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=300))
+    line = run_prefill_case(args, None, rank, world, dist if world > 1 else None)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def max_over_ranks(torch, dist, world, v):
+    """The largest of every rank's v (a float), on every rank."""
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def run_gemv_case(args):
@@ -772,6 +895,15 @@ def run_gpu(args, rank, world, local_rank):
             subs[name] = {k: sub[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
                                               "dtype", "config", "roofline", "e2e",
                                               "cpu_baseline", "gpu_launches", "clocks")}
+    elif world > 1 and not args.no_sub:
+        # config 4 at N GPUs: the prefill with row-sharded weights (every rank)
+        sub_args = argparse.Namespace(**vars(args))
+        sub_args.steps, sub_args.warmup, sub_args.no_cpu = 20, 3, True
+        dist.barrier()
+        sub = run_prefill_case(sub_args, ctx, rank, world, dist)
+        subs["prefill"] = {k: sub[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
+                                               "dtype", "config", "roofline", "e2e", "gpu_launches",
+                                               "clocks", "tp_check") if k in sub}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_sample(layers, lm, c, budget_s=args.cpu_seconds)
@@ -1029,7 +1161,7 @@ def main():
     elif args.case == "trace":
         run_trace_case(args, rank, world, local_rank)
     elif args.case == "prefill":
-        print(json.dumps(run_prefill_case(args)), flush=True)
+        run_prefill_standalone(args, rank, world, local_rank)
     else:
         run_gpu(args, rank, world, local_rank)
 
