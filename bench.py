@@ -430,7 +430,7 @@ def run_prefill_case(args, ctx=None, rank=0, world=1, dist=None):
     Xo = X[hid][:, o0:o1].contiguous() if world > 1 else X[hid]
     Xd = X[ffn][:, f0:f1].contiguous() if world > 1 else X[ffn]
     x_in = [X[hid], Xo, X[hid], Xd]
-    ws = torch.empty(max(lb.prefill_ws_bytes(k, T) for _, _, k in wq), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(max(lb.prefill_ws_bytes(r, k, T) for _, r, k in wq), dtype=torch.uint8, device="cuda")
     # outputs: qkv and gate/up shards; o and down [T][hidden] partial sums, all-reduced
     Y = [torch.empty((T, wq[j][1]), dtype=torch.float32, device="cuda") for j in range(4)]
     calls = [(wq[4 * l + j][0], wq[4 * l + j][1], wq[4 * l + j][2], x_in[j], Y[j], world > 1 and j in (1, 3))

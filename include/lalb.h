@@ -396,9 +396,11 @@ LALB_API int lalb_decoder_destroy(lalb_decoder *dec);
  * two, the min terms as bf16 parts; each 256-weight super-block is scaled
  * by d in the epilogue.  Every output is within 1e-5 of the exact value
  * relative to the sum of its term magnitudes.  `ws` (ws_bytes from
- * lalb_prefill_ws_bytes, 256-byte aligned) holds the prepared tokens.
- * K % 256 == 0. */
-LALB_API int lalb_prefill_ws_bytes(int K, int T, size_t *ws_bytes);
+ * lalb_prefill_ws_bytes, 256-byte aligned) holds the prepared tokens and,
+ * for calls with fewer 128 x 128 output tiles than SMs, the partial sums of
+ * a split of K over several CTAs per tile (added in a fixed order: the
+ * result does not depend on which CTA finishes last).  K % 256 == 0. */
+LALB_API int lalb_prefill_ws_bytes(int rows, int K, int T, size_t *ws_bytes);
 LALB_API int lalb_matmul_q4_k_prefill(lalb_ctx *ctx, const void *W, int rows, int K,
                                       const float *X, int T, void *ws, float *Y,
                                       lalb_stream stream);

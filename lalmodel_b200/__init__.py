@@ -190,7 +190,7 @@ class Context:
         straight from the Q4_K rows W (as for matmul_q4_k)."""
         T = X.shape[0]
         if ws is None:
-            ws = torch.empty(prefill_ws_bytes(K, T), dtype=torch.uint8, device=X.device)
+            ws = torch.empty(prefill_ws_bytes(rows, K, T), dtype=torch.uint8, device=X.device)
         Y = out if out is not None else torch.empty((T, rows), dtype=torch.float32, device=X.device)
         self._call("lalb_matmul_q4_k_prefill", self.h, _p(W), rows, K, _p(X), T, _p(ws), _p(Y), _stream())
         return Y
@@ -199,12 +199,12 @@ class Context:
 MMA_F16, MMA_I8 = 0, 1   # LALB_MMA_F16, LALB_MMA_I8
 
 
-def prefill_ws_bytes(K, T):
-    """Workspace bytes of a prefill call of T tokens of width K (the prepared tokens)."""
+def prefill_ws_bytes(rows, K, T):
+    """Workspace bytes of a prefill call (the prepared tokens, split-K partial sums)."""
     ws = ctypes.c_size_t()
-    st = _abi.lib().lalb_prefill_ws_bytes(K, T, ctypes.byref(ws))
+    st = _abi.lib().lalb_prefill_ws_bytes(rows, K, T, ctypes.byref(ws))
     if st != 0:
-        raise LalbError("lalb_prefill_ws_bytes", st, "K=%d T=%d" % (K, T))
+        raise LalbError("lalb_prefill_ws_bytes", st, "rows=%d K=%d T=%d" % (rows, K, T))
     return ws.value
 
 

@@ -95,7 +95,7 @@ SIGNATURES = {
     "lalb_decoder_set_wait_limit": (c_int, [P, ctypes.c_double]),
     "lalb_decoder_reset": (c_int, [P, P]),
     "lalb_decoder_set_path": (c_int, [P, c_int]),
-    "lalb_prefill_ws_bytes": (c_int, [c_int, c_int, ctypes.POINTER(ctypes.c_size_t)]),
+    "lalb_prefill_ws_bytes": (c_int, [c_int, c_int, c_int, ctypes.POINTER(ctypes.c_size_t)]),
     "lalb_measure_mma_peak": (c_int, [P, c_int, ctypes.POINTER(ctypes.c_double)]),
     "lalb_matmul_q4_k_prefill": (c_int, [P, P, c_int, c_int, P, c_int, P, P, P]),
     "lalb_binlayer_create": (c_int, [P, P, P, P, c_int, c_int, c_int, ctypes.c_float, c_int,

@@ -182,8 +182,10 @@ inline int launch_pdl(lalb_ctx *ctx, const void *fn, dim3 grid, dim3 block, size
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    void *params[8];
-    int i = 0;
+    constexpr size_t kMaxParams = 16;
+    if (args.size() > kMaxParams) return lalb_fail(ctx, LALB_ERR_INVALID, "launch_pdl: more than 16 parameters");
+    void *params[kMaxParams];
+    size_t i = 0;
     for (void *p : args) params[i++] = p;
     LALB_CUDA_TRY(ctx, cudaLaunchKernelExC(&cfg, fn, params));
     return LALB_OK;

@@ -129,8 +129,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
 
 struct PfArgs {
     int rows, K, T;
+    int splits, sb_per;     // K split over gridDim.z CTAs of sb_per super-blocks each (the last fewer)
     const float *inv;       // [Tp] 2^-e_t
     float *Y;               // [T][rows]
+    float *part;            // splits > 1: [splits][T][rows] partial sums (prefill_split_sum_kernel adds them)
     unsigned int *status;
 };
 
@@ -292,8 +294,12 @@ __global__ void __launch_bounds__(kRThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = blockIdx.y * PM, t0 = blockIdx.x * PN;
-    const int nkb = a.K / PK;
-    const int nsb = a.K / 256;
+    // this CTA's super-blocks: sb0 .. sb0 + nsb - 1 of the K / 256 (every
+    // index below counts from sb0; the host makes every split non-empty)
+    const int sb0 = blockIdx.z * a.sb_per;
+    const int nsb = min(a.K / 256 - sb0, a.sb_per);
+    const int nkb = nsb * 4;
+    const int kb0 = sb0 * 4;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRBStages; ++s) {
@@ -337,7 +343,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
             // preparation): their first tiles go out before the dependency wait
             for (int sb = 0; sb < kRawSlots && sb < nsb; ++sb) {
                 mbar_arrive_expect_tx(&rfull[sb], kRawBytes);
-                tma2d(rawring + sb * kRawBytes, &mW, sb * 144, r0, &rfull[sb]);
+                tma2d(rawring + sb * kRawBytes, &mW, (sb0 + sb) * 144, r0, &rfull[sb]);
             }
             pdl_wait();
             pdl_launch_dependents();
@@ -347,9 +353,9 @@ __global__ void __launch_bounds__(kRThreads, 1)
                 if (use > 0 && !mbar_wait_fast(&kempty[s], (use - 1) & 1u, a.status)) break;
                 uint8_t *st = bring + (size_t)s * kRBStage;
                 mbar_arrive_expect_tx(&bfull[s], kRBStage);
-                tma2d(st, &mBh, kb * PK, t0, &bfull[s]);
-                tma2d(st + kPB, &mBl, kb * PK, t0, &bfull[s]);
-                tma2d(st + kRBOffBx, &mBx, kb * 16, t0, &bfull[s]);
+                tma2d(st, &mBh, (kb0 + kb) * PK, t0, &bfull[s]);
+                tma2d(st + kPB, &mBl, (kb0 + kb) * PK, t0, &bfull[s]);
+                tma2d(st + kRBOffBx, &mBx, (kb0 + kb) * 16, t0, &bfull[s]);
             }
         } else {
             pdl_wait();
@@ -448,7 +454,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
                 if (warp == 2 && sb + kRawSlots < nsb) {   // refill the raw slot
                     if (mbar_wait_bounded(&rempty[rs], (uint32_t)(sb / kRawSlots) & 1u, a.status)) {
                         mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
-                        tma2d(rawring + rs * kRawBytes, &mW, (sb + kRawSlots) * 144, r0, &rfull[rs]);
+                        tma2d(rawring + rs * kRawBytes, &mW, (sb0 + sb + kRawSlots) * 144, r0, &rfull[rs]);
                     }
                 }
             }
@@ -459,16 +465,18 @@ __global__ void __launch_bounds__(kRThreads, 1)
         if (ok) ok = epilogue(nsb - 1, Dprev);
         // undo 2^e_t; rows are the fast dimension of Y: lane = row gives 128-byte stores
         const int r = r0 + row;
+        float *out = a.splits == 1 ? a.Y : a.part + (size_t)blockIdx.z * a.T * a.rows;
         if (ok && r < a.rows) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const int t = t0 + grp * 32 + 2 * i;
-                if (t < a.T) a.Y[(size_t)t * a.rows + r] = acc[i].x * __ldg(a.inv + t);
-                if (t + 1 < a.T) a.Y[(size_t)(t + 1) * a.rows + r] = acc[i].y * __ldg(a.inv + t + 1);
+                if (t < a.T) out[(size_t)t * a.rows + r] = acc[i].x * __ldg(a.inv + t);
+                if (t + 1 < a.T) out[(size_t)(t + 1) * a.rows + r] = acc[i].y * __ldg(a.inv + t + 1);
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     }
+    __syncwarp();   // warp 0's lane 0 ran the producer loop alone: the barrier below is warp-aligned
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -582,6 +590,38 @@ __global__ void __launch_bounds__(kActThreads, 4) prefill_act_kernel(const float
     for (int g = warp + kActCache * nwarp; g < ngrp; g += nwarp) group(g, x4[g * 32 + lane]);
 }
 
+// The K splits of a call: Y = the partial sums part[z] added in split order
+// z = 0, 1, .. (the same sum on every run).  4 consecutive outputs per thread
+// when rows is a multiple of 4, else one.
+__global__ void __launch_bounds__(256) prefill_split_sum_kernel(const float *__restrict__ part, int splits,
+                                                               long long n, int vec4, float *__restrict__ Y) {
+    // the partial sums are the matmul's output: wait for it to complete
+    pdl_wait();
+    pdl_launch_dependents();
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    if (vec4) {
+        const long long n4 = n >> 2;
+        const float4 *p4 = reinterpret_cast<const float4 *>(part);
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += stride) {
+            float4 v = __ldcg(p4 + i);
+            for (int z = 1; z < splits; ++z) {
+                const float4 u = __ldcg(p4 + z * n4 + i);
+                v.x += u.x;
+                v.y += u.y;
+                v.z += u.z;
+                v.w += u.w;
+            }
+            reinterpret_cast<float4 *>(Y)[i] = v;
+        }
+    } else {
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride) {
+            float v = __ldcg(part + i);
+            for (int z = 1; z < splits; ++z) v += __ldcg(part + z * n + i);
+            Y[i] = v;
+        }
+    }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -620,25 +660,60 @@ int map2d(lalb_ctx *ctx, CUtensorMap *m, const void *base, CUtensorMapDataType d
 int tokens_padded(int T) { return (T + PN - 1) / PN * PN; }
 size_t up256(size_t n) { return (n + 255) / 256 * 256; }
 
-// workspace: Bh | Bl | Bx | inv
+// workspace: Bh | Bl | Bx | inv | part
 size_t act_b_bytes(int T, int K) { return up256((size_t)T * K * sizeof(__half)); }
 size_t act_bx_bytes(int T, int K) { return up256((size_t)T * (K / 4) * sizeof(__nv_bfloat16)); }
+size_t act_bytes(int T, int K) {
+    return 2 * act_b_bytes(T, K) + act_bx_bytes(T, K) + up256((size_t)tokens_padded(T) * sizeof(float));
+}
+int n_tiles(int rows, int T) { return ((rows + PM - 1) / PM) * (tokens_padded(T) / PN); }
+
+// The K split of a call: with fewer output tiles than the B200's 148 SMs,
+// the K super-blocks are shared out over `splits` CTAs per tile, sb_per each.
+// Cost model, in super-blocks of MMA work: waves x (sb_per + 1), the 1 being
+// a CTA's fixed cost (set-up, pipeline fill, epilogue).
+constexpr int kSplitSms = 148;
+constexpr int kMaxSplits = 16;
+void split_plan(int rows, int K, int T, int *splits, int *sb_per) {
+    const int tiles = n_tiles(rows, T), nsb = K / 256;
+    int best = 1, best_per = nsb;
+    if (tiles < kSplitSms) {
+        long long best_cost = (long long)nsb + 1;
+        for (int s = 2; s <= std::min(nsb, kMaxSplits); ++s) {
+            const int per = (nsb + s - 1) / s, se = (nsb + per - 1) / per;
+            const long long waves = ((long long)tiles * se + kSplitSms - 1) / kSplitSms;
+            const long long cost = waves * (per + 1);
+            if (cost < best_cost) best_cost = cost, best = se, best_per = per;
+        }
+    }
+    *splits = best;
+    *sb_per = best_per;
+}
+size_t part_bytes(int rows, int K, int T) {
+    int splits, per;
+    split_plan(rows, K, T, &splits, &per);
+    return splits > 1 ? up256((size_t)splits * T * rows * sizeof(float)) : 0;
+}
 
 }  // namespace
 
-size_t lalb_prefill_act_bytes(int T, int K) {
-    return 2 * act_b_bytes(T, K) + act_bx_bytes(T, K) + (size_t)tokens_padded(T) * sizeof(float);
+size_t lalb_prefill_ws_bytes(int rows, int K, int T) {
+    return act_bytes(T, K) + part_bytes(rows, K, T);
 }
 
 // W: rows x K/256 Q4_K blocks of 144 bytes, 16-byte aligned; ws: the prepared
-// tokens (lalb_prefill_act_bytes), 256-byte aligned.
+// tokens and the split-K partial sums (lalb_prefill_ws_bytes),
+// 256-byte aligned.
 int lalb_prefill_matmul(lalb_ctx *ctx, const void *W, int rows, int K, const float *X, int T, void *ws,
-                            float *Y, cudaStream_t s) {
+                        float *Y, cudaStream_t s) {
     uint8_t *w = static_cast<uint8_t *>(ws);
     __half *Bh = reinterpret_cast<__half *>(w);
     __half *Bl = reinterpret_cast<__half *>(w + act_b_bytes(T, K));
     __nv_bfloat16 *Bx = reinterpret_cast<__nv_bfloat16 *>(w + 2 * act_b_bytes(T, K));
     float *inv = reinterpret_cast<float *>(w + 2 * act_b_bytes(T, K) + act_bx_bytes(T, K));
+    float *part = reinterpret_cast<float *>(w + act_bytes(T, K));
+    int splits, sb_per;
+    split_plan(rows, K, T, &splits, &sb_per);
     const int Tp = tokens_padded(T);
     int st;
     if ((st = launch_pdl(ctx, (const void *)prefill_act_kernel, dim3(T), dim3(kActThreads), 0, s,
@@ -665,21 +740,34 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *W, int rows, int K, const flo
     a.rows = rows;
     a.K = K;
     a.T = T;
+    a.splits = splits;
+    a.sb_per = sb_per;
     a.inv = inv;
     a.Y = Y;
+    a.part = part;
     a.status = &ctx->scratch->status;
-    const dim3 grid(Tp / PN, (rows + PM - 1) / PM);
+    const dim3 grid(Tp / PN, (rows + PM - 1) / PM, splits);
     if ((st = launch_pdl(ctx, (const void *)prefill_q4k_kernel, grid, dim3(kRThreads), kRSmem, s,
                          {&mW, &mBh, &mBl, &mBx, &a})))
         return st;
     LALB_LAUNCH_CHECK(ctx, "prefill_q4k_kernel");
+    if (splits > 1) {
+        long long n = (long long)T * rows;
+        int vec4 = (rows % 4) == 0;
+        const long long work = vec4 ? n / 4 : n;
+        const int blocks = (int)std::min<long long>((work + 255) / 256, (long long)ctx->sm_count * 8);
+        if ((st = launch_pdl(ctx, (const void *)prefill_split_sum_kernel, dim3(blocks), dim3(256), 0, s,
+                             {&part, &splits, &n, &vec4, &Y})))
+            return st;
+        LALB_LAUNCH_CHECK(ctx, "prefill_split_sum_kernel");
+    }
     return LALB_OK;
 }
 
 // ---- C ABI -------------------------------------------------------------------
-extern "C" int lalb_prefill_ws_bytes(int K, int T, size_t *ws_bytes) {
-    if (K <= 0 || K % 256 || T <= 0 || !ws_bytes) return LALB_ERR_INVALID;
-    *ws_bytes = lalb_prefill_act_bytes(T, K);
+extern "C" int lalb_prefill_ws_bytes(int rows, int K, int T, size_t *ws_bytes) {
+    if (rows <= 0 || K <= 0 || K % 256 || T <= 0 || !ws_bytes) return LALB_ERR_INVALID;
+    *ws_bytes = lalb_prefill_ws_bytes(rows, K, T);
     return LALB_OK;
 }
 

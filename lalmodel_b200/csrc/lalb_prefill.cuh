@@ -6,6 +6,6 @@
 
 #include "lalb_internal.cuh"
 
-size_t lalb_prefill_act_bytes(int T, int K);
+size_t lalb_prefill_ws_bytes(int rows, int K, int T);
 int lalb_prefill_matmul(lalb_ctx *ctx, const void *W, int rows, int K, const float *X, int T, void *ws,
                         float *Y, cudaStream_t s);

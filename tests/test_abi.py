@@ -69,12 +69,17 @@ def test_null_arguments_rejected_without_device():
 
 def test_prefill_ws_bytes_host_only():
     # two fp16 parts per token element + bf16 min-term parts (16 per 64
-    # weights) + 2^-e per token, tokens padded to 128; the weights need no
+    # weights) + 2^-e per token (tokens padded to 128); the weights need no
     # prepared copy: the kernel reads the Q4_K rows themselves
-    assert lb.prefill_ws_bytes(3584, 512) == 2 * 512 * 3584 * 2 + 512 * 896 * 2 + 512 * 4
-    assert lb.prefill_ws_bytes(256, 1) == 2 * 512 + 256 + 128 * 4
+    tok = 2 * 512 * 3584 * 2 + 512 * 896 * 2 + 512 * 4
+    assert lb.prefill_ws_bytes(37888, 3584, 512) == tok                # 1184 tiles: K not split
+    # 28 x 4 tiles of a 74-super-block K: split in 5 (15 super-blocks each),
+    # 5 partial sums of [512][3584] fp32
+    tok_d = 2 * 512 * 18944 * 2 + 512 * 4736 * 2 + 512 * 4
+    assert lb.prefill_ws_bytes(3584, 18944, 512) == tok_d + 5 * 512 * 3584 * 4
+    assert lb.prefill_ws_bytes(128, 256, 1) == 2 * 512 + 256 + 128 * 4
     L = _abi.lib()
     n = ctypes.c_size_t()
-    for K, T in [(256, 0), (100, 1), (0, 1)]:
-        assert L.lalb_prefill_ws_bytes(K, T, ctypes.byref(n)) != 0
-    assert L.lalb_prefill_ws_bytes(256, 1, None) != 0
+    for rows, K, T in [(8, 256, 0), (8, 100, 1), (8, 0, 1), (0, 256, 1)]:
+        assert L.lalb_prefill_ws_bytes(rows, K, T, ctypes.byref(n)) != 0
+    assert L.lalb_prefill_ws_bytes(8, 256, 1, None) != 0

@@ -88,6 +88,8 @@ def check(W, X, rows, K, Y):
     (130, 512, 7),       # two row tiles, the second with 2 rows
     (256, 768, 130),     # three super-blocks: the raw-tile ring's first refill
     (128, 2048, 64),     # eight super-blocks: every raw slot and TMEM slot reused
+    (19200, 512, 64),    # 150 output tiles: one CTA per tile, K not split
+    (3584, 3584, 100),   # 28 tiles of 14 super-blocks: K split over 5 CTAs per tile
 ])
 def test_prefill_matmul_matches_exact(ctx, rows, K, T):
     W, X = make(rows, K, T, seed=7 * rows + K + T)
@@ -163,7 +165,7 @@ def test_prefill_rejects_bad_arguments(ctx):
     Wd = dev(W)
     with pytest.raises(lb.LalbError):
         ctx.matmul_q4_k_prefill(Wd, rows, 200, dev(X[:, :200]))        # K not a multiple of 256
-    ws = torch.empty(lb.prefill_ws_bytes(K, 4) + 256, dtype=torch.uint8, device="cuda")
+    ws = torch.empty(lb.prefill_ws_bytes(rows, K, 4) + 256, dtype=torch.uint8, device="cuda")
     with pytest.raises(lb.LalbError):
         ctx.matmul_q4_k_prefill(Wd, rows, K, dev(X), ws=ws[16:])       # workspace not 256-aligned
     Wo = torch.empty(W.size + 16, dtype=torch.uint8, device="cuda")
