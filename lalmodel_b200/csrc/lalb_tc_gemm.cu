@@ -397,6 +397,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     }
+    __syncwarp();   // lane 0 of warps 0 and 1 ran their loops alone: the barrier below is warp-aligned
     __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -408,6 +409,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
+    __syncwarp();   // .aligned: the whole warp executes the barrier together (a lane may have looped alone)
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
