@@ -402,7 +402,7 @@ __device__ __forceinline__ bool keys_arrive_wait(const PersistArgs &a, const XVi
 // no copy is ever in flight when a slot is refilled or the CTA exits.
 __device__ __forceinline__ void pwait(const PersistArgs &a, uint64_t *bar, uint32_t parity,
                                       bool &dead, unsigned long long &polls) {
-    if (dead) return;
+    if (dead || mbar_test_wait(bar, parity)) return;
     const unsigned long long limit = 4ull * a.wait_ns;
     unsigned long long t0 = 0;
     for (uint32_t i = 0; i < kWaitIterCap; ++i) {

@@ -109,11 +109,27 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t *bar,
     return ok;
 }
 
+// Non-blocking test of an mbarrier phase.  A try_wait on a phase that has
+// already completed still costs on the order of a hundred cycles; most waits
+// of a streaming pipeline find their phase complete.
+__device__ __forceinline__ uint32_t mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done;
+}
+
 // Bounded wait on an mbarrier phase.  Returns false (and raises the status
 // word) when the spin limit is reached.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar,
                                                   uint32_t parity,
                                                   unsigned int *status) {
+    if (mbar_test_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < LALB_SPIN_LIMIT; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     if (status) atomicOr(status, LALB_STATUS_WAIT_TIMEOUT);

@@ -165,23 +165,8 @@ __device__ __forceinline__ void commit_elect(uint64_t *bar) {
         : "memory");
 }
 
-// A bounded wait that first tests the phase without suspending: a try_wait on
-// a phase that has already completed still costs on the order of a hundred
-// cycles, and most waits of the MMA warp find their phase complete.
-__device__ __forceinline__ bool mbar_wait_fast(uint64_t *bar, uint32_t parity, unsigned int *status) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done || mbar_wait_bounded(bar, parity, status);
-}
-
 __device__ __forceinline__ bool warp_wait_fast(uint64_t *bar, uint32_t parity, unsigned int *status) {
-    return __all_sync(0xffffffffu, mbar_wait_fast(bar, parity, status));
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, status));
 }
 
 // 8 (32) columns of the warp's 32 TMEM lanes: register j of lane i -> (lane i, column + j)
@@ -350,7 +335,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kRBStages;
                 const uint32_t use = kb / kRBStages;
-                if (use > 0 && !mbar_wait_fast(&kempty[s], (use - 1) & 1u, a.status)) break;
+                if (use > 0 && !mbar_wait_bounded(&kempty[s], (use - 1) & 1u, a.status)) break;
                 uint8_t *st = bring + (size_t)s * kRBStage;
                 mbar_arrive_expect_tx(&bfull[s], kRBStage);
                 tma2d(st, &mBh, (kb0 + kb) * PK, t0, &bfull[s]);
