@@ -206,9 +206,10 @@ def run_ste_case(args, ctx=None):
     """The seed STE model's forward matmuls (8 layers, d=448, FFN 1792, vocab
     32768) on X 1024 x 448 fp32: per-element CORE/BINARY/PRUNE weights drawn
     10/50/40, packed as int8 codes with a per-row scale; every matmul on the
-    tcgen05 tf32-part GEMM.  Two weight sets (larger than L2 together) are
-    used on alternate steps.  Returns its own JSON line (`--case ste`; the
-    decode line carries it as "ste")."""
+    tcgen05 GEMM that decodes the codes on chip (exact fp16) against the
+    activations as two fp16 parts.  Five weight sets (larger than L2 together)
+    are used in turn.  Returns its own JSON line (`--case ste`; the decode line
+    carries it as "ste")."""
     import torch
 
     import lalmodel_b200 as lb
@@ -220,7 +221,7 @@ def run_ste_case(args, ctx=None):
     gen.manual_seed(55)
     M, d, f = c["rows"], c["d"], c["ffn"]
     shapes = [(3 * d, d), (d, d), (f, d), (d, f)] * c["n_layer"] + [(c["vocab"], d)]
-    nsets = 2
+    nsets = 5   # 34 MB of codes each: 170 MB in rotation, more than L2
     sets = []
     for ws in range(nsets):
         layers = []
@@ -240,7 +241,7 @@ def run_ste_case(args, ctx=None):
     ctx.fill_normal(X2, seed=8, sigma=1.0)
     outs = [torch.empty((M, rows), dtype=torch.float32, device="cuda") for rows, _ in shapes]
     flops = sum(2.0 * M * rows * K for rows, K in shapes)
-    weight_bytes = sum(rows * K * 4 + rows * 8 for rows, K in shapes)   # codes as fp32 + scale, bias
+    weight_bytes = sum(rows * K + rows * 8 for rows, K in shapes)   # int8 codes + scale, bias
     stream = torch.cuda.Stream()
 
     def step(layers):
@@ -299,10 +300,27 @@ def run_ste_case(args, ctx=None):
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
             bf16 = float(json.load(fh)["bf16_tflops"])
-        kind = "measured bf16 / 2 (tf32 runs at half the bf16 rate)"
+        kind = "measured bf16 burst (cuBLAS; fp16 runs at the bf16 rate)"
     except Exception:
-        bf16, kind = 1590.0, "fallback bf16 / 2"
-    tf32_peak = bf16 / 2
+        bf16, kind = 1590.0, "fallback bf16"
+    with torch.cuda.stream(stream):
+        f16_mma = ctx.measure_mma_peak(lb.MMA_F16)
+    # launches per step: per matmul the token preparation and the GEMM, plus
+    # the split-sum where K is split over CTAs (the library's cost model:
+    # fewer 128 x 128 tiles than 148 SMs, waves x (K-blocks per CTA + 6) + 10
+    # for the split-sum launch)
+    def splits(rows, K):
+        tiles, nkb = -(-rows // 128) * -(-M // 128), -(-K // 64)
+        best, cost = 1, nkb + 6
+        if tiles < 148:
+            for sp in range(2, min(nkb, 16) + 1):
+                per = -(-nkb // sp)
+                se = -(-nkb // per)
+                cc = -(-tiles * se // 148) * (per + 6) + 10
+                if cc < cost:
+                    best, cost = se, cc
+        return best
+    launches = sum(2 + (splits(rows, K) > 1) for rows, K in shapes)
     # the CPU port (the oracle's OpenMP restatement of the per-element forward)
     # on a bounded sample: the first layer's qkv over 64 rows, repeated for
     # ~cpu_seconds, scaled to the step's flops
@@ -326,20 +344,23 @@ def run_ste_case(args, ctx=None):
             "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp32 as tf32 parts (hi+lo activations x int8 codes), fp32 accumulate",
+            "dtype": "int8 codes decoded to exact fp16 x activations as fp16 hi+lo parts under a per-row "
+                     "power of two, fp32 accumulate",
             "data": "synthetic: seeded N(0,0.02) weights, per-element states 10/50/40, X N(0,1)",
             "config": {"workload": "seed STE forward: 8 x (qkv 1344x448, o 448x448, fc 1792x448, "
                                    "down 448x1792) + LM head 32768x448 on X 1024x448",
-                       "flops_per_step": flops, "gemm_launches_per_step": len(shapes),
-                       "l2": "inputs larger than L2: two weight sets of %.0f MB on alternate steps"
-                             % (weight_bytes / 1e6)},
-            "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
-                         "tensor_work": round(2 * tflops, 2), "peak": tf32_peak,
+                       "flops_per_step": flops, "gemm_calls_per_step": len(shapes),
+                       "l2": "inputs larger than L2: %d weight sets of %.0f MB used in turn"
+                             % (nsets, weight_bytes / 1e6)},
+            "roofline": {"kernel": "logic_gemm_kernel", "bound": "tensor", "achieved": round(tflops, 2),
+                         "tensor_work": round(2 * tflops, 2), "peak": bf16,
                          "peak_kind": kind, "unit": "TFLOP/s",
-                         "frac": round(2 * tflops / tf32_peak, 4),
-                         "traffic_head_launch": profile_traffic("tc_gemm_ste_head_ncu.md",
-                                                                "traffic_bytes_per_launch")},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": len(shapes) * args.steps,
+                         "frac": round(2 * tflops / bf16, 4),
+                         "f16_mma_peak": round(f16_mma, 1),
+                         "frac_of_f16_mma_peak": round(2 * tflops / f16_mma, 4),
+                         "note": "tensor_work = 2 x useful: the B_hi and B_lo products",
+                         "traffic": None},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps,
             "clocks": clocks}
     for layers in sets:
         for L in layers:

@@ -503,8 +503,12 @@ LALB_API int lalb_binlayer_destroy(lalb_binlayer *bl);
  * BINARY weights +-(row's mean |w| in the same scale), PRUNE 0. */
 LALB_API int lalb_logic_pack(lalb_ctx *ctx, const float *W, const uint8_t *state, int rows,
                              int K, int8_t *codes, float *srow, lalb_stream stream);
-/* Y [M][rows] = srow * (X . codes^T) + bias; bias nullable; the layer keeps
- * pointers to srow and bias.  X 16-byte aligned, K % 32 == 0. */
+/* Y [M][rows] = srow * (X . codes^T) + bias; bias nullable.  The layer reads
+ * codes, srow and bias in place (keep them alive while it exists): the codes
+ * stay 1 byte per weight and are decoded on chip into exact fp16 for the
+ * tcgen05 tensor cores, X goes in as two fp16 parts under a per-row power of
+ * two (22 bits); within 1e-5 of the exact products.  codes and X 16-byte
+ * aligned, K % 32 == 0, M <= max_rows. */
 typedef struct lalb_logic_layer lalb_logic_layer;
 LALB_API int lalb_logic_layer_create(lalb_ctx *ctx, const int8_t *codes, const float *srow,
                                      const float *bias, int rows, int K, int max_rows,

@@ -21,11 +21,13 @@
 // lalb_binlayer_forward splits X and computes K.
 //
 // The per-element encoding (each weight CORE, BINARY or PRUNE, packed as
-// int8 codes with a per-row scale) is the same GEMM with B = codes:
-// lalb_logic_pack / lalb_logic_layer_*.
+// int8 codes with a per-row scale: lalb_logic_pack / lalb_logic_layer_*)
+// runs on its own tensor-core GEMM straight from the int8 codes
+// (lalb_logic_gemm.cu).
 #include <algorithm>
 
 #include "lalb_internal.cuh"
+#include "lalb_logic_gemm.cuh"
 #include "lalb_tc_gemm.cuh"
 
 struct lalb_binlayer {
@@ -42,8 +44,10 @@ struct lalb_binlayer {
 struct lalb_logic_layer {
     lalb_ctx *ctx;
     int rows, K, max_rows;
-    float *b;               // codes as fp32 [rows][K] (exact in tf32)
+    const int8_t *codes;    // [rows][K], the caller's (read in place)
     const float *srow, *bias;
+    void *ws;               // token parts and split-K partial sums
+    size_t ws_bytes;
 };
 
 namespace {
@@ -159,12 +163,6 @@ __global__ void logic_pack_kernel(const float *__restrict__ W, const uint8_t *__
     if (threadIdx.x == 0) srow[j] = s;
 }
 
-__global__ void codes_to_f32_kernel(const int8_t *__restrict__ c, float *__restrict__ f, size_t n) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-         i += (size_t)gridDim.x * blockDim.x)
-        f[i] = (float)c[i];
-}
-
 void free_binlayer(lalb_binlayer *b) {
     for (float *p : {b->b0_hi, b->b0_lo, b->b1_hi, b->b1_lo, b->cs0, b->bias0, b->cs1, b->bias1,
                      b->alpha, b->knorm})
@@ -173,7 +171,7 @@ void free_binlayer(lalb_binlayer *b) {
 }
 
 void free_logic(lalb_logic_layer *L) {
-    cudaFree(L->b);
+    cudaFree(L->ws);
     delete L;
 }
 
@@ -279,6 +277,8 @@ extern "C" int lalb_logic_layer_create(lalb_ctx *ctx, const int8_t *codes, const
         return lalb_fail(ctx, LALB_ERR_INVALID, "logic_layer_create: bad arguments");
     if (K % 32)
         return lalb_fail(ctx, LALB_ERR_UNSUPPORTED, "logic_layer_create: K must be a multiple of 32");
+    if ((uintptr_t)codes & 15u)
+        return lalb_fail(ctx, LALB_ERR_INVALID, "logic_layer_create: codes must be 16-byte aligned");
     *out = nullptr;
     LALB_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     lalb_logic_layer *L = new (std::nothrow) lalb_logic_layer();
@@ -287,21 +287,15 @@ extern "C" int lalb_logic_layer_create(lalb_ctx *ctx, const int8_t *codes, const
     L->rows = rows;
     L->K = K;
     L->max_rows = max_rows;
+    L->codes = codes;
     L->srow = srow;
     L->bias = bias;
-    const size_t wn = (size_t)rows * K;
-    if (cudaMalloc(&L->b, 4 * wn) != cudaSuccess) {
+    L->ws_bytes = lalb_logic_gemm_ws_bytes(rows, K, max_rows);
+    if (cudaMalloc(&L->ws, L->ws_bytes) != cudaSuccess) {
         cudaGetLastError();
+        L->ws = nullptr;
         free_logic(L);
         return lalb_fail(ctx, LALB_ERR_NOMEM, "logic_layer_create: device buffers");
-    }
-    const int blocks = (int)std::min<size_t>((wn + 255) / 256, (size_t)ctx->sm_count * 8);
-    codes_to_f32_kernel<<<blocks, 256>>>(codes, L->b, wn);
-    cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) {
-        free_logic(L);
-        return lalb_cuda_fail(ctx, e, "codes_to_f32_kernel");
     }
     *out = L;
     return LALB_OK;
@@ -314,19 +308,8 @@ extern "C" int lalb_logic_layer_forward(lalb_logic_layer *L, const float *X, int
     if (!X || !Y || M <= 0 || M > L->max_rows)
         return lalb_fail(ctx, LALB_ERR_INVALID, "logic_layer_forward: bad arguments (M <= %d)",
                          L->max_rows);
-    cudaStream_t s = (cudaStream_t)stream;
-    TcGemmParts p = {};
-    p.M = M;
-    p.N = L->rows;
-    p.K = L->K;
-    p.a_hi = X;   // the GEMM splits X into tf32 parts in shared memory
-    p.split_a = 1;
-    p.b_hi = L->b;
-    p.b_lo = nullptr;
-    p.Y = Y;
-    p.colscale = L->srow;
-    p.bias = L->bias;
-    return lalb_tc_gemm_tf32(ctx, p, s);
+    return lalb_logic_gemm(ctx, L->codes, L->srow, L->bias, L->rows, L->K, X, M, L->ws, L->ws_bytes, Y,
+                           (cudaStream_t)stream);
 }
 
 extern "C" int lalb_logic_layer_destroy(lalb_logic_layer *L) {
