@@ -1,7 +1,9 @@
-"""The seed STE model's forward matmuls on tensor cores (tcgen05, tf32 parts)
-against the reference's goldens and the oracle.  Tolerance: 1e-5 normwise
-(max |diff| / max |ref|) for every fp32 output; PRUNE rows exactly 0; the
-per-element codes and row scales bit-exact."""
+"""The seed STE model's forward matmuls on tensor cores against the
+reference's goldens and the oracle: per-row masks (BinLayer) on the tf32-part
+GEMM, per-element int8 codes (LogicLayer) on the GEMM that decodes the codes
+into exact fp16 on chip.  Tolerance: 1e-5 normwise (max |diff| / max |ref|)
+for every fp32 output; PRUNE rows exactly 0; the per-element codes and row
+scales bit-exact."""
 import os
 
 import numpy as np
@@ -112,4 +114,62 @@ def test_logic_layer_rejects_too_many_rows(ctx):
     with pytest.raises(lb.LalbError) as e:
         L.forward(torch.zeros((9, 64), dtype=torch.float32, device="cuda"))
     assert e.value.status == -1
+    L.close()
+
+
+@pytest.mark.parametrize("rows,K,M", [(300, 96, 70), (129, 160, 129), (256, 32, 5)])
+def test_logic_layer_k_not_a_multiple_of_64(ctx, rows, K, M):
+    """K % 64 == 32: the last K-block's code and token tiles are half outside
+    the matrices and read as zeros."""
+    W = O.normal(rows * K, seed=rows + 5 * K, sigma=0.02).reshape(rows, K)
+    st = O.logic_state(rows * 13 + K, rows * K, 0.10, 0.50).reshape(rows, K)
+    codes, srow = O.logic_pack(W, st)
+    bias = O.normal(rows, seed=9, sigma=0.01)
+    X = O.normal(M * K, seed=M + 3).reshape(M, K)
+    ref = O.logic_forward(codes, srow, bias, X)
+    L = lb.LogicLayer(ctx, dev(codes), dev(srow), dev(bias), max_rows=M)
+    assert O.normwise_rel_err(host(L.forward(dev(X))), ref) < TOL
+    L.close()
+
+
+def test_logic_layer_token_magnitudes_and_zero_rows(ctx):
+    """Token rows scaled by 2^-60 .. 2^40 and all-zero rows: the per-row power
+    of two keeps the fp16 parts in range, so every row's relative error is the
+    same; a zero row gives exactly the bias."""
+    rows, K, M = 384, 448, 9
+    W = O.normal(rows * K, seed=77, sigma=0.02).reshape(rows, K)
+    st = O.logic_state(78, rows * K, 0.10, 0.50).reshape(rows, K)
+    codes, srow = O.logic_pack(W, st)
+    bias = O.normal(rows, seed=79, sigma=0.01)
+    X = O.normal(M * K, seed=80).reshape(M, K)
+    for t, e in enumerate([-60, -20, 0, 13, 25, 40, 0, 0, 0]):
+        X[t] *= np.float32(2.0 ** e)
+    X[6] = 0.0
+    X[7, :100] = 0.0
+    X[8, 5] = 1e6      # one spike in an otherwise N(0,1) row
+    ref = O.logic_forward(codes, srow, bias, X)
+    L = lb.LogicLayer(ctx, dev(codes), dev(srow), dev(bias), max_rows=M)
+    Y = host(L.forward(dev(X)))
+    for t in range(M):
+        if t == 6:
+            assert np.array_equal(Y[t], bias.astype(np.float32))
+        else:
+            assert O.normwise_rel_err(Y[t] - bias, ref[t] - bias) < TOL
+    L.close()
+
+
+def test_logic_layer_many_units_per_cta(ctx):
+    """More 128 x 128 units than SMs with a count that is not a multiple of
+    them (each CTA takes every 148th unit: some take one more), and a ragged
+    last row and token tile."""
+    rows, K, M = 19000, 256, 300
+    W = O.normal(rows * K, seed=81, sigma=0.02).reshape(rows, K)
+    st = O.logic_state(82, rows * K, 0.10, 0.50).reshape(rows, K)
+    codes, srow = O.logic_pack(W, st)
+    X = O.normal(M * K, seed=83).reshape(M, K)
+    ref = O.logic_forward(codes, srow, None, X)
+    L = lb.LogicLayer(ctx, dev(codes), dev(srow), None, max_rows=M)
+    Y = host(L.forward(dev(X)))
+    assert O.normwise_rel_err(Y, ref) < TOL
+    assert np.array_equal(Y, host(L.forward(dev(X))))
     L.close()
