@@ -171,14 +171,25 @@ __global__ void __launch_bounds__(kLThreads, 1)
     // base is column 0, and anything else raises a status bit and skips the work
     const bool tmem_ok = tmem == 0;
     if (!tmem_ok && threadIdx.x == 0) atomicOr(a.status, LALB_STATUS_WAIT_TIMEOUT);
-    // the token parts are the preceding kernel's output
-    pdl_wait();
-    pdl_launch_dependents();
-
     // K-blocks are numbered across this CTA's units (kbg): stage kbg % 4,
     // phase (kbg / 4) & 1
     if (warp == 0) {
         if (lane == 0 && tmem_ok) {
+            // The codes are never the preceding kernel's output (it prepares
+            // the tokens), so the code tiles of the first stages go out
+            // before the dependency wait; each stage's one expect_tx covers
+            // them and the token tiles that follow after it.
+            int npre = 0;
+            if (n_my > 0) {
+                const LgUnit w0 = lg_unit(a, blockIdx.x);
+                npre = min(w0.nkb, kLStages);
+                for (int kb = 0; kb < npre; ++kb) {
+                    mbar_arrive_expect_tx(&bfull[kb], kLStage);
+                    tma2d(smem + (size_t)kb * kLStage + 2 * kLB, &mC, (w0.kb0 + kb) * LK, w0.r0, &bfull[kb]);
+                }
+            }
+            pdl_wait();   // the token parts are the preceding kernel's output
+            pdl_launch_dependents();
             int kbg = 0;
             bool ok = true;
             for (int j = 0; j < n_my && ok; ++j) {
@@ -191,14 +202,21 @@ __global__ void __launch_bounds__(kLThreads, 1)
                         break;
                     }
                     uint8_t *st = smem + (size_t)s * kLStage;
-                    mbar_arrive_expect_tx(&bfull[s], kLStage);
+                    if (kbg >= npre) {
+                        mbar_arrive_expect_tx(&bfull[s], kLStage);
+                        tma2d(st + 2 * kLB, &mC, (w.kb0 + kb) * LK, w.r0, &bfull[s]);
+                    }
                     tma2d(st, &mBh, (w.kb0 + kb) * LK, w.t0, &bfull[s]);
                     tma2d(st + kLB, &mBl, (w.kb0 + kb) * LK, w.t0, &bfull[s]);
-                    tma2d(st + 2 * kLB, &mC, (w.kb0 + kb) * LK, w.r0, &bfull[s]);
                 }
             }
+        } else {
+            pdl_wait();
+            pdl_launch_dependents();
         }
     } else if (warp == 1) {
+        pdl_wait();
+        pdl_launch_dependents();
         const uint32_t stage0 = smem_u32(smem);
         bool ok = tmem_ok;
         int kbg = 0;
@@ -230,6 +248,8 @@ __global__ void __launch_bounds__(kLThreads, 1)
             if (ok) commit_elect(&sfull[slot]);
         }
     } else {
+        pdl_wait();
+        pdl_launch_dependents();
         const int q = warp & 3;             // TMEM lane quarter: rows 32 q .. 32 q + 31
         const int g = (warp - 2) >> 2;      // K-blocks with kbg % 4 == g; tokens 32 g .. of the epilogue
         const int row = q * 32 + lane;
