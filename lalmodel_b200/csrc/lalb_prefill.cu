@@ -150,7 +150,9 @@ __device__ __forceinline__ uint32_t pack_bf16(__nv_bfloat16 lo, __nv_bfloat16 hi
 
 // The 16 bf16 min-term values of one row's K-block (sub-blocks 2 kbl and
 // 2 kbl + 1) as 8 words: {c0 c0 c1 c0 c1 c2} of each sub-block's
-// c = -dmin m / D, then four zeros (the prefill_pack_kernel layout).
+// c = -dmin m / D, then four zeros; against the token side's {a0 a1 a0 a2 a1
+// a0} (prefill_act_kernel) the 16-wide bf16 MMA adds the six products
+// c_i a_j with i + j <= 2.
 __device__ __forceinline__ void conv_minparts(float dmin, float D, int m0, int m1, uint32_t (&o)[8]) {
     __nv_bfloat16 a0, a1, a2, b0, b1, b2;
     split3_bf16(-__fdiv_rn(__fmul_rn(dmin, (float)m0), D), a0, a1, a2);
