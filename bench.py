@@ -668,6 +668,50 @@ def run_prefill_standalone(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def full_token_case(ctx, lb, torch, c, layers, lm, stream, h_in, am, warmup, peak,
+                    start=512, steps=200):
+    """The whole decode token as a GPU step: the same weights with decode
+    attention over F32 KV caches (GQA, head_dim 128, 28 q heads over 4 KV
+    heads at the 7B shape), positions start .. start + steps, the earlier
+    positions' keys and values seeded at random.  A sub-measurement of the
+    decode line (its headline is the matmul set, config 3)."""
+    max_ctx = start + warmup + steps + 8
+    dec = lb.Decoder(ctx, **c, head_dim=128, max_ctx=max_ctx, rope_theta=1e6)
+    for l, m in enumerate(layers):
+        dec.set_layer_shard(0, l, *m)
+    dec.set_lm_head_shard(0, *lm)
+    kv = []
+    for l in range(c["n_layer"]):
+        k = torch.empty((max_ctx, c["kv_rows"]), dtype=torch.float32, device="cuda")
+        v = torch.empty_like(k)
+        ctx.fill_normal(k, seed=3000 + 2 * l, sigma=1.0)
+        ctx.fill_normal(v, seed=3001 + 2 * l, sigma=1.0)
+        dec.set_kv_cache(l, k, v)
+        kv.append((k, v))
+    with torch.cuda.stream(stream):
+        dec.set_position(start - warmup)
+        for _ in range(warmup):
+            dec.step(h_in, None, None, am)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            dec.step(h_in, None, None, am)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    status = ctx.device_status()
+    per_layer_b, head_b = algorithmic_bytes(c)
+    kv_b = c["n_layer"] * 2 * c["kv_rows"] * 4 * (start + steps / 2.0)   # keys and values read, mean position
+    tok_b = c["n_layer"] * sum(per_layer_b) + head_b + kv_b
+    dec.close()
+    del kv
+    return {"tok_s": round(1000.0 / ms, 2), "ms_per_step": round(ms, 5),
+            "context": "positions %d..%d (F32 KV caches, RoPE theta 1e6)" % (start, start + steps),
+            "bytes_per_token": int(tok_b), "gbs": round(tok_b / (ms * 1e-3) / 1e9, 1),
+            "frac": round(tok_b / (ms * 1e-3) / 1e9 / peak, 4), "steps": steps,
+            "status": status}
+
+
 def max_over_ranks(torch, dist, world, v):
     """The largest of every rank's v (a float), on every rank."""
     if world == 1:
@@ -905,6 +949,8 @@ def run_gpu(args, rank, world, local_rank):
     # configs 4 and 5 on one GPU, each a compact sub-line of this one
     subs = {}
     if world == 1 and not args.no_sub:
+        subs["full_token"] = full_token_case(ctx, lb, torch, c, layers, lm, stream, h_in, am,
+                                             args.warmup, peak)
         sub_args = argparse.Namespace(**vars(args))
         sub_args.steps, sub_args.warmup = 20, 3
         sub_args.cpu_seconds = min(args.cpu_seconds, 5.0)
