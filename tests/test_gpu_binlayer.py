@@ -158,6 +158,29 @@ def test_logic_layer_token_magnitudes_and_zero_rows(ctx):
     L.close()
 
 
+def test_logic_layer_long_rows(ctx):
+    """Rows many times longer than one pass of the token preparation's CTA
+    (K = 4640: 1160 float4 over 128 threads, the last pass partial), each
+    row's maximum at a different place: the last element, the middle, the
+    first pass; 37 rows."""
+    rows, K, M = 200, 4640, 37
+    W = O.normal(rows * K, seed=91, sigma=0.02).reshape(rows, K)
+    st = O.logic_state(92, rows * K, 0.10, 0.50).reshape(rows, K)
+    codes, srow = O.logic_pack(W, st)
+    bias = O.normal(rows, seed=93, sigma=0.01)
+    X = O.normal(M * K, seed=94).reshape(M, K)
+    X[0, K - 1] = 300.0
+    X[1, 2048] = -500.0
+    X[2, 10] = 1.0e3
+    X[36, 4000] = 2.0e4
+    ref = O.logic_forward(codes, srow, bias, X)
+    L = lb.LogicLayer(ctx, dev(codes), dev(srow), dev(bias), max_rows=M)
+    Y = host(L.forward(dev(X)))
+    for t in range(M):
+        assert O.normwise_rel_err(Y[t] - bias, ref[t] - bias) < TOL
+    L.close()
+
+
 def test_logic_layer_many_units_per_cta(ctx):
     """More 128 x 128 units than SMs with a count that is not a multiple of
     them (each CTA takes every 148th unit: some take one more), and a ragged

@@ -121,6 +121,20 @@ def test_prefill_down_shape_long_k(ctx):
     check(W, X, rows, K, Y)
 
 
+def test_prefill_long_k_spike_past_the_register_cache(ctx):
+    """Token preparation keeps the first 10240 weights of a token in registers
+    and reads the rest again for the conversion: spikes only there (the first
+    and the last such element, one in between) must set the token's scales."""
+    rows, K, T = 128, 18944, 5
+    W, X = make(rows, K, T, seed=37)
+    X[0, 10240] = 900.0
+    X[1, 18943] = -700.0
+    X[2, 15001] = 5.0e4
+    X[3, 10239] = 800.0   # the last element kept in registers
+    Y = host(ctx.matmul_q4_k_prefill(dev(W), rows, K, dev(X)))
+    check(W, X, rows, K, Y)
+
+
 def test_prefill_token_magnitudes(ctx):
     """Tokens scaled by 2^-60 .. 2^40: the per-token power of two keeps B in
     fp16 range, so the relative error does not depend on the magnitude."""
