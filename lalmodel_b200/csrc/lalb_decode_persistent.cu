@@ -11,9 +11,11 @@
 //     through a ring of kSlots shared-memory slots with 1-D bulk copies (TMA
 //     engine), one full/empty mbarrier pair per slot, and prefetches the
 //     chunks beyond the ring into L2.  Weights never depend on activations,
-//     so the producers run ahead across phase boundaries: while the CTA
-//     waits for the previous phase to finish everywhere, the next phase's
-//     weights are already landing;
+//     so the L2 prefetch runs ahead across phase boundaries and HBM keeps
+//     streaming while the CTA waits for the previous phase to finish
+//     everywhere; a phase's shared-memory copies start once this CTA has
+//     arrived at that wait (copies in flight would hold up its release
+//     fence), and they hit L2;
 //   * the other kNC warps are consumers.  Between phases they meet at a named
 //     barrier, one thread arrives at a global counter and waits (bounded)
 //     until every CTA has arrived, then they rebuild the phase's quantized
@@ -66,6 +68,7 @@ constexpr int kMaxTiles = 8;                 // gate/up 64-row tiles per CTA
 constexpr int kMaxNS = kPersistMaxFfn / 32;
 constexpr uint32_t kWaitIterCap = 1u << 28;   // safety net beside the time limit
 constexpr int kTraceFields = 8;
+constexpr uint32_t kGoSpinCap = 1u << 22;      // producer's pause at a phase start, bounded
 constexpr int kPrefetchChunks = LALB_PERSIST_PREFETCH;   // L2 prefetch distance beyond the ring
 constexpr int kQuads = kConsThreads / 4;     // quantizer quads per pass
 constexpr int kPrepPasses = (kPersistMaxHidden / 32 + kQuads - 1) / kQuads;
@@ -77,7 +80,7 @@ static_assert(kPersistMaxFfn >= (int)kAttnSmemBytes, "attention scratch lives in
 
 struct Layout {
     uint32_t off_bar, off_xq, off_sx, off_sq, off_red, off_bestv, off_besti, off_tile, off_tcnt,
-        off_slot, total;
+        off_go, off_slot, total;
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) {
@@ -95,7 +98,8 @@ __host__ __device__ inline Layout make_layout() {
     L.off_besti = L.off_bestv + 4 * kNC;
     L.off_tile = align_up(L.off_besti + 4 * kNC, 16);
     L.off_tcnt = L.off_tile + 4 * 64 * kMaxTiles;
-    L.off_slot = align_up(L.off_tcnt + 4 * (kMaxTiles + 1), 128);
+    L.off_go = L.off_tcnt + 4 * (kMaxTiles + 1);            // last phase arrived for
+    L.off_slot = align_up(L.off_go + 4, 128);
     L.total = L.off_slot + kSlots * kSlotBytes;
     return L;
 }
@@ -289,7 +293,10 @@ __device__ __forceinline__ void grid_arrive(const PersistArgs &a, const XView &o
     const unsigned int t_local = (seq + 1u) * nl;
     unsigned int *lbar = own.gbar + ph;
     if (nr == 0) {
-        if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(lbar) : "memory");
+        if (lane == 0) {
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+            asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(lbar) : "memory");
+        }
         return;
     }
     unsigned int last = 0;
@@ -673,6 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     float *tile_s = reinterpret_cast<float *>(smem + L.off_tile);
     int *tcnt_s = reinterpret_cast<int *>(smem + L.off_tcnt);
     uint8_t *slot_s = smem + L.off_slot;
+    volatile int *go_s = reinterpret_cast<volatile int *>(smem + L.off_go);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NP = PPL * a.n_layer + 1;
@@ -690,6 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             mbar_init(&empty[s], 1);
         }
         fence_barrier_init();
+        *go_s = 0;
     }
     __syncthreads();
 
@@ -725,6 +734,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             uint32_t g = 0;
             for (int p = 0; p < NP && !dead; ++p) {
                 const Phase d = phase_desc<PPL>(a, p, w);
+                // Phase p's copies wait until this CTA has arrived at the
+                // barrier after phase p-1.  The arrival's release fence waits
+                // for every copy the SM still has in flight (measured: 0.5 us
+                // with none, 0.7-1.7 us with the next phase's copies landing),
+                // and the last CTA's fence is on every CTA's critical path.
+                // The L2 prefetch keeps running ahead meanwhile, so HBM stays
+                // busy and the copies issued after the arrival hit L2.  The
+                // pause is bounded: it only orders work, nothing depends on it.
+                if (p > 0)
+                    for (uint32_t it = 0; it < kGoSpinCap && *go_s < p; ++it) __nanosleep(32);
                 for (int j = 0; j < d.nchunks; ++j, ++g) {
                     if (g % kNP != (uint32_t)warp) continue;
                     const int slot = g % kSlots;
@@ -793,6 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 cs.wait_ns = cs.busy_ns = cs.polls = 0;
             }
             if (ct < 32) grid_arrive<PPL>(a, own, w.rank, p - 1, seq, ct);
+            if (ct == 0) *go_s = p;   // this CTA has arrived: the producers may go on
             if (ct == 0) {
                 d = phase_desc<PPL>(a, p, w);   // while the arrivals propagate
                 // a grid barrier that gives up leaves the rest of the token
