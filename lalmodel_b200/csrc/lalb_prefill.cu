@@ -86,9 +86,10 @@ static_assert(kRBStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment
 static_assert(kRawBytes % 128 == 0, "raw slots keep 128-byte alignment");
 static_assert(kRAStages == kRBStages && kRAStages == 4, "A stage g holds K-block g of each super-block");
 constexpr int kActThreads = 128;   // token preparation: 4 warps per token, 4 tokens per SM at once
+constexpr int kActThreadsLong = 256;   // rows longer than 4 warps' caches: 8 warps, 2 tokens per SM
 constexpr int kActCache = 20;      // 128-element groups a warp keeps in registers between the passes
-                                   // (K <= 4 x 20 x 128 = 10240 reads X once, longer rows
-                                   // re-read the rest)
+                                   // (K <= 4 x 20 x 128 = 10240 reads X once with 4 warps, K <=
+                                   // 20480 with 8; longer rows re-read the rest)
 
 // kind::f16, f32 accumulator, fp16 A (TMEM) and B (shared memory), both
 // K-major, M = 128, N = 128
@@ -404,7 +405,8 @@ __global__ void __launch_bounds__(kRThreads, 1)
 // of two e (largest block amax * 2^e in [2^14, 2^15)), and
 //   Bhi + Blo = xq * sx * 2^e (fp16 parts),  Bx = the parts of sx * sumq * 2^e,
 //   inv[t] = 2^-e.
-__global__ void __launch_bounds__(kActThreads, 4) prefill_act_kernel(const float *__restrict__ X, int T, int K, __half *__restrict__ Bh,
+template <int NT>
+__global__ void __launch_bounds__(NT, 512 / NT) prefill_act_kernel(const float *__restrict__ X, int T, int K, __half *__restrict__ Bh,
                                    __half *__restrict__ Bl, __nv_bfloat16 *__restrict__ Bx,
                                    float *__restrict__ inv) {
     __shared__ float s_amax[32];
@@ -593,7 +595,13 @@ int lalb_prefill_matmul(lalb_ctx *ctx, const void *W, int rows, int K, const flo
     split_plan(rows, K, T, &splits, &sb_per);
     const int Tp = tokens_padded(T);
     int st;
-    if ((st = launch_pdl(ctx, (const void *)prefill_act_kernel, dim3(T), dim3(kActThreads), 0, s,
+    // 8 warps per token once 4 warps' register caches cannot hold the row: the
+    // 18944-long rows of the down projection are then read once (measured:
+    // 420.6-420.9 -> 424.0-425.5 TOPS per 7B prefill step)
+    const bool long_k = K / 128 > 4 * kActCache;
+    const void *act_fn = long_k ? (const void *)prefill_act_kernel<kActThreadsLong>
+                                : (const void *)prefill_act_kernel<kActThreads>;
+    if ((st = launch_pdl(ctx, act_fn, dim3(T), dim3(long_k ? kActThreadsLong : kActThreads), 0, s,
                          {&X, &T, &K, &Bh, &Bl, &Bx, &inv})))
         return st;
     LALB_LAUNCH_CHECK(ctx, "prefill_act_kernel");

@@ -121,16 +121,21 @@ def test_prefill_down_shape_long_k(ctx):
     check(W, X, rows, K, Y)
 
 
-def test_prefill_long_k_spike_past_the_register_cache(ctx):
-    """Token preparation keeps the first 10240 weights of a token in registers
-    and reads the rest again for the conversion: spikes only there (the first
-    and the last such element, one in between) must set the token's scales."""
-    rows, K, T = 128, 18944, 5
+@pytest.mark.parametrize("K", [18944, 23040])
+def test_prefill_long_k_spike_past_the_register_cache(ctx, K):
+    """Token preparation keeps a token's first 4 x 20 groups of 128 weights in
+    registers with 4 warps (K <= 10240) and 8 x 20 with 8 warps (rows longer
+    than that: K <= 20480), and reads the rest again for the conversion.
+    Spikes at the cache edges and past them (the first and the last element,
+    one in between) must set the token's scales; K = 23040 is read twice."""
+    rows, T = 128, 5
     W, X = make(rows, K, T, seed=37)
     X[0, 10240] = 900.0
-    X[1, 18943] = -700.0
+    X[1, K - 1] = -700.0
     X[2, 15001] = 5.0e4
-    X[3, 10239] = 800.0   # the last element kept in registers
+    X[3, 10239] = 800.0   # the last element 4 warps keep in registers
+    if K > 20480:
+        X[4, 20480] = -3.0e3   # the first element 8 warps read again
     Y = host(ctx.matmul_q4_k_prefill(dev(W), rows, K, dev(X)))
     check(W, X, rows, K, Y)
 
