@@ -104,7 +104,7 @@ __host__ __device__ inline Layout make_layout() {
     return L;
 }
 
-enum : int { kQkv = 0, kAttn = 1, kO = 2, kGu = 3, kDown = 4, kHead = 5 };
+enum : int { kQkv = 0, kAttn = 1, kO = 2, kGu = 3, kDown = 4, kHead = 5, kSmall = 6 };
 
 // Kind of phase p: per layer qkv, (attention,) o, gate/up, down; then the head.
 template <int PPL>
@@ -453,6 +453,8 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                                               const XView &own, const PersistRank &rk, Cons &cs) {
     const int lane = cs.lane;
     const int NS = d.K >> 5, NH = d.K >> 7;
+    // kSmall: one instantiation for qkv, o and gate/up, the kind read at run time
+    const int kind = KIND == kSmall ? d.kind : KIND;
     const int myrow = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
 
     // per-lane activation registers
@@ -523,7 +525,7 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
         float pre = 0.0f;
         if (lane < nr) {
             const int grow = d.goff + rs + lane;
-            if (KIND == kO) pre = __ldcg((d.layer == 0 ? a.h_in : own.h) + grow);
+            if (kind == kO) pre = __ldcg((d.layer == 0 ? a.h_in : own.h) + grow);
             if (KIND == kDown) pre = __ldcg(own.h + grow);
             if (KIND == kHead) pre = rk.lm_s[rs + lane];
         }
@@ -619,12 +621,12 @@ __device__ __forceinline__ void consume_phase(const PersistArgs &a, const Phase 
                     // every rank computes all of qkv and of the residual update, so
                     // they stay in its own buffer (k and v are read by the
                     // attention phase, when there is one)
-                    if (KIND == kQkv && (PPL == 5 || grow < a.q_rows)) own.q[grow] = (float)v;
-                    if (KIND == kO) own.h[grow] = __fadd_rn(prev, (float)v);
-                    if (KIND == kGu) cs.tile_s[row - d.r0] = (float)v;   // gate/up tile entry
+                    if (kind == kQkv && (PPL == 5 || grow < a.q_rows)) own.q[grow] = (float)v;
+                    if (kind == kO) own.h[grow] = __fadd_rn(prev, (float)v);
+                    if (kind == kGu) cs.tile_s[row - d.r0] = (float)v;   // gate/up tile entry
                 }
             }
-            if (KIND == kGu) {
+            if (kind == kGu) {
                 // 64-row tiles: the warp that completes one finishes it
                 const int t = (rs - d.r0) >> 6;
                 __syncwarp();
@@ -939,12 +941,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         cons_bar();
         if (ct == 0 && a.trace) a.trace[((size_t)blockIdx.x * NP + p) * kTraceFields + 2] = global_ns();
 
-        switch (d.kind) {
-            case kQkv: consume_phase<kQkv, PPL>(a, d, g_base, XL, own, rk, cs); break;
-            case kO: consume_phase<kO, PPL>(a, d, g_base, XL, own, rk, cs); break;
-            case kGu: consume_phase<kGu, PPL>(a, d, g_base, XL, own, rk, cs); break;
-            case kDown: consume_phase<kDown, PPL>(a, d, g_base, XL, own, rk, cs); break;
-            default: consume_phase<kHead, PPL>(a, d, g_base, XL, own, rk, cs); break;
+        if constexpr (PPL == 5) {
+            // With the attention phase the per-layer code no longer fits the
+            // instruction cache (ncu, 2-layer token: no_instruction stalls
+            // 2.09 per issue against 1.48 without attention), so qkv, o and
+            // gate/up share one inlined copy of the matvec loop (one call
+            // site) and the kind is read at run time.  Without attention the
+            // loops specialised per kind are faster (812 against 796 tok/s).
+            switch (d.kind) {
+                case kQkv:
+                case kO:
+                case kGu: consume_phase<kSmall, PPL>(a, d, g_base, XL, own, rk, cs); break;
+                case kDown: consume_phase<kDown, PPL>(a, d, g_base, XL, own, rk, cs); break;
+                default: consume_phase<kHead, PPL>(a, d, g_base, XL, own, rk, cs); break;
+            }
+        } else {
+            switch (d.kind) {
+                case kQkv: consume_phase<kQkv, PPL>(a, d, g_base, XL, own, rk, cs); break;
+                case kO: consume_phase<kO, PPL>(a, d, g_base, XL, own, rk, cs); break;
+                case kGu: consume_phase<kGu, PPL>(a, d, g_base, XL, own, rk, cs); break;
+                case kDown: consume_phase<kDown, PPL>(a, d, g_base, XL, own, rk, cs); break;
+                default: consume_phase<kHead, PPL>(a, d, g_base, XL, own, rk, cs); break;
+            }
         }
         g_base += d.nchunks;
     }
