@@ -776,12 +776,23 @@ def run_trace_case(args, rank, world, local_rank):
             rows[kinds[p % 4]].append(((bar_left[p] - work_end[p]) / 1e3,
                                        (pro[p + 1] - bar_left[p]) / 1e3,
                                        (work_end[p + 1] - pro[p + 1]) / 1e3))
+        # consumer warp 0 of every CTA: time spent waiting on its ring slots
+        # against time spent on the math, and the producers' last copy issued
+        # relative to the phase's prologue end (median CTA, median layer)
+        cons = {k: [] for k in kinds}
+        for p in range(n_p - 1):
+            cons[kinds[p % 4]].append((np.median(tr[:, p, 3]) / 1e3, np.median(tr[:, p, 4]) / 1e3,
+                                       np.median(tr[:, p, 5] - tr[:, p, 2]) / 1e3))
         out = {"case": "trace", "n_gpus": world,
                "token_us": round(float(tr[:, n_p - 1, 0].max() - t0) / 1e3, 1),
                "after_phase_us": {k: dict(zip(("barrier", "next_prologue", "next_work"),
                                               (round(float(v), 2)
                                                for v in np.median(np.array(rows[k]), 0))))
-                                  for k in kinds}}
+                                  for k in kinds},
+               "consumer0_us": {k: dict(zip(("ring_wait", "math", "last_copy_after_prologue"),
+                                            (round(float(v), 2)
+                                             for v in np.median(np.array(cons[k]), 0))))
+                                for k in kinds}}
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
