@@ -71,6 +71,23 @@ constexpr int kTraceFields = 8;
 constexpr uint32_t kGoSpinCap = 1u << 22;      // producer's pause at a phase start, bounded
 constexpr int kPrefetchChunks = LALB_PERSIST_PREFETCH;   // L2 prefetch distance beyond the ring
 constexpr int kQuads = kConsThreads / 4;     // quantizer quads per pass
+// Register split (setmaxnreg): the producer warps, in which one lane issues
+// the copies, give up registers to the consumer warps, whose exact Q4_K/Q8
+// arithmetic is latency-bound at two warps per SM sub-partition and
+// schedules better with more registers (measured, the matmul-only token on
+// one box: 813-815 tok/s without the split, 820-821 with 56/224, 821-825
+// with 40/232).  The block is launched with kThreads x 168 registers (ptxas
+// reports 168 for every instantiation, and the launcher checks it); each
+// split adds up to exactly that: 4 x 32 x 40 + 8 x 32 x 232 = 4 x 32 x 56 +
+// 8 x 32 x 224 = 384 x 168.  The kernel with the attention phase keeps 56
+// for its producers, whose phase descriptions need them.
+constexpr int kLaunchRegs = 168;
+constexpr int kProdRegs(int ppl) { return ppl == 4 ? 40 : 56; }
+constexpr int kConsRegs(int ppl) { return ppl == 4 ? 232 : 224; }
+static_assert(kNP * 32 * kProdRegs(4) + kNC * 32 * kConsRegs(4) <= kThreads * kLaunchRegs &&
+                  kNP * 32 * kProdRegs(5) + kNC * 32 * kConsRegs(5) <= kThreads * kLaunchRegs,
+              "the register split must fit the block's launch allocation");
+static_assert(kNP == 4 && kNC % 4 == 0, "setmaxnreg works on whole warpgroups");
 constexpr int kPrepPasses = (kPersistMaxHidden / 32 + kQuads - 1) / kQuads;
 static_assert(kNC < 24, "red_s holds kNC partial sums and the scale");
 static_assert((2 * kSlots) % kNC == 0, "slot reuse two uses back must be the same consumer");
@@ -708,6 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     // Producer warp w (lane 0) issues the chunks g with g % kNP == w, so each
     // slot (g % kSlots) is always filled by the same producer, in order.
     if (warp < kNP) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs(PPL)) : "memory");
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
             bool dead = false;
@@ -774,6 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     }
 
     // ===================== consumers ========================================
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs(PPL)) : "memory");
     const int ci = warp - kNP;        // consumer index 0..kNC-1
     const int ct = tid - 32 * kNP;    // consumer thread 0..kConsThreads-1
     uint32_t g_base = 0;
@@ -1062,6 +1081,23 @@ int lalb_launch_persist(lalb_ctx *ctx, const PersistArgs &a, cudaStream_t stream
     {
         const int st = lalb_set_smem_attr(ctx, fn, (int)L.total);
         if (st) return st;
+    }
+    {
+        // the consumers' setmaxnreg.inc waits until the producers' released
+        // registers cover it: the split is sized for exactly kLaunchRegs per
+        // thread at launch, so refuse any other count rather than launch a
+        // kernel whose consumers could wait forever
+        static int regs[2][2] = {{0, 0}, {0, 0}};
+        int &r = regs[a.ppl == 5][a.norm ? 1 : 0];
+        if (r == 0) {
+            cudaFuncAttributes fa;
+            LALB_CUDA_TRY(ctx, cudaFuncGetAttributes(&fa, fn));
+            r = fa.numRegs;
+        }
+        if (r != kLaunchRegs)
+            return lalb_fail(ctx, LALB_ERR_UNSUPPORTED,
+                             "decode_persistent_kernel: %d registers per thread, the register split "
+                             "needs %d", r, kLaunchRegs);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.cta_per_rank * a.ranks_here);
