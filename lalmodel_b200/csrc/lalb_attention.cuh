@@ -43,17 +43,21 @@ struct AttnStep {
 
 constexpr int kAttnWarps = 8;
 constexpr int kAttnMaxHd = 256;
+constexpr int kAttnMaxS = 8;    // position chunks per head at most (attn_chunks)
 
 // Shared memory of one item (bytes): rotated q and k of the head, and the
 // warps' softmax states.
 constexpr uint32_t kAttnSmemBytes = 2 * kAttnMaxHd * 4 + 2 * kAttnWarps * 8 +
                                     kAttnWarps * kAttnMaxHd * 8 + 16;
+// the last chunk's merge reuses the warps' states for the S partials
+static_assert(kAttnMaxS * (kAttnMaxHd + 2) <= 2 * kAttnWarps + kAttnWarps * kAttnMaxHd,
+              "the partials of a head fit where the warps' states were");
 
 // Chunks per head: as many as the CTAs allow (at most 8), never more than
 // the positions.
 __host__ __device__ inline int attn_chunks(int n_head, int pos, int ctas) {
     int S = ctas / n_head;
-    if (S > 8) S = 8;
+    if (S > kAttnMaxS) S = kAttnMaxS;
     if (S > pos + 1) S = pos + 1;
     return S < 1 ? 1 : S;
 }
@@ -227,16 +231,34 @@ __device__ __noinline__ void attn_item(const AttnStep &a, int h, int c, int t, u
     if (t == 0) flag_s[0] = atomicAdd(a.cnt + h, 1u) == (unsigned)(a.S - 1);
     bar();
     if (flag_s[0]) {
-        // the last chunk of head h to finish merges all S in chunk order
+        // the last chunk of head h to finish merges all S in chunk order.
+        // The S partials come into shared memory first, every load of a
+        // thread in flight at once (one memory round trip on the phase's
+        // critical path instead of one per dependent load); they take the
+        // place of the warps' states (m_s, l_s, acc_s: S (hd + 2) <= 8 x 258
+        // doubles, exactly that area), which every thread has finished
+        // reading at the barriers above.
         __threadfence();
         const double *ph = a.part + (size_t)h * a.S * (hd + 2);
+        double *ps = m_s;
+        const int np = a.S * (hd + 2);
+        constexpr int kNT = 32 * kAttnWarps;
+        for (int i0 = t; i0 < np; i0 += 4 * kNT) {
+            double v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = i0 + k * kNT < np ? __ldcg(ph + i0 + k * kNT) : 0.0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (i0 + k * kNT < np) ps[i0 + k * kNT] = v[k];
+        }
+        bar();
         double MM = -INFINITY;
-        for (int cc = 0; cc < a.S; ++cc) MM = fmax(MM, __ldcg(ph + cc * (hd + 2)));
+        for (int cc = 0; cc < a.S; ++cc) MM = fmax(MM, ps[cc * (hd + 2)]);
         double LL = 0.0, AA = 0.0;
         for (int cc = 0; cc < a.S; ++cc) {
-            const double f = exp(__ldcg(ph + cc * (hd + 2)) - MM);
-            LL += __ldcg(ph + cc * (hd + 2) + 1) * f;
-            if (t < hd) AA += __ldcg(ph + cc * (hd + 2) + 2 + t) * f;
+            const double f = exp(ps[cc * (hd + 2)] - MM);
+            LL += ps[cc * (hd + 2) + 1] * f;
+            if (t < hd) AA += ps[cc * (hd + 2) + 2 + t] * f;
         }
         if (t < hd) a.out[(size_t)h * hd + t] = (float)(AA * (1.0 / (LL + 1e-12)));
         if (t == 0) atomicExch(a.cnt + h, 0u);
