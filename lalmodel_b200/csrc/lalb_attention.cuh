@@ -123,6 +123,42 @@ __device__ __noinline__ void attn_item(const AttnStep &a, int h, int c, int t, u
     // the designated item of each KV head stores this step's cache rows
     const bool writer = (h % group == 0) && c == a.S - 1;
 
+    // ---- the warp's first batch of cached rows goes out first ----------------------
+    // (the cache rows only; their latency overlaps the RoPE section below)
+    const int w = t >> 5, lane = t & 31;
+    const int d0 = lane * DPL;
+    const float *kbase = a.k_cache + (size_t)g * hd + d0;
+    const float *vbase = a.v_cache + (size_t)g * hd + d0;
+    constexpr int U = DPL >= 8 ? 2 : 4;   // row loads in flight per lane: 2 * U * DPL / 4
+    // Batch j: positions j + u * kAttnWarps, u < U.  Rows past the chunk are
+    // zero (and masked); row pos is this token's, filled in from shared memory.
+    float kv[U][DPL], vv[U][DPL];
+    auto load_batch = [&](int j) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int jj = j + u * kAttnWarps;
+            if (jj < j1 && jj != a.pos) {
+                attn_load_row<DPL>(kbase + (size_t)jj * kvr, kv[u]);
+                attn_load_row<DPL>(vbase + (size_t)jj * kvr, vv[u]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) kv[u][i] = vv[u][i] = 0.0f;
+            }
+        }
+    };
+    auto fill_pos = [&](int j) {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (j + u * kAttnWarps == a.pos) {
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) {
+                    kv[u][i] = k_s[d0 + i];
+                    vv[u][i] = vcur[d0 + i];
+                }
+            }
+    };
+    if (j0 + w < j1) load_batch(j0 + w);
+
     // ---- rotated q of head h and k of KV head g ---------------------------------
     if (t < half) {
         float q0 = a.qkv[(size_t)h * hd + t], q1 = a.qkv[(size_t)h * hd + t + half];
@@ -143,8 +179,6 @@ __device__ __noinline__ void attn_item(const AttnStep &a, int h, int c, int t, u
     bar();
 
     // ---- per warp: online softmax over positions j0 + w + 8i ----------------------
-    const int w = t >> 5, lane = t & 31;
-    const int d0 = lane * DPL;
     double qd[DPL], acc[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; ++i) {
@@ -153,25 +187,9 @@ __device__ __noinline__ void attn_item(const AttnStep &a, int h, int c, int t, u
     }
     const double scale = 1.0 / sqrt((double)hd);
     double m = -INFINITY, l = 0.0;
-    const float *kbase = a.k_cache + (size_t)g * hd + d0;
-    const float *vbase = a.v_cache + (size_t)g * hd + d0;
-    constexpr int U = DPL >= 8 ? 2 : 4;   // row loads in flight per lane: 2 * U * DPL / 4
     for (int j = j0 + w; j < j1; j += U * kAttnWarps) {
-        float kv[U][DPL], vv[U][DPL];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int jj = j + u * kAttnWarps;
-            if (jj < j1 && jj != a.pos) {
-                attn_load_row<DPL>(kbase + (size_t)jj * kvr, kv[u]);
-                attn_load_row<DPL>(vbase + (size_t)jj * kvr, vv[u]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) {
-                    kv[u][i] = jj == a.pos ? k_s[d0 + i] : 0.0f;
-                    vv[u][i] = jj == a.pos ? vcur[d0 + i] : 0.0f;
-                }
-            }
-        }
+        if (j != j0 + w) load_batch(j);
+        fill_pos(j);
         double s[U];
         double mx = m;
 #pragma unroll
