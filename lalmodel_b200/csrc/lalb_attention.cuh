@@ -62,10 +62,33 @@ __host__ __device__ inline int attn_chunks(int n_head, int pos, int ctas) {
     return S < 1 ? 1 : S;
 }
 
-__device__ __forceinline__ double attn_warp_sum(double v) {
+// Sums U per-lane values (U = 2 or 4) over the warp at once and returns every
+// total on every lane: the first exchange levels halve the values a lane
+// carries (lane L ends with total ((L >> 4) & 1) * 2 + ((L >> 3) & 1) for
+// U = 4, (L >> 4) & 1 for U = 2), the last ones add plainly, then each total
+// is read from a lane that holds it.  10 double shuffles for U = 4 instead of
+// 20 for four separate reductions.
+template <int U>
+__device__ __forceinline__ void attn_warp_sums(double (&v)[U], int lane) {
+    static_assert(U == 2 || U == 4, "two or four values");
+    const bool b4 = lane & 16;
+    double x;
+    if constexpr (U == 4) {
+        const double w0 = (b4 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[2], 16);
+        const double w1 = (b4 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, b4 ? v[1] : v[3], 16);
+        const bool b3 = lane & 8;
+        x = (b3 ? w1 : w0) + __shfl_xor_sync(0xffffffffu, b3 ? w0 : w1, 8);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
+        for (int o = 4; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = __shfl_sync(0xffffffffu, x, (u >> 1) * 16 + (u & 1) * 8);
+    } else {
+        x = (b4 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[1], 16);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) v[u] = __shfl_sync(0xffffffffu, x, u * 16);
+    }
 }
 
 // Rotates the pair (x0, x1) of dimension d of a head by the angle at pos.
@@ -197,8 +220,12 @@ __device__ __noinline__ void attn_item(const AttnStep &a, int h, int c, int t, u
             double dot = 0.0;
 #pragma unroll
             for (int i = 0; i < DPL; ++i) dot = fma(qd[i], (double)kv[u][i], dot);
-            dot = attn_warp_sum(dot);
-            s[u] = (j + u * kAttnWarps < j1) ? dot * scale : -INFINITY;
+            s[u] = dot;
+        }
+        attn_warp_sums<U>(s, lane);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            s[u] = (j + u * kAttnWarps < j1) ? s[u] * scale : -INFINITY;
             mx = fmax(mx, s[u]);
         }
         const double corr = exp(m - mx);   // m = -inf on the first batch: 0
