@@ -112,10 +112,13 @@ def run_decoder_tokens(ctx, cfg, path, start, n_tok, seed, n_rank=1):
 
 @pytest.mark.parametrize("path", [lb.Decoder.KERNELS, lb.Decoder.PERSISTENT],
                          ids=["kernels", "persistent"])
-@pytest.mark.parametrize("ci,start,n_tok", [(0, 0, 4), (1, 300, 2)], ids=["small", "qwen"])
+@pytest.mark.parametrize("ci,start,n_tok", [(0, 0, 4), (0, 30, 2), (1, 300, 2)],
+                         ids=["small", "small-8-chunks", "qwen"])
 def test_decoder_with_attention_matches_oracle(ctx, path, ci, start, n_tok):
     """Tokens at consecutive positions: the attention output feeds o, the
-    caches grow by one row per token; both decode paths match the oracle."""
+    caches grow by one row per token; both decode paths match the oracle.
+    From position 30 the persistent kernel splits each of the 8 heads over
+    8 position chunks (the most it uses), whose partials one chunk merges."""
     res, caches, kv = run_decoder_tokens(ctx, ATT_CFGS[ci], path, start, n_tok, seed=3300 + ci)
     for h, logits, am, (ref_h, ref_logits, ref_am) in res:
         assert_fp32_parity(h, ref_h, exact_frac=0.99)
