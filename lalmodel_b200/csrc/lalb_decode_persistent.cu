@@ -32,6 +32,7 @@
 // Every wait is bounded; an expired wait raises the status word and lets the
 // kernel run to completion with whatever data it has.
 #include <algorithm>
+#include <atomic>
 
 #include "lalb_internal.cuh"
 #include "lalb_kernels.cuh"
@@ -1087,12 +1088,14 @@ int lalb_launch_persist(lalb_ctx *ctx, const PersistArgs &a, cudaStream_t stream
         // registers cover it: the split is sized for exactly kLaunchRegs per
         // thread at launch, so refuse any other count rather than launch a
         // kernel whose consumers could wait forever
-        static int regs[2][2] = {{0, 0}, {0, 0}};
-        int &r = regs[a.ppl == 5][a.norm ? 1 : 0];
+        static std::atomic<int> regs[2][2];   // per instantiation, 0 until read
+        std::atomic<int> &slot = regs[a.ppl == 5][a.norm ? 1 : 0];
+        int r = slot.load(std::memory_order_relaxed);
         if (r == 0) {
             cudaFuncAttributes fa;
             LALB_CUDA_TRY(ctx, cudaFuncGetAttributes(&fa, fn));
             r = fa.numRegs;
+            slot.store(r, std::memory_order_relaxed);
         }
         if (r != kLaunchRegs)
             return lalb_fail(ctx, LALB_ERR_UNSUPPORTED,
