@@ -61,6 +61,19 @@ def algorithmic_bytes(c):
     return per_layer, head
 
 
+def decode_config(c, world, persistent=True):
+    """The decode line's `config`, shared by both arms so that they describe
+    the same workload at the same N."""
+    per_layer_b, head_b = algorithmic_bytes(c)
+    tok_bytes = c["n_layer"] * sum(per_layer_b) + head_b
+    return {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": 1, "seq_len": 1,
+            "parallelism": "tp%d (row shards, in-kernel NVLink exchange)" % world
+                           if world > 1 else "single",
+            "path": "persistent" if persistent else "kernels",
+            "l2": "inputs larger than L2: %.2f GB of weights streamed per step" % (tok_bytes / 1e9),
+            "bytes_per_step": tok_bytes}
+
+
 def measured_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -994,14 +1007,7 @@ def run_gpu(args, rank, world, local_rank):
             "dtype": "int8 (q4 x i8 dp4a -> int32 per 32-block, fp32 terms, f64 row sum)",
             "data": "synthetic: seeded N(0,0.02) weights quantized on the GPU (Q4_K min-max, "
                     "int8 per-row LM head); seeded N(0,1) hidden state",
-            "config": {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": 1,
-                       "seq_len": 1,
-                       "parallelism": "tp%d (row shards, in-kernel NVLink exchange)" % world
-                                      if tp else "single",
-                       "path": "persistent" if persistent else "kernels",
-                       "l2": "inputs larger than L2: %.2f GB of weights streamed per step"
-                             % (tok_bytes / 1e9),
-                       "bytes_per_step": tok_bytes},
+            "config": decode_config(c, world, persistent),
             "roofline": roofline,
             "phase_chain": chain,
             "gemv": gemv and {**gemv, "frac": round(gemv["gbs"] / peak, 4)},
@@ -1189,11 +1195,11 @@ def run_reference(args, rank, world):
                                         args.cpu_seconds * 4)
     line = {"impl": "reference", "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s",
             "n_gpus": world, "steps": n, "warmup": args.warmup,
-            "ms_per_step": round(1e3 / tok_s, 3), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(1e3 / tok_s, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8 (AVX2 maddubs -> int32, fp32 combine)",
             "data": "synthetic: seeded N(0,0.02) weights quantized on the CPU, N(0,1) hidden state",
-            "config": {"workload": WORKLOAD, "n_layer": c["n_layer"], "global_batch": 1,
-                       "seq_len": 1, "parallelism": "host cores (OpenMP)"},
+            "config": decode_config(c, world),
+            "host": "the whole token on rank 0's host cores (OpenMP, %d threads)" % cores,
             "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": cores,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
