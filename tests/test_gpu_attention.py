@@ -62,6 +62,10 @@ ATT_CFGS = [
          max_ctx=40),
     dict(n_layer=1, hidden=3584, q_rows=3584, kv_rows=512, ffn=18944, vocab=20000, head_dim=128,
          max_ctx=400, rope_theta=1e6),
+    # the largest head: 4 heads of 256 over one KV head; from position 7 the
+    # persistent kernel's 8 chunks' partials fill the merge area exactly
+    dict(n_layer=1, hidden=1024, q_rows=1024, kv_rows=256, ffn=2048, vocab=3000, head_dim=256,
+         max_ctx=40),
 ]
 
 
@@ -112,8 +116,8 @@ def run_decoder_tokens(ctx, cfg, path, start, n_tok, seed, n_rank=1):
 
 @pytest.mark.parametrize("path", [lb.Decoder.KERNELS, lb.Decoder.PERSISTENT],
                          ids=["kernels", "persistent"])
-@pytest.mark.parametrize("ci,start,n_tok", [(0, 0, 4), (0, 30, 2), (1, 300, 2)],
-                         ids=["small", "small-8-chunks", "qwen"])
+@pytest.mark.parametrize("ci,start,n_tok", [(0, 0, 4), (0, 30, 2), (1, 300, 2), (2, 30, 2)],
+                         ids=["small", "small-8-chunks", "qwen", "hd256-8-chunks"])
 def test_decoder_with_attention_matches_oracle(ctx, path, ci, start, n_tok):
     """Tokens at consecutive positions: the attention output feeds o, the
     caches grow by one row per token; both decode paths match the oracle.
